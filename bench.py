@@ -1,0 +1,366 @@
+#!/usr/bin/env python
+"""Benchmark of the Mosaic block-sparse attention forward on B200.
+
+Workload ("S1"): one mosaic_attn_func forward at Nside 64 —
+B=1 per GPU, N=49152 tokens, 12 query / 3 kv heads, head_dim 64, sparse block 64,
+top-k 24, local window 1024, bf16, synthetic q/k/v ~ N(0,1) and gates
+sigmoid(N(0,1)). A step = the four kernels of the op on one member's inputs:
+(a) block pool, coarse attention, (b) scores + top-k, (c) fused local + selected
+attention with the gated combine. Ensemble members are independent, so with
+--gpus N every rank runs its own member (weak scaling, no collective in the step).
+
+Timing: W untimed warm-up steps, then K steps between barrier + synchronize,
+CUDA events on the launching stream, max over ranks. Three input sets
+(3 x 117 MB > 126 MB L2) rotate so no step reads inputs left in L2 by the
+previous one. Per-kernel durations come from events recorded between the
+stages of every timed step; `roofline` uses the fused kernel (c).
+
+`--impl reference` times the reference algorithm on the host cores instead: the
+reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
+the oracle port (oracle/bsa_oracle.py), run on a bounded sample of the same
+workload (all of the global compression/top-k, local + selected branches for 4
+of the 48 windows per step).
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "BSA fwd tokens/s/GPU @Nside64 (N=49152,12h,d64,k24); 24-member step/s @1-8 GPU"
+UNIT = "tokens/s"
+S1 = dict(B=1, N=49152, Hq=12, Hk=3, D=64, bs=64, K=24, bas=1024)
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+MEMBERS = 24
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return PEAKS_FALLBACK["hbm_gbs"], PEAKS_FALLBACK["bf16_tflops"], "fallback"
+
+
+def flops_attend(c):
+    """FLOP of kernel (c): QK^T and PV over K*bs selected + bas local keys, 2 FLOP/MAC."""
+    return 4 * c["B"] * c["N"] * c["Hq"] * c["D"] * (c["K"] * c["bs"] + c["bas"])
+
+
+def bytes_pool(c):
+    """Algorithmic HBM bytes of the pool kernel: read q, k, v once, write the pooled rows."""
+    heads = c["Hq"] + 2 * c["Hk"]
+    return c["B"] * c["N"] * heads * c["D"] * 2 + c["B"] * (c["N"] // c["bs"]) * heads * c["D"] * 2
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls SM clock and throttle reasons through NVML (read-only) while running."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                    self.h = h
+            self.nvml = pynvml
+            if self.h is not None:
+                self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.h = None
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.h is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.h is not None:
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_sample(c, windows, reps, warm=1):
+    """Times oracle.mosaic_attn_func_sample on the host cores; returns (tokens/s, cores, seconds)."""
+    from oracle import bsa_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x = O.make_inputs(c["B"], c["N"], c["Hq"], c["Hk"], seed=0, rope=False)
+    args = (x["q"], x["k"], x["v"], x["w"], c["bas"], c["bs"], c["K"])
+    for _ in range(warm):
+        O.mosaic_attn_func_sample(*args, windows=windows)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.mosaic_attn_func_sample(*args, windows=windows)
+        times.append(time.perf_counter() - t0)
+    tok = c["B"] * len(windows) * c["bas"]
+    return tok * reps / sum(times), torch.get_num_threads(), sum(times)
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    c = S1
+    windows = [0, 17, 30, 47]
+    value, cores, secs = cpu_sample(c, windows, reps=args.steps, warm=args.warmup)
+    sample = (f"per step: oracle port (fp32 torch) of mosaic_attn_func on S1 inputs, global pooling/coarse "
+              f"attention/top-k over all 49152 tokens, local + selected branches for 4 of 48 windows "
+              f"({len(windows) * c['bas']} query tokens); {args.steps} steps after {args.warmup} warm-up")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "S1 mosaic_attn_func forward, Nside 64 (N=49152, 12/3 heads, d64, bs64, k24, "
+                               "window 1024), CPU sample", "B": c["B"], "N": c["N"]},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- B200 arm
+class Stages:
+    """The four kernels of mosaic_bsa_fwd, called one by one through the C ABI so
+    that CUDA events can bracket each of them."""
+
+    def __init__(self, lib, c, dev):
+        from mosaic_b200.ops import _ptr
+        self.lib, self.c, self._ptr = lib, c, _ptr
+        B, N, Hq, Hk, D, bs, K = c["B"], c["N"], c["Hq"], c["Hk"], c["D"], c["bs"], c["K"]
+        nb = N // bs
+        e = lambda *s, dt=torch.bfloat16: torch.empty(*s, dtype=dt, device=dev)
+        self.q_cmp, self.k_cmp, self.v_cmp = e(B, nb, Hq, D), e(B, nb, Hk, D), e(B, nb, Hk, D)
+        self.o_cmp = e(B, nb, Hq, D)
+        self.idx = e(B, nb, Hk, K, dt=torch.int64)
+        self.out = e(B, N, Hq, D)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def run(self, x, stream, events=None):
+        p, c, L = self._ptr, self.c, self.lib
+        B, N, Hq, Hk, D, bs, K, bas = (c[k] for k in ("B", "N", "Hq", "Hk", "D", "bs", "K", "bas"))
+        nb = N // bs
+        s = ctypes.c_void_p(stream.cuda_stream)
+        null = ctypes.c_void_p(0)
+        rec = (lambda i: events[i].record(stream)) if events else (lambda i: None)
+        rec(0)
+        rc = L.mosaic_block_pool(p(x["q"]), p(x["k"]), p(x["v"]), null, null, null, null, p(self.q_cmp),
+                                 p(self.k_cmp), p(self.v_cmp), B, N, Hq, Hk, D, bs, s)
+        rec(1)
+        rc |= L.mosaic_cmp_attn_fwd(p(self.q_cmp), p(self.k_cmp), p(self.v_cmp), p(self.o_cmp), p(self.status),
+                                    B, nb, Hq, Hk, D, 0.125, s)
+        rec(2)
+        rc |= L.mosaic_attn_topk(p(self.q_cmp), p(self.k_cmp), p(self.idx), B, nb, Hq, Hk, D, K, s)
+        rec(3)
+        rc |= L.mosaic_bsa_attend_fwd(p(x["q"]), p(x["k"]), p(x["v"]), p(self.idx), p(x["w"]), p(self.o_cmp),
+                                      p(self.out), p(self.status), B, N, Hq, Hk, D, bas, bs, K, 0, 0.125, s)
+        rec(4)
+        if rc:
+            raise RuntimeError(f"mosaic_b200 stage launch failed (rc={rc})")
+
+
+STAGE_NAMES = ["pool", "cmp_attn", "topk", "attend"]
+LAUNCHES_PER_STEP = 4
+
+
+def b200_arm(args):
+    from mosaic_b200 import _lib
+    import mosaic_b200 as M
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+    c = S1
+    B, N, Hq, Hk, D = c["B"], c["N"], c["Hq"], c["Hk"], c["D"]
+
+    # three input sets per rank (member = rank), rotated so inputs are never L2-resident
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sets = []
+    for _ in range(3):
+        sets.append(dict(
+            q=torch.randn(B, N, Hq, D, generator=g, device=dev).bfloat16(),
+            k=torch.randn(B, N, Hk, D, generator=g, device=dev).bfloat16(),
+            v=torch.randn(B, N, Hk, D, generator=g, device=dev).bfloat16(),
+            w=torch.sigmoid(torch.randn(3, B, N, Hq, generator=g, device=dev)).bfloat16()))
+    st = Stages(lib, c, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        st.run(sets[i % 3], stream)
+    torch.cuda.synchronize()
+    barrier()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        t_start.record(stream)
+        for i in range(args.steps):
+            st.run(sets[i % 3], stream, events[i])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = t_start.elapsed_time(t_end)
+    stage_ms = [sum(events[i][s].elapsed_time(events[i][s + 1]) for i in range(args.steps)) / args.steps
+                for s in range(4)]
+    status = int(st.status.item())
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * B * N * args.steps / (ms / 1000.0)
+
+    # e2e: public API with host buffers (pinned), H2D of inputs and D2H of the output every step
+    e2e = None
+    if not args.no_e2e:
+        host = [{k: v.cpu().pin_memory() for k, v in s_.items()} for s_ in sets[:2]]
+        out_host = torch.empty(B, N, Hq, D, dtype=torch.bfloat16).pin_memory()
+        dbuf = {k: torch.empty_like(v) for k, v in sets[0].items()}
+        h2d = sum(v.numel() * v.element_size() for v in host[0].values())
+        d2h = out_host.numel() * out_host.element_size()
+
+        def e2e_step(i):
+            for k_, v_ in host[i % 2].items():
+                dbuf[k_].copy_(v_, non_blocking=True)
+            o = M.mosaic_attn_func(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["w"], c["bas"], c["bs"], c["K"], False)
+            out_host.copy_(o, non_blocking=True)
+
+        n_e2e = max(3, min(args.steps, 50))
+        for i in range(args.warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(n_e2e):
+            e2e_step(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = a.elapsed_time(b)
+        if dist is not None:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": world * B * N * n_e2e / (e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": n_e2e}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        windows = [0, 9, 17, 25, 30, 38, 41, 47]
+        v_cpu, cores, secs = cpu_sample(c, windows, reps=3)
+        cpu = {"value": v_cpu, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"oracle port (fp32 torch) of mosaic_attn_func on S1: global pooling/coarse attention/"
+                         f"top-k over all tokens, local + selected branches for {len(windows)} of 48 windows "
+                         f"({len(windows) * c['bas']} query tokens), 3 timed reps after 1 warm-up, {secs:.1f} s"}
+
+    hbm, tf, src = peaks()
+    t_att = stage_ms[3] / 1000.0
+    achieved = flops_attend(c) / t_att / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "S1 mosaic_attn_func forward, Nside 64: N=49152, 12/3 heads, d64, sparse block 64, "
+                               "top-k 24, window 1024; one ensemble member per GPU",
+                   "B_per_gpu": B, "N": N, "Hq": Hq, "Hk": Hk, "head_dim": D, "sparse_block": c["bs"],
+                   "topk": c["K"], "window": c["bas"], "parallelism": f"members x{world}",
+                   "l2": "3 rotating input sets, 351 MB > 126 MB L2"},
+        "ensemble_step_per_s": value / (MEMBERS * N),
+        "roofline": {"bound": "tensor", "kernel": "bsa_engine_kernel (c: local + selected + gated combine)",
+                     "achieved": achieved, "peak": tf, "unit": "TFLOP/s", "frac": achieved / tf,
+                     "peak_source": src + " bf16_tflops (burst)", "traffic": None,
+                     "flop_per_launch": flops_attend(c)},
+        "kernels_us": {n: 1000 * t for n, t in zip(STAGE_NAMES, stage_ms)},
+        "pool_hbm": {"achieved_gbs": bytes_pool(c) / (stage_ms[0] / 1000) / 1e9, "peak_gbs": hbm,
+                     "frac": bytes_pool(c) / (stage_ms[0] / 1000) / 1e9 / hbm},
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "clocks": clk.summary(),
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        b200_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,143 @@
+/*
+ * mosaic_b200 — C ABI of the B200 (sm_100a) block-sparse attention forward of
+ * Mosaic (maxxxzdn/mosaic). Every entry point takes plain device pointers,
+ * sizes and a cudaStream_t (passed as void*), launches asynchronously on that
+ * stream, allocates nothing and synchronises nothing. Tensors are dense and
+ * row-major in the reference's layouts ([batch, seq, heads, head_dim]); all
+ * activations are bf16, head_dim is 64, and query heads per kv head (G) is 4.
+ *
+ * Return value: MOSAIC_OK or a MOSAIC_ERR_* code (argument errors are detected
+ * on the host before anything is launched). Faults detected on the device are
+ * OR-ed into the optional int32 status word (`status`, device memory) as
+ * MOSAIC_STATUS_* bits; the caller reads it when it wants to (no implicit sync).
+ */
+#ifndef MOSAIC_B200_H_
+#define MOSAIC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOSAIC_API __attribute__((visibility("default")))
+#else
+#define MOSAIC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ---------------------------------------------------- */
+#define MOSAIC_OK 0
+#define MOSAIC_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, misaligned pointer */
+#define MOSAIC_ERR_UNSUPPORTED 2      /* a shape this build does not handle (head_dim != 64, G != 4, ...) */
+#define MOSAIC_ERR_WORKSPACE 3        /* workspace missing or smaller than mosaic_bsa_workspace_bytes() */
+#define MOSAIC_ERR_CUDA 4             /* a CUDA runtime / driver call failed (launch, tensor map) */
+
+/* ---- device status bits (OR-ed into *status) -------------------------- */
+#define MOSAIC_STATUS_TIMEOUT 1   /* a pipeline wait exceeded its time limit; the kernel gave up */
+#define MOSAIC_STATUS_BAD_INDEX 2 /* a block index was outside [0, seq_len / block_size); it was clamped to 0 */
+
+/* Arguments of mosaic_bsa_fwd (the flags mirror primitives.mosaic_attn_func). */
+typedef struct MosaicBsaArgs {
+  const void* q;        /* [B, N, Hq, 64] bf16                                            */
+  const void* k;        /* [B, N, Hk, 64] bf16                                            */
+  const void* v;        /* [B, N, Hk, 64] bf16                                            */
+  const void* gates;    /* [3, B, N, Hq] bf16 = weight_ba_cmp_slc; NULL iff block_attn_only */
+  const float* rope_cos; /* [N, 32] fp32 or NULL. When set, q and k are NOT yet rotated:   */
+  const float* rope_sin; /*   the library applies Mosaic's 2D RoPE before pooling.          */
+  void* out;            /* [B, N, Hq, 64] bf16                                            */
+  int64_t* block_indices; /* [B, N/bs, Hk, K] int64 selected blocks (written); may be NULL */
+  void* workspace;      /* device scratch of >= mosaic_bsa_workspace_bytes() bytes, 256-aligned */
+  size_t workspace_bytes;
+  int* status;          /* device int32 status word or NULL                               */
+  int batch;            /* B  */
+  int seq_len;          /* N  */
+  int num_q_heads;      /* Hq */
+  int num_kv_heads;     /* Hk */
+  int head_dim;         /* must be 64 */
+  int block_attn_size;  /* local window length (primitives.block_attention)               */
+  int sparse_block_size;  /* bs: pooling / selection block length, multiple of 64         */
+  int sparse_block_count; /* K: selected blocks per query block (0 = no selected branch)  */
+  int block_attn_only;  /* != 0: return the local branch only                              */
+  int no_compression;   /* != 0: drop the compressed branch, renormalise w_ba / w_slc       */
+  float softmax_scale;  /* <= 0 selects head_dim^-0.5                                      */
+} MosaicBsaArgs;
+
+/* Version of this ABI (bumped on any signature or struct change). */
+MOSAIC_API int mosaic_abi_version(void);
+
+/* Human-readable text for a MOSAIC_ERR_* code. */
+MOSAIC_API const char* mosaic_error_string(int code);
+
+/* Scratch bytes mosaic_bsa_fwd needs for these sizes (pooled q/k/v, coarse
+ * attention output, block indices and, with RoPE, rotated q/k). */
+MOSAIC_API size_t mosaic_bsa_workspace_bytes(int batch, int seq_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                  int sparse_block_size, int sparse_block_count, int with_rope);
+
+/* Full Mosaic block-sparse attention forward: local block attention, compressed
+ * attention over mean-pooled blocks, top-k block selection, selected-block
+ * attention, gated combine.
+ * Replaces primitives.mosaic_attn_func (primitives.py:54-89) including the
+ * flash_attn_func calls at primitives.py:31 and :77 and ops.mosaic_sparse_attn
+ * (ops.py:557-566) it makes. */
+MOSAIC_API int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream);
+
+/* The fused attention stage of mosaic_bsa_fwd on its own: local-window attention
+ * + selected-block attention over the given block_indices + the gated combine
+ * with the coarse-attention rows o_cmp ([B, N/bs, Hq, 64] bf16, NULL when
+ * no_compression or when sparse_block_count == 0 uses only (w_ba, w_cmp)).
+ * combine: 0 = w0*o_ba + w1*o_cmp + w2*o_slc (primitives.py:89),
+ *          1 = no_compression renormalisation (primitives.py:71-74),
+ *          2 = sparse_block_count == 0 renormalisation (primitives.py:81-84). */
+MOSAIC_API int mosaic_bsa_attend_fwd(const void* q, const void* k, const void* v, const int64_t* block_indices,
+                                     const void* gates, const void* o_cmp, void* out, int* status, int batch,
+                                     int seq_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                     int block_attn_size, int sparse_block_size, int sparse_block_count,
+                                     int combine, float softmax_scale, void* stream);
+
+/* Selected-block attention: out[b,n,j] = softmax over the K*bs keys of blocks
+ * block_indices[b, n/bs, j/G, :] of kv head j/G. Optional lse (log2 units, fp32
+ * [B,N,Hq]). Replaces ops.mosaic_attn_fwd / mosaic_attn_fwd_kernel
+ * (ops.py:137-176, ops.py:25-134) behind ops.mosaic_sparse_attn (ops.py:557). */
+MOSAIC_API int mosaic_sparse_attn_fwd(const void* q, const void* k, const void* v, const int64_t* block_indices, void* out,
+                           float* lse, int* status, int batch, int seq_len, int num_q_heads, int num_kv_heads,
+                           int head_dim, int block_size, int block_count, float softmax_scale, void* stream);
+
+/* Local block attention: full (non-causal) GQA attention inside each window of
+ * block_size consecutive tokens. Replaces primitives.block_attention
+ * (primitives.py:28-32) = flash_attn_func on [(B*N/bs), bs, H, 64]. */
+MOSAIC_API int mosaic_block_attn_fwd(const void* q, const void* k, const void* v, void* out, int* status, int batch,
+                          int seq_len, int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                          float softmax_scale, void* stream);
+
+/* Mean-pool q, k, v over contiguous blocks of block_size tokens (fp32 sums,
+ * bf16 results); with rope_cos/rope_sin set, rotate q and k first and also write
+ * the rotated tensors to q_rot / k_rot. q_cmp and v_cmp may be NULL to skip them.
+ * Replaces the einops reduce calls at primitives.py:65-66,76 and, with RoPE,
+ * RoPE.forward (primitives.py:132-135) for q and k. */
+MOSAIC_API int mosaic_block_pool(const void* q, const void* k, const void* v, const float* rope_cos, const float* rope_sin,
+                      void* q_rot, void* k_rot, void* q_cmp, void* k_cmp, void* v_cmp, int batch, int seq_len,
+                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, void* stream);
+
+/* Coarse (compressed) attention over nb pooled tokens: full GQA attention with
+ * scale softmax_scale. Replaces flash_attn_func(q_cmp, k_cmp, v_cmp) at
+ * primitives.py:77 (without the repeat_interleave of :78, which the fused
+ * epilogue of mosaic_bsa_fwd does by indexing). */
+MOSAIC_API int mosaic_cmp_attn_fwd(const void* q_cmp, const void* k_cmp, const void* v_cmp, void* o_cmp, int* status,
+                        int batch, int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
+                        float softmax_scale, void* stream);
+
+/* Top-k block selection: scores_j = q_cmp[:, :, j] . k_cmp[:, :, j/G]^T (bf16),
+ * mean over the strided head group {h, h+Hk, ...} (bf16), then the indices of
+ * the block_count largest per (b, query block, kv head), sorted by score
+ * descending, ties to the lower index. Replaces primitives.attn_topk
+ * (primitives.py:35-51). */
+MOSAIC_API int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indices, int batch, int num_blocks,
+                     int num_q_heads, int num_kv_heads, int head_dim, int block_count, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOSAIC_B200_H_ */

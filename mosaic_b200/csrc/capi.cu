@@ -1,0 +1,340 @@
+// extern "C" entry points of libmosaic_b200.so (declared in include/mosaic_b200.h).
+//
+// Each entry point validates its arguments on the host before touching CUDA, so
+// a bad call returns an error code and launches nothing. Validation mirrors what
+// the reference path requires implicitly (einops rearranges that need N % bs == 0,
+// topk's K <= nb) plus the limits of these kernels (head_dim 64, G = 4).
+#include <cstring>
+
+#include <cudaTypedefs.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace mosaic {
+
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return 1;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 1;
+}
+
+namespace {
+
+constexpr int kMaxTopK = 128;    // topk.cu kMaxK
+constexpr int kMaxSelect = 1024;  // bsa_engine.cu kMaxSel
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+inline float default_scale(float s) { return s > 0.f ? s : 0.125f; }  // 64 ** -0.5
+
+// Shape checks shared by every attention entry point.
+int check_heads(int B, int N, int Hq, int Hk, int D) {
+  if (B < 0 || N < 0 || Hq <= 0 || Hk <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (D != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
+  if (Hq % Hk != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (Hq / Hk != 4) return MOSAIC_ERR_UNSUPPORTED;
+  return MOSAIC_OK;
+}
+
+struct Workspace {
+  size_t q_cmp, k_cmp, v_cmp, o_cmp, idx, q_rot, k_rot, total;
+};
+
+Workspace workspace_layout(int B, int N, int Hq, int Hk, int bs, int K, bool rope) {
+  Workspace w;
+  const size_t nb = bs > 0 ? static_cast<size_t>(N) / bs : 0;
+  size_t off = 0;
+  w.q_cmp = off; off += round256(static_cast<size_t>(B) * nb * Hq * 128);
+  w.k_cmp = off; off += round256(static_cast<size_t>(B) * nb * Hk * 128);
+  w.v_cmp = off; off += round256(static_cast<size_t>(B) * nb * Hk * 128);
+  w.o_cmp = off; off += round256(static_cast<size_t>(B) * nb * Hq * 128);
+  w.idx = off; off += round256(static_cast<size_t>(B) * nb * Hk * (K > 0 ? K : 0) * 8);
+  w.q_rot = off; off += rope ? round256(static_cast<size_t>(B) * N * Hq * 128) : 0;
+  w.k_rot = off; off += rope ? round256(static_cast<size_t>(B) * N * Hk * 128) : 0;
+  w.total = off;
+  return w;
+}
+
+}  // namespace
+}  // namespace mosaic
+
+using namespace mosaic;
+
+extern "C" {
+
+int mosaic_abi_version(void) { return 1; }
+
+const char* mosaic_error_string(int code) {
+  switch (code) {
+    case MOSAIC_OK: return "ok";
+    case MOSAIC_ERR_INVALID_ARGUMENT: return "invalid argument (null/misaligned pointer, negative or inconsistent size)";
+    case MOSAIC_ERR_UNSUPPORTED: return "unsupported shape (needs head_dim 64, 4 query heads per kv head, block sizes multiple of 64)";
+    case MOSAIC_ERR_WORKSPACE: return "workspace missing or smaller than mosaic_bsa_workspace_bytes()";
+    case MOSAIC_ERR_CUDA: return "CUDA call failed (kernel launch or tensor-map encoding)";
+    default: return "unknown mosaic_b200 error code";
+  }
+}
+
+size_t mosaic_bsa_workspace_bytes(int batch, int seq_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                  int sparse_block_size, int sparse_block_count, int with_rope) {
+  (void)head_dim;
+  if (batch < 0 || seq_len < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || sparse_block_size <= 0) return 0;
+  return workspace_layout(batch, seq_len, num_q_heads, num_kv_heads, sparse_block_size, sparse_block_count,
+                          with_rope != 0)
+      .total;
+}
+
+int mosaic_sparse_attn_fwd(const void* q, const void* k, const void* v, const int64_t* block_indices, void* out,
+                           float* lse, int* status, int batch, int seq_len, int num_q_heads, int num_kv_heads,
+                           int head_dim, int block_size, int block_count, float softmax_scale, void* stream) {
+  int rc = check_heads(batch, seq_len, num_q_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (batch == 0 || seq_len == 0) return MOSAIC_OK;
+  if (!q || !k || !v || !out || !block_indices) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_size <= 0 || block_count <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_size % 64 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (seq_len % block_size != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_count > kMaxSelect) return MOSAIC_ERR_UNSUPPORTED;
+  if (batch == 0 || seq_len == 0) return MOSAIC_OK;
+  EngineLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = q; a.k = k; a.v = v;
+  a.block_idx = block_indices;
+  a.out = out; a.lse = lse; a.status = status;
+  a.B = batch; a.Nq = seq_len; a.Nk = seq_len; a.Hq = num_q_heads; a.Hk = num_kv_heads;
+  a.win = 0; a.bs = block_size; a.K = block_count;
+  a.combine = kCombineSel;
+  a.softmax_scale = default_scale(softmax_scale);
+  return launch_engine(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_bsa_attend_fwd(const void* q, const void* k, const void* v, const int64_t* block_indices,
+                          const void* gates, const void* o_cmp, void* out, int* status, int batch, int seq_len,
+                          int num_q_heads, int num_kv_heads, int head_dim, int block_attn_size,
+                          int sparse_block_size, int sparse_block_count, int combine, float softmax_scale,
+                          void* stream) {
+  int rc = check_heads(batch, seq_len, num_q_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (batch == 0 || seq_len == 0) return MOSAIC_OK;
+  if (combine < kCombineGated || combine > kCombineNoSlc) return MOSAIC_ERR_INVALID_ARGUMENT;
+  const bool want_slc = combine != kCombineNoSlc;
+  const bool want_cmp = combine != kCombineNoCmp;
+  if (!q || !k || !v || !out || !gates) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (want_slc && !block_indices) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (want_cmp && !o_cmp) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || (o_cmp && !aligned16(o_cmp)))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_attn_size <= 0 || seq_len % block_attn_size != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_attn_size % 64 != 0 && block_attn_size != seq_len) return MOSAIC_ERR_UNSUPPORTED;
+  if (sparse_block_size <= 0 || seq_len % sparse_block_size != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (sparse_block_size % 64 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (want_slc && (sparse_block_count <= 0 || sparse_block_count > seq_len / sparse_block_size))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (sparse_block_count > kMaxSelect) return MOSAIC_ERR_UNSUPPORTED;
+  EngineLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = q; a.k = k; a.v = v;
+  a.block_idx = want_slc ? block_indices : nullptr;
+  a.gates = gates;
+  a.o_cmp = want_cmp ? o_cmp : nullptr;
+  a.out = out; a.status = status;
+  a.B = batch; a.Nq = seq_len; a.Nk = seq_len; a.Hq = num_q_heads; a.Hk = num_kv_heads;
+  a.win = block_attn_size; a.bs = sparse_block_size; a.K = want_slc ? sparse_block_count : 0;
+  a.combine = combine;
+  a.softmax_scale = default_scale(softmax_scale);
+  return launch_engine(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_block_attn_fwd(const void* q, const void* k, const void* v, void* out, int* status, int batch,
+                          int seq_len, int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                          float softmax_scale, void* stream) {
+  int rc = check_heads(batch, seq_len, num_q_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (batch == 0 || seq_len == 0) return MOSAIC_OK;
+  if (!q || !k || !v || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_size <= 0 || seq_len % block_size != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_size % 64 != 0 && block_size != seq_len) return MOSAIC_ERR_UNSUPPORTED;
+  if (batch == 0 || seq_len == 0) return MOSAIC_OK;
+  EngineLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = q; a.k = k; a.v = v; a.out = out; a.status = status;
+  a.B = batch; a.Nq = seq_len; a.Nk = seq_len; a.Hq = num_q_heads; a.Hk = num_kv_heads;
+  a.win = block_size; a.bs = 64; a.K = 0;
+  a.combine = kCombineLocal;
+  a.softmax_scale = default_scale(softmax_scale);
+  return launch_engine(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_cmp_attn_fwd(const void* q_cmp, const void* k_cmp, const void* v_cmp, void* o_cmp, int* status,
+                        int batch, int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
+                        float softmax_scale, void* stream) {
+  int rc = check_heads(batch, num_blocks, num_q_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (batch == 0 || num_blocks == 0) return MOSAIC_OK;
+  if (!q_cmp || !k_cmp || !v_cmp || !o_cmp) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q_cmp) || !aligned16(k_cmp) || !aligned16(v_cmp) || !aligned16(o_cmp))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || num_blocks == 0) return MOSAIC_OK;
+  EngineLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = q_cmp; a.k = k_cmp; a.v = v_cmp; a.out = o_cmp; a.status = status;
+  a.B = batch; a.Nq = num_blocks; a.Nk = num_blocks; a.Hq = num_q_heads; a.Hk = num_kv_heads;
+  a.win = num_blocks; a.bs = 64; a.K = 0;
+  a.combine = kCombineLocal;
+  a.softmax_scale = default_scale(softmax_scale);
+  return launch_engine(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_block_pool(const void* q, const void* k, const void* v, const float* rope_cos, const float* rope_sin,
+                      void* q_rot, void* k_rot, void* q_cmp, void* k_cmp, void* v_cmp, int batch, int seq_len,
+                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, void* stream) {
+  if (batch < 0 || seq_len < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
+  if (block_size <= 0 || seq_len % block_size != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!k || !k_cmp || (q_cmp && !q) || (v_cmp && !v)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (rope_cos && (!q || !q_cmp || !q_rot || !k_rot)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  const void* ptrs[] = {q, k, v, q_rot, k_rot, q_cmp, k_cmp, v_cmp, rope_cos, rope_sin};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || seq_len == 0) return MOSAIC_OK;
+  PoolLaunch a;
+  a.q = q; a.k = k; a.v = v;
+  a.rope_cos = rope_cos; a.rope_sin = rope_sin;
+  a.q_rot = q_rot; a.k_rot = k_rot;
+  a.q_cmp = q_cmp; a.k_cmp = k_cmp; a.v_cmp = v_cmp;
+  a.B = batch; a.N = seq_len; a.Hq = num_q_heads; a.Hk = num_kv_heads; a.bs = block_size;
+  return launch_pool(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indices, int batch, int num_blocks,
+                     int num_q_heads, int num_kv_heads, int head_dim, int block_count, void* stream) {
+  if (batch < 0 || num_blocks < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
+  if (num_q_heads % num_kv_heads != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (num_q_heads / num_kv_heads > 8) return MOSAIC_ERR_UNSUPPORTED;
+  if (!q_cmp || !k_cmp || !block_indices) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q_cmp) || !aligned16(k_cmp)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_count < 0 || block_count > num_blocks) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_count > kMaxTopK || num_blocks > 65535) return MOSAIC_ERR_UNSUPPORTED;
+  if (batch == 0 || num_blocks == 0 || block_count == 0) return MOSAIC_OK;
+  TopkLaunch a;
+  a.q_cmp = q_cmp; a.k_cmp = k_cmp; a.idx = block_indices;
+  a.B = batch; a.nb = num_blocks; a.Hq = num_q_heads; a.Hk = num_kv_heads; a.K = block_count;
+  return launch_topk(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
+  if (args == nullptr) return MOSAIC_ERR_INVALID_ARGUMENT;
+  const MosaicBsaArgs& A = *args;
+  const int B = A.batch, N = A.seq_len, Hq = A.num_q_heads, Hk = A.num_kv_heads;
+  const int bas = A.block_attn_size, bs = A.sparse_block_size, K = A.sparse_block_count;
+  const bool local_only = A.block_attn_only != 0, no_cmp = A.no_compression != 0;
+  const bool rope = A.rope_cos != nullptr;
+  int rc = check_heads(B, N, Hq, Hk, A.head_dim);
+  if (rc) return rc;
+  if (B == 0 || N == 0) return MOSAIC_OK;
+  if (!A.q || !A.k || !A.v || !A.out) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!local_only && !A.gates) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if ((A.rope_cos == nullptr) != (A.rope_sin == nullptr)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  const void* ptrs[] = {A.q, A.k, A.v, A.out, A.rope_cos, A.rope_sin, A.workspace};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (bas <= 0 || N % bas != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (bas % 64 != 0 && bas != N) return MOSAIC_ERR_UNSUPPORTED;
+  if (!local_only || rope) {
+    if (bs <= 0 || N % bs != 0 || K < 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+    if (bs % 64 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  }
+  const int nb = bs > 0 ? N / bs : 0;
+  if (!local_only) {
+    if (K > nb) return MOSAIC_ERR_INVALID_ARGUMENT;
+    if (no_cmp && K == 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+    if (K > kMaxTopK || nb > 65535) return MOSAIC_ERR_UNSUPPORTED;
+  }
+  const Workspace ws = workspace_layout(B, N, Hq, Hk, bs > 0 ? bs : 64, local_only ? 0 : K, rope);
+  const bool need_ws = !local_only || rope;
+  if (need_ws && (A.workspace == nullptr || A.workspace_bytes < ws.total)) return MOSAIC_ERR_WORKSPACE;
+  if (B == 0 || N == 0) return MOSAIC_OK;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(A.workspace);
+  const void* q = A.q;
+  const void* k = A.k;
+  void* q_cmp = w ? w + ws.q_cmp : nullptr;
+  void* k_cmp = w ? w + ws.k_cmp : nullptr;
+  void* v_cmp = w ? w + ws.v_cmp : nullptr;
+  void* o_cmp = w ? w + ws.o_cmp : nullptr;
+  int64_t* idx = A.block_indices ? A.block_indices : (w ? reinterpret_cast<int64_t*>(w + ws.idx) : nullptr);
+  const float scale = default_scale(A.softmax_scale);
+  const bool want_cmp = !local_only && !no_cmp;     // compressed branch
+  const bool want_slc = !local_only && K > 0;       // selected branch
+
+  // (a) RoPE + block mean-pool
+  if (need_ws) {
+    PoolLaunch pl;
+    pl.q = A.q; pl.k = A.k; pl.v = A.v;
+    pl.rope_cos = A.rope_cos; pl.rope_sin = A.rope_sin;
+    pl.q_rot = rope ? w + ws.q_rot : nullptr;
+    pl.k_rot = rope ? w + ws.k_rot : nullptr;
+    pl.q_cmp = q_cmp; pl.k_cmp = k_cmp;
+    pl.v_cmp = want_cmp ? v_cmp : nullptr;
+    pl.B = B; pl.N = N; pl.Hq = Hq; pl.Hk = Hk; pl.bs = bs > 0 ? bs : 64;
+    if ((rc = launch_pool(pl, st))) return rc;
+    if (rope) {
+      q = pl.q_rot;
+      k = pl.k_rot;
+    }
+  }
+  // (a) coarse attention over the pooled blocks
+  if (want_cmp) {
+    EngineLaunch e;
+    std::memset(&e, 0, sizeof(e));
+    e.q = q_cmp; e.k = k_cmp; e.v = v_cmp; e.out = o_cmp; e.status = A.status;
+    e.B = B; e.Nq = nb; e.Nk = nb; e.Hq = Hq; e.Hk = Hk;
+    e.win = nb; e.bs = 64; e.K = 0; e.combine = kCombineLocal; e.softmax_scale = scale;
+    if ((rc = launch_engine(e, st))) return rc;
+  }
+  // (b) block scores + top-k
+  if (want_slc) {
+    TopkLaunch t;
+    t.q_cmp = q_cmp; t.k_cmp = k_cmp; t.idx = idx;
+    t.B = B; t.nb = nb; t.Hq = Hq; t.Hk = Hk; t.K = K;
+    if ((rc = launch_topk(t, st))) return rc;
+  }
+  // (c) fused local + selected attention with the gated combine
+  EngineLaunch e;
+  std::memset(&e, 0, sizeof(e));
+  e.q = q; e.k = k; e.v = A.v;
+  e.block_idx = want_slc ? idx : nullptr;
+  e.gates = A.gates;
+  e.o_cmp = want_cmp ? o_cmp : nullptr;
+  e.out = A.out;
+  e.status = A.status;
+  e.B = B; e.Nq = N; e.Nk = N; e.Hq = Hq; e.Hk = Hk;
+  e.win = bas;
+  e.bs = bs > 0 ? bs : 64;
+  e.K = want_slc ? K : 0;
+  e.combine = local_only ? kCombineLocal : (no_cmp ? kCombineNoCmp : (want_slc ? kCombineGated : kCombineNoSlc));
+  e.softmax_scale = scale;
+  return launch_engine(e, st);
+}
+
+}  // extern "C"

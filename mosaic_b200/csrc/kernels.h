@@ -1,0 +1,76 @@
+// Internal (C++) launch interface shared by the .cu files of libmosaic_b200.
+// The public C ABI lives in include/mosaic_b200.h; nothing here crosses it.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace mosaic {
+
+constexpr int kHeadDim = 64;
+
+// How the attention engine combines its branches in the epilogue, per output row
+// with gates (w0, w1, w2) = weight_ba_cmp_slc[:, b, n, head]:
+enum Combine : int {
+  kCombineGated = 0,  // w0*o_ba + w1*o_cmp + w2*o_slc              primitives.py:89
+  kCombineNoCmp = 1,  // (w0*o_ba + w2*o_slc) / (w0 + w2 + 1e-8)     primitives.py:71-74
+  kCombineNoSlc = 2,  // (w0*o_ba + w1*o_cmp) / (w0 + w1 + 1e-8)     primitives.py:81-84
+  kCombineLocal = 3,  // o_ba                                         primitives.py:28-32, 62-63
+  kCombineSel = 4,    // o_slc                                        ops.py:25-134
+};
+
+// One launch of the fused attention engine: for every (batch b, kv head h,
+// 64-query tile) it runs the local-window branch and/or the selected-block branch
+// for the G = 4 query heads of kv group h and writes the combined bf16 rows.
+struct EngineLaunch {
+  const void* q;  // [B, Nq, Hq, 64] bf16
+  const void* k;  // [B, Nk, Hk, 64] bf16
+  const void* v;  // [B, Nk, Hk, 64] bf16
+  const int64_t* block_idx;  // [B, Nq/bs, Hk, K] or null when K == 0
+  const void* gates;         // [3, B, Nq, Hq] bf16 or null
+  const void* o_cmp;         // [B, Nq/bs, Hq, 64] bf16 or null
+  void* out;                 // [B, Nq, Hq, 64] bf16
+  float* lse;                // [B, Nq, Hq] fp32 (selected branch, log2 units) or null
+  int* status;               // device status word or null
+  int B, Nq, Nk, Hq, Hk;
+  int win;  // local window length; 0 = no local branch
+  int bs;   // selected block length (multiple of 64)
+  int K;    // selected blocks per query block; 0 = no selected branch
+  int combine;
+  float softmax_scale;
+};
+
+// Mean-pool (optionally after 2D RoPE) of q, k, v over contiguous blocks of `bs` rows.
+struct PoolLaunch {
+  const void* q;  // [B, N, Hq, 64] bf16
+  const void* k;  // [B, N, Hk, 64] bf16
+  const void* v;  // [B, N, Hk, 64] bf16
+  const float* rope_cos;  // [N, 32] fp32 or null (no rotation)
+  const float* rope_sin;  // [N, 32] fp32 or null
+  void* q_rot;            // [B, N, Hq, 64] bf16 rotated copy (only when rope_cos != null)
+  void* k_rot;            // [B, N, Hk, 64] bf16 rotated copy (only when rope_cos != null)
+  void* q_cmp;            // [B, N/bs, Hq, 64] bf16 (may be null: skip q)
+  void* k_cmp;            // [B, N/bs, Hk, 64] bf16
+  void* v_cmp;            // [B, N/bs, Hk, 64] bf16 (may be null: skip v)
+  int B, N, Hq, Hk, bs;
+};
+
+// Block scores + top-k selection (GQA group shared, strided head mean).
+struct TopkLaunch {
+  const void* q_cmp;  // [B, nb, Hq, 64] bf16
+  const void* k_cmp;  // [B, nb, Hk, 64] bf16
+  int64_t* idx;       // [B, nb, Hk, K]
+  int B, nb, Hq, Hk, K;
+};
+
+int launch_engine(const EngineLaunch& a, cudaStream_t stream);
+int launch_pool(const PoolLaunch& a, cudaStream_t stream);
+int launch_topk(const TopkLaunch& a, cudaStream_t stream);
+
+// Encodes a 2D bf16 tensor map over `rows` x `cols` elements (row pitch = cols),
+// 64x64 boxes, 128-byte swizzle. Returns 0 on success.
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
+
+}  // namespace mosaic

@@ -1,0 +1,116 @@
+"""Drop-in for the reference's ops module (ops.py): `mosaic_sparse_attn`.
+
+Same call signature and semantics as ops.mosaic_sparse_attn (ops.py:557-566):
+q [B, N, Hq, D], k/v [B, N, Hk, D], block_indices int64 [B, N // block_size, Hk, K];
+query n of q head j attends to the K*block_size keys of blocks
+block_indices[b, n // block_size, j // (Hq // Hk), :] of kv head j // (Hq // Hk)
+with softmax scale `softmax_scale` (default D ** -0.5). Like the reference
+kernel (ops.py:92,115-116) the arithmetic is bf16 with fp32 accumulation
+whatever the input dtype; the result is returned in q's dtype (ops.py:538).
+
+The work runs in `mosaic_sparse_attn_fwd` of libmosaic_b200.so on the current
+CUDA stream. There is no CPU path: CPU tensors raise, as the reference's
+Triton kernel would.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = ["mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "MosaicAttnFunction"]
+
+
+def _stream_ptr(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError("mosaic_b200 ops need CUDA tensors (there is no CPU implementation)")
+    dev = tensors[0].device
+    for t in tensors[1:]:
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same CUDA device")
+
+
+def _bf16(t):
+    t = t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
+    return t.contiguous()
+
+
+def _check_qkv(q, k, v):
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("q, k, v must be [batch, seq_len, heads, head_dim]")
+    if k.shape != v.shape or q.shape[0] != k.shape[0] or q.shape[1] != k.shape[1] or q.shape[3] != k.shape[3]:
+        raise ValueError(f"inconsistent q/k/v shapes {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
+    if q.shape[2] % k.shape[2] != 0:
+        raise ValueError("num_q_heads must be a multiple of num_kv_heads")
+
+
+def status_buffer(device):
+    """A zeroed device int32 status word for the C ABI's optional `status` argument."""
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def check_status(status):
+    """Synchronising read of a status word; raises on any device-side fault bit."""
+    s = int(status.item())
+    if s & _lib.MOSAIC_STATUS_TIMEOUT:
+        raise RuntimeError("mosaic_b200: a kernel pipeline wait timed out (results are invalid)")
+    if s & _lib.MOSAIC_STATUS_BAD_INDEX:
+        raise RuntimeError("mosaic_b200: block index outside [0, seq_len // block_size)")
+    return s
+
+
+def _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse, status=None):
+    _require_cuda(q, k, v, block_indices)
+    _check_qkv(q, k, v)
+    B, N, Hq, D = q.shape
+    Hk = k.shape[2]
+    if block_indices.dim() != 4 or tuple(block_indices.shape[:3]) != (B, N // block_size, Hk):
+        raise ValueError(f"block_indices must be [B, N // block_size, Hk, K], got {tuple(block_indices.shape)}")
+    lib = _lib.load()
+    qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
+    idx = block_indices.to(torch.int64).contiguous()
+    out = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=q.device)
+    lse = torch.empty(B, N, Hq, dtype=torch.float32, device=q.device) if want_lse else None
+    with torch.cuda.device(q.device):
+        rc = lib.mosaic_sparse_attn_fwd(
+            _ptr(qb), _ptr(kb), _ptr(vb), _ptr(idx), _ptr(out), _ptr(lse), _ptr(status),
+            B, N, Hq, Hk, D, int(block_size), int(idx.shape[-1]), float(softmax_scale), _stream_ptr(q.device))
+    _lib.check("mosaic_sparse_attn_fwd", rc)
+    return out, lse
+
+
+class MosaicAttnFunction(torch.autograd.Function):
+    """Forward of ops.MosaicAttnFunction (ops.py:510-538). Backward is not part of
+    this library (inference forward only) and raises if reached."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, block_indices, block_size, softmax_scale):
+        out, _ = _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=False)
+        return out.to(q.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_o):
+        raise NotImplementedError("mosaic_b200 implements the block-sparse attention forward only")
+
+
+def mosaic_sparse_attn(q, k, v, block_indices, block_size, softmax_scale=None):
+    """Selected-block attention forward (ops.py:557-566)."""
+    softmax_scale = q.shape[-1] ** -0.5 if softmax_scale is None else softmax_scale
+    return MosaicAttnFunction.apply(q, k, v, block_indices, block_size, softmax_scale)
+
+
+def mosaic_sparse_attn_with_lse(q, k, v, block_indices, block_size, softmax_scale=None, status=None):
+    """Like mosaic_sparse_attn, also returning the log-sum-exp in log2 units
+    (fp32 [B, N, Hq]), the second output of ops.mosaic_attn_fwd (ops.py:176)."""
+    softmax_scale = q.shape[-1] ** -0.5 if softmax_scale is None else softmax_scale
+    out, lse = _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=True, status=status)
+    return out.to(q.dtype), lse

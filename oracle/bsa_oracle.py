@@ -1,0 +1,298 @@
+"""CPU restatement of the reference's block-sparse attention forward.
+
+TEST INFRASTRUCTURE: the checker for the CUDA path and the timed CPU baseline.
+Only tests/, __graft_entry__.smoke() and bench.py's CPU legs use it; the product
+path never does.
+
+Each function restates one piece of maxxxzdn/mosaic in plain torch on the CPU
+(fp32 arithmetic unless stated), citing the reference file:line it follows.
+Two pieces of the reference live in third-party code that is absent here and are
+restated from their published definitions:
+  * flash_attn.flash_attn_func (flash-attn, unpinned `flash-attn>=2.0` in
+    requirements.txt:9; 2.8.3 in the build image): non-causal softmax attention,
+    default scale head_dim**-0.5, query head j reads kv head j // (Hq // Hk);
+  * healpy.pix2ang(nest=True) (healpy>=1.16, requirements.txt:3): see
+    `pix2ang_nest_scalar` below (HEALPix nested geometry, Gorski et al. 2005).
+Pinning: tests/golden/make_golden.py runs the reference code itself (imported
+from the reference checkout, its Triton kernel under TRITON_INTERPRET=1) on
+seeded inputs and commits the results as fixtures; tests/test_oracle_golden.py
+checks this module against them. The HEALPix restatement has no reference-side
+fixture (healpy is not installed), so it is pinned by HEALPix known answers only.
+"""
+import math
+
+import torch
+
+LOG2_E = 1.44269504089
+
+
+# --------------------------------------------------------------------------- geometry
+_JRLL = [2, 2, 2, 2, 3, 3, 3, 3, 4, 4, 4, 4]
+_JPLL = [1, 3, 5, 7, 0, 2, 4, 6, 1, 3, 5, 7]
+
+
+def pix2ang_nest_scalar(nside, ipix):
+    """(theta, phi) radians of one NESTED pixel centre (healpy.pix2ang(nest=True)).
+
+    Pure-Python restatement (Gorski et al. 2005): de-interleave the in-face index
+    into (x, y), ring jr = jrll[face]*nside - x - y - 1, then z and phi from the
+    polar-cap / equatorial-belt formulas."""
+    npface = nside * nside
+    face, ipf = divmod(ipix, npface)
+    ix = iy = 0
+    bit = 0
+    while ipf:
+        ix |= (ipf & 1) << bit
+        iy |= ((ipf >> 1) & 1) << bit
+        ipf >>= 2
+        bit += 1
+    jr = _JRLL[face] * nside - ix - iy - 1
+    npix = 12 * npface
+    if jr < nside:
+        nr = jr
+        z = 1.0 - nr * nr * 4.0 / npix
+        kshift = 0
+    elif jr > 3 * nside:
+        nr = 4 * nside - jr
+        z = -(1.0 - nr * nr * 4.0 / npix)
+        kshift = 0
+    else:
+        nr = nside
+        z = (2 * nside - jr) * 2.0 * nside * 4.0 / npix
+        kshift = (jr - nside) & 1
+    jp = (_JPLL[face] * nr + ix - iy + 1 + kshift) // 2
+    if jp > 4 * nside:
+        jp -= 4 * nside
+    if jp < 1:
+        jp += 4 * nside
+    phi = (jp - (kshift + 1) * 0.5) * (0.5 * math.pi / nr)
+    return math.acos(max(-1.0, min(1.0, z))), phi
+
+
+def healpix_grid(nside):
+    """float32 [npix, 2] (lon deg, lat deg): utils.get_healpix_grid (utils.py:19-30)."""
+    rows = []
+    for p in range(12 * nside * nside):
+        th, ph = pix2ang_nest_scalar(nside, p)
+        rows.append((math.degrees(ph), 90.0 - math.degrees(th)))
+    return torch.tensor(rows, dtype=torch.float64).float()
+
+
+def rope_tables(positions, dim=64, theta=10000):
+    """(cos, sin) [N, dim/2] fp32: RoPE.initialize_rope (primitives.py:115-123)."""
+    base = 1.0 / (theta ** (torch.arange(0, dim // 2, 2).float() / (dim // 2)))
+    lon = torch.deg2rad(positions[:, 0:1])
+    lat = torch.deg2rad(positions[:, 1:2])
+    freqs = torch.cat([lon @ base.unsqueeze(0), lat @ base.unsqueeze(0)], dim=-1)
+    return freqs.cos(), freqs.sin()
+
+
+def rope_apply(x, cos, sin):
+    """RoPE.forward (primitives.py:126-135): interleaved-pair rotation in fp32, cast back."""
+    c = cos.unsqueeze(0).unsqueeze(2).repeat_interleave(2, dim=-1)
+    s = sin.unsqueeze(0).unsqueeze(2).repeat_interleave(2, dim=-1)
+    xf = x.float()
+    pairs = xf.unflatten(-1, (-1, 2))
+    rot = torch.stack((-pairs[..., 1], pairs[..., 0]), dim=-1).flatten(-2)
+    return (xf * c + rot * s).to(x.dtype)
+
+
+# --------------------------------------------------------------------------- attention pieces
+def dense_attention(q, k, v, scale=None):
+    """flash_attn_func semantics (third-party; see module docstring): q [B, L, Hq, D],
+    k/v [B, S, Hk, D] -> [B, L, Hq, D] fp32, query head j reads kv head j // G."""
+    B, L, Hq, D = q.shape
+    Hk = k.shape[2]
+    G = Hq // Hk
+    scale = D ** -0.5 if scale is None else scale
+    qf = q.float().transpose(1, 2)                                   # B Hq L D
+    kf = k.float().repeat_interleave(G, dim=2).transpose(1, 2)       # B Hq S D
+    vf = v.float().repeat_interleave(G, dim=2).transpose(1, 2)
+    att = torch.softmax((qf @ kf.transpose(-1, -2)) * scale, dim=-1)
+    return (att @ vf).transpose(1, 2)
+
+
+def block_attention(q, k, v, block_size):
+    """primitives.block_attention (primitives.py:28-32): dense attention per window."""
+    B, N, Hq, D = q.shape
+    nb = N // block_size
+    r = lambda x: x.reshape(B * nb, block_size, x.shape[2], D)
+    return dense_attention(r(q), r(k), r(v)).reshape(B, N, Hq, D)
+
+
+def pool_mean(x, block_size):
+    """reduce(x, 'b (nb bs) h d -> b nb h d', 'mean') (primitives.py:65-66,76):
+    fp32 sum, one rounding to x's dtype."""
+    B, N, H, D = x.shape
+    return x.float().reshape(B, N // block_size, block_size, H, D).mean(dim=2).to(x.dtype)
+
+
+def topk_scores(q_cmp, k_cmp):
+    """The score matrix attn_topk ranks (primitives.py:37-49), with the reference's
+    rounding points for bf16 inputs: S_j = q_j . k_{j//G} rounded to the input
+    dtype, then the mean over the STRIDED group (g h), h fastest
+    ('b (g h) t k -> b h t k', :47), again rounded. Returns [B, nb, Hk, nb]."""
+    Hq, Hk = q_cmp.shape[2], k_cmp.shape[2]
+    G = Hq // Hk
+    dt = q_cmp.dtype
+    kk = k_cmp.repeat_interleave(G, dim=2)
+    s = (q_cmp.float().transpose(1, 2) @ kk.float().transpose(1, 2).transpose(-1, -2)).to(dt)  # B Hq t k
+    if Hq != Hk:
+        s = s.float().reshape(s.shape[0], G, Hk, s.shape[2], s.shape[3]).mean(dim=1).to(dt)
+    return s.transpose(1, 2)  # B t Hk k
+
+
+def attn_topk(q_cmp, k_cmp, block_count):
+    """primitives.attn_topk (primitives.py:35-51): int64 [B, nb, Hk, K], scores descending,
+    ties to the lower index (torch leaves tie order unspecified; the checker accepts
+    any order inside a tie)."""
+    t = topk_scores(q_cmp, k_cmp).float()
+    order = torch.sort(-t, dim=-1, stable=True).indices  # descending, equal scores keep index order
+    return order[..., :block_count].contiguous()
+
+
+def sparse_attention(q, k, v, block_indices, block_size, softmax_scale=None, return_lse=False, qblocks=None):
+    """ops.mosaic_attn_fwd_kernel (ops.py:25-134) in fp32: query n of head j attends to
+    the keys of blocks block_indices[b, n // block_size, j // G, :] of kv head j // G
+    (the CONTIGUOUS group, ops.py:47-49). LSE in log2 units (ops.py:131).
+    `qblocks=(lo, hi)` restricts the work to query blocks lo..hi-1 (other rows are
+    left uninitialised); the CPU timing sample uses it."""
+    B, N, Hq, D = q.shape
+    Hk = k.shape[2]
+    G = Hq // Hk
+    K = block_indices.shape[-1]
+    scale = D ** -0.5 if softmax_scale is None else softmax_scale
+    nb = N // block_size
+    out = torch.empty(B, N, Hq, D, dtype=torch.float32)
+    lse = torch.empty(B, N, Hq, dtype=torch.float32)
+    qf, kf, vf = q.float(), k.float(), v.float()
+    ar = torch.arange(block_size)
+    lo, hi = (0, nb) if qblocks is None else qblocks
+    n0, n1 = lo * block_size, hi * block_size
+    for b in range(B):
+        for h in range(Hk):
+            sel = block_indices[b, lo:hi, h, :].long()
+            rows = (sel.unsqueeze(-1) * block_size + ar).reshape(hi - lo, K * block_size)
+            ks = kf[b, :, h][rows]                                   # nblk, K*bs, D
+            vs = vf[b, :, h][rows]
+            for g in range(G):
+                j = h * G + g
+                qq = qf[b, n0:n1, j].reshape(hi - lo, block_size, D) * (scale * LOG2_E)
+                s2 = qq @ ks.transpose(-1, -2)                       # nblk, bs, K*bs  (log2 domain)
+                m = s2.amax(dim=-1, keepdim=True)
+                p = torch.exp2(s2 - m)
+                l = p.sum(dim=-1, keepdim=True)
+                out[b, n0:n1, j] = ((p @ vs) / l).reshape(n1 - n0, D)
+                lse[b, n0:n1, j] = (m + torch.log2(l)).reshape(n1 - n0)
+    return (out, lse) if return_lse else out
+
+
+def mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,
+                     block_attn_only, no_compression=False, block_indices=None, parts=None):
+    """primitives.mosaic_attn_func (primitives.py:54-89), fp32 arithmetic.
+
+    `block_indices` overrides the top-k selection (to compare outputs against a
+    kernel whose selection differs from this oracle's only inside score ties);
+    `parts`, if a dict, receives o_ba / o_cmp / o_slc / block_indices."""
+    o_ba = block_attention(q, k, v, block_attn_size)
+    if parts is not None:
+        parts["o_ba"] = o_ba
+    if block_attn_only:
+        return o_ba
+    w = weight_ba_cmp_slc.float()
+    q_cmp = pool_mean(q, sparse_block_size)
+    k_cmp = pool_mean(k, sparse_block_size)
+    if no_compression:
+        idx = attn_topk(q_cmp, k_cmp, sparse_block_count) if block_indices is None else block_indices
+        o_slc = sparse_attention(q, k, v, idx, sparse_block_size)
+        if parts is not None:
+            parts.update(o_slc=o_slc, block_indices=idx)
+        w_sum = w[0] + w[2] + 1e-8
+        return o_ba * (w[0] / w_sum) + o_slc * (w[2] / w_sum)
+    v_cmp = pool_mean(v, sparse_block_size)
+    o_cmp = dense_attention(q_cmp, k_cmp, v_cmp).repeat_interleave(sparse_block_size, dim=1)
+    if parts is not None:
+        parts["o_cmp"] = o_cmp
+    if sparse_block_count == 0:
+        w_sum = w[0] + w[1] + 1e-8
+        return o_ba * (w[0] / w_sum) + o_cmp * (w[1] / w_sum)
+    idx = attn_topk(q_cmp, k_cmp, sparse_block_count) if block_indices is None else block_indices
+    o_slc = sparse_attention(q, k, v, idx, sparse_block_size)
+    if parts is not None:
+        parts.update(o_slc=o_slc, block_indices=idx)
+    return o_ba * w[0] + o_cmp * w[1] + o_slc * w[2]
+
+
+def mosaic_attn_func_sample(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,
+                            windows):
+    """mosaic_attn_func restricted to the queries of the given local windows: the
+    compression and top-k run over the whole sequence (they are global), the
+    local and selected branches only for those windows. A bounded, proportional
+    sample of the full forward for CPU timing. Returns [B, len(windows)*bas, Hq, D]."""
+    bas, bs, K = block_attn_size, sparse_block_size, sparse_block_count
+    w = weight_ba_cmp_slc.float()
+    q_cmp, k_cmp, v_cmp = pool_mean(q, bs), pool_mean(k, bs), pool_mean(v, bs)
+    o_cmp = dense_attention(q_cmp, k_cmp, v_cmp)
+    idx = attn_topk(q_cmp, k_cmp, K)
+    outs = []
+    for win in windows:
+        n0, n1 = win * bas, (win + 1) * bas
+        o_ba = dense_attention(q[:, n0:n1], k[:, n0:n1], v[:, n0:n1])
+        o_slc = sparse_attention(q, k, v, idx, bs, qblocks=(n0 // bs, n1 // bs))[:, n0:n1]
+        o_c = o_cmp.repeat_interleave(bs, dim=1)[:, n0:n1]
+        outs.append(o_ba * w[0, :, n0:n1] + o_c * w[1, :, n0:n1] + o_slc * w[2, :, n0:n1])
+    return torch.cat(outs, dim=1)
+
+
+# --------------------------------------------------------------------------- checkers
+def topk_matches(idx_test, idx_ref, scores, rel=1e-3):
+    """Top-k parity up to score ties: for every row the two index SETS must agree,
+    except for entries whose score lies within `rel` (relative) of that row's K-th
+    score (the tie boundary). Returns (ok, number_of_rows_that_differ)."""
+    idx_test = idx_test.long()
+    idx_ref = idx_ref.long()
+    sc = scores.float()
+    K = idx_ref.shape[-1]
+    kth = torch.gather(sc, -1, idx_ref).amin(dim=-1, keepdim=True)       # reference K-th score
+    tol = kth.abs() * rel + 1e-30
+    a = torch.zeros_like(sc, dtype=torch.bool).scatter_(-1, idx_test, True)
+    b = torch.zeros_like(sc, dtype=torch.bool).scatter_(-1, idx_ref, True)
+    diff = a ^ b
+    near = (sc - kth).abs() <= tol
+    bad = diff & ~near
+    # a kernel row must also hold K distinct indices
+    distinct = a.sum(dim=-1) == K
+    ok = bool((~bad).all()) and bool(distinct.all())
+    return ok, int(diff.any(dim=-1).sum())
+
+
+def make_inputs(B, N, Hq, Hk, D=64, seed=0, dtype=torch.bfloat16, rope=True):
+    """Seeded synthetic inputs (draw order q, k, v, gate logits): q/k/v ~ N(0,1),
+    gates = sigmoid(N(0,1)) [3, B, N, Hq, 1]; with `rope`, q and k are rotated by
+    the nested-HEALPix 2D RoPE of nside = sqrt(N / 12) (as MosaicAttention.forward
+    does before calling the op, primitives.py:193-195). Returns a dict with the
+    un-rotated tensors too."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, N, Hq, D, generator=g).to(dtype)
+    k = torch.randn(B, N, Hk, D, generator=g).to(dtype)
+    v = torch.randn(B, N, Hk, D, generator=g).to(dtype)
+    w = torch.sigmoid(torch.randn(3, B, N, Hq, 1, generator=g)).to(dtype)
+    out = dict(q_raw=q, k_raw=k, v=v, w=w, q=q, k=k, cos=None, sin=None)
+    if rope:
+        nside = int(round(math.sqrt(N / 12)))
+        if 12 * nside * nside != N:
+            raise ValueError(f"N={N} is not a HEALPix pixel count")
+        cos, sin = rope_tables(healpix_grid_fast(nside), D)
+        out.update(q=rope_apply(q, cos, sin), k=rope_apply(k, cos, sin), cos=cos, sin=sin)
+    return out
+
+
+def healpix_grid_fast(nside):
+    """healpix_grid for large nside (the scalar loop is slow at nside 64+); same maths,
+    cached per nside."""
+    if nside not in _GRID_CACHE:
+        _GRID_CACHE[nside] = healpix_grid(nside)
+    return _GRID_CACHE[nside]
+
+
+_GRID_CACHE = {}

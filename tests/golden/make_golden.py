@@ -1,0 +1,157 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE code.
+
+Run from the repository root in a container that has the reference checkout:
+
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/mosaic/reference
+
+It imports the reference's `ops` and `primitives` modules and runs, on the CPU:
+  * primitives.mosaic_attn_func / attn_topk / RoPE / the einops pooling as-is;
+  * ops.mosaic_attn_fwd_kernel (the Triton kernel itself) through Triton's
+    interpreter, as the selected-branch attention (primitives.mosaic_sparse_attn
+    is rebound to that launch);
+  * primitives.flash_attn_func rebound to torch SDPA with GQA (flash-attn is a
+    CUDA-only third-party op; its published semantics are non-causal softmax
+    attention, scale head_dim**-0.5, query head j -> kv head j // G).
+healpy is not installed: the nested pixel centres for the RoPE angles come from
+the restatement in oracle/bsa_oracle.py (pinned separately by known answers).
+
+Harness patches (test-side only, to the Triton interpreter): bf16 operands of
+tl.dot are up-converted to fp32 before numpy's matmul (the stock interpreter
+stores bf16 as uint16 and would multiply the raw bits). Kernel inputs are fp32
+tensors holding bf16-representable values; the kernel casts them to bf16 itself
+(ops.py:92,115-116), so this is the bf16 computation of the reference.
+
+Outputs are fp32 (the reference run in fp32 on bf16-valued inputs); top-k is
+taken from the bf16 run of attn_topk on bf16 pooled tensors, which is the
+precision of the B200 path, and the fp32 run is driven with those indices.
+Fixtures keep the full indices, the small pooled outputs, 64 sampled query rows
+of every larger output (fp16) and fp64 per-head sums of the full outputs.
+"""
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _import_reference(ref_dir):
+    if os.environ.get("TRITON_INTERPRET") != "1":
+        raise SystemExit("set TRITON_INTERPRET=1 (the reference Triton kernel runs in the interpreter)")
+    sys.path.insert(0, ref_dir)
+    sys.modules.setdefault("healpy", types.ModuleType("healpy"))
+    import triton.language as tl
+    import triton.runtime.interpreter as interp
+
+    def create_dot(self, a, b, d, input_precision, max_num_imprecise_acc):
+        def up(h):
+            if h.dtype.scalar == tl.bfloat16:
+                return interp._convert_float(h.data, tl.bfloat16, tl.float32, None).view(np.float32)
+            return h.data
+        return interp.TensorHandle(np.matmul(up(a), up(b), dtype=d.data.dtype) + d.data, d.dtype.scalar)
+
+    interp.InterpreterBuilder.create_dot = create_dot
+    import ops
+    import primitives
+    return ops, primitives
+
+
+def sdpa_gqa(q, k, v):
+    """flash_attn_func(q, k, v) semantics on CPU (fp32)."""
+    G = q.shape[2] // k.shape[2]
+    o = F.scaled_dot_product_attention(q.transpose(1, 2).float(), k.transpose(1, 2).float(),
+                                       v.transpose(1, 2).float(), enable_gqa=G > 1)
+    return o.transpose(1, 2)
+
+
+def make_triton_sparse(ops):
+    def triton_sparse(q, k, v, block_indices, block_size, softmax_scale=None):
+        B, N, Hq, D = q.shape
+        Hk = k.shape[2]
+        scale = D ** -0.5 if softmax_scale is None else softmax_scale
+        q, k, v = (t.float().contiguous() for t in (q, k, v))
+        idx = block_indices.contiguous()
+        out = torch.empty(B, N, Hq, D)
+        lse = torch.empty(B, N, Hq)
+        ops.mosaic_attn_fwd_kernel.fn[(N // 64, Hq // Hk, B * Hk)](
+            q, k, v, out, lse, idx, softmax_scale=scale, seq_len=N, num_kv_heads=Hk, num_q_heads=Hq,
+            q_heads_per_kv_head=Hq // Hk, feature_dim=D, kv_block_size=block_size,
+            num_kv_blocks_per_q_block=idx.shape[-1], q_tile_size=64)
+        triton_sparse.last_lse = lse
+        return out
+    return triton_sparse
+
+
+CONFIGS = {
+    # name: B, N, Hq, Hk, bs, K, bas, seed
+    "g1_n768_h4x1_bs64_k4": (1, 768, 4, 1, 64, 4, 256, 0),
+    "c1_n3072_h4x1_bs64_k8": (1, 3072, 4, 1, 64, 8, 1024, 1),
+    "g3_n3072_h8x2_bs128_k4": (1, 3072, 8, 2, 128, 4, 512, 2),
+}
+
+
+def main(ref_dir):
+    sys.path.insert(0, ROOT)
+    from oracle import bsa_oracle as O
+    ops, P = _import_reference(ref_dir)
+    triton_sparse = make_triton_sparse(ops)
+    P.flash_attn_func = sdpa_gqa
+    P.mosaic_sparse_attn = triton_sparse
+    real_topk = P.attn_topk
+
+    for name, (B, N, Hq, Hk, bs, K, bas, seed) in CONFIGS.items():
+        g = torch.Generator().manual_seed(seed)
+        q_raw = torch.randn(B, N, Hq, 64, generator=g).bfloat16()
+        k_raw = torch.randn(B, N, Hk, 64, generator=g).bfloat16()
+        v = torch.randn(B, N, Hk, 64, generator=g).bfloat16()
+        w = torch.sigmoid(torch.randn(3, B, N, Hq, 1, generator=g)).bfloat16()
+        nside = int(round((N / 12) ** 0.5))
+        rope = P.RoPE(64, 10000)
+        rope.initialize_rope(O.healpix_grid(nside))
+        q = rope(q_raw)  # bf16 out, like MosaicAttention.forward (primitives.py:193-195)
+        k = rope(k_raw)
+        # bf16 top-k, exactly as the reference computes it on bf16 activations
+        from einops import reduce
+        q_cmp = reduce(q, 'b (nb bs) h d -> b nb h d', 'mean', bs=bs)
+        k_cmp = reduce(k, 'b (nb bs) h d -> b nb h d', 'mean', bs=bs)
+        idx = real_topk(q_cmp, k_cmp, K)
+        # fp32 run of the orchestration on the same (bf16-valued) inputs, driven by that selection
+        P.attn_topk = lambda qc, kc, kk, _idx=idx: _idx
+        qf, kf, vf, wf = q.float(), k.float(), v.float(), w.float()
+        out = P.mosaic_attn_func(qf, kf, vf, wf, bas, bs, K, False, False)
+        o_ba = P.block_attention(qf, kf, vf, bas)
+        o_slc = triton_sparse(qf, kf, vf, idx, bs)
+        lse = triton_sparse.last_lse
+        qc, kc, vc = (reduce(t, 'b (nb bs) h d -> b nb h d', 'mean', bs=bs) for t in (qf, kf, vf))
+        o_cmp = sdpa_gqa(qc, kc, vc)
+        out_nocmp = P.mosaic_attn_func(qf, kf, vf, wf, bas, bs, K, False, True)
+        out_k0 = P.mosaic_attn_func(qf, kf, vf, wf, bas, bs, 0, False, False)
+        P.attn_topk = real_topk
+        rows = torch.sort(torch.randperm(N, generator=torch.Generator().manual_seed(100 + seed))[:64]).values
+        f16 = lambda t: t[:, rows].to(torch.float16).numpy()
+        sums = lambda t: t.double().sum(dim=(1, 3)).numpy()  # [B, Hq]
+        np.savez_compressed(
+            os.path.join(HERE, f"{name}.npz"),
+            meta=np.array([B, N, Hq, Hk, bs, K, bas, seed], dtype=np.int64),
+            rows=rows.numpy().astype(np.int32),
+            block_indices=idx.numpy().astype(np.int16),
+            q_rot_rows=f16(q.float()), k_rot_rows=f16(k.float()),
+            q_cmp=q_cmp.float().numpy().astype(np.float16), k_cmp=k_cmp.float().numpy().astype(np.float16),
+            o_cmp=o_cmp.numpy().astype(np.float16),
+            out_rows=f16(out), o_ba_rows=f16(o_ba), o_slc_rows=f16(o_slc),
+            lse_rows=lse[:, rows].numpy(),
+            out_nocmp_rows=f16(out_nocmp), out_k0_rows=f16(out_k0),
+            out_sums=sums(out), o_ba_sums=sums(o_ba), o_slc_sums=sums(o_slc),
+        )
+        print(name, "written")
+
+
+if __name__ == "__main__":
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOSAIC_REFERENCE_DIR", "")
+    if not ref or not os.path.isdir(ref):
+        raise SystemExit("usage: TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout>")
+    main(ref)

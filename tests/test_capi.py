@@ -1,0 +1,128 @@
+"""The C-ABI library: it loads without a GPU, exports every symbol that
+include/mosaic_b200.h declares, and rejects bad arguments on the host (before any
+CUDA call, so these run on a CPU-only machine)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from mosaic_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "mosaic_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(mosaic_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for n in ("mosaic_bsa_fwd", "mosaic_sparse_attn_fwd", "mosaic_block_attn_fwd", "mosaic_attn_topk",
+              "mosaic_block_pool", "mosaic_cmp_attn_fwd", "mosaic_bsa_workspace_bytes"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_abi_version_and_error_strings():
+    lib = _lib.load()
+    assert lib.mosaic_abi_version() == _lib.EXPECTED_ABI_VERSION
+    for code in range(5):
+        assert lib.mosaic_error_string(code)
+    assert b"unknown" in lib.mosaic_error_string(99)
+
+
+def test_struct_layout_matches_header():
+    # the Python mirror must have the header's field order
+    src = open(HEADER).read()
+    body = src[src.index("typedef struct MosaicBsaArgs"): src.index("} MosaicBsaArgs;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = re.findall(r"\b(\w+);", body)
+    assert [f for f, _ in _lib.MosaicBsaArgs._fields_] == fields
+
+
+def test_workspace_size():
+    lib = _lib.load()
+    b = lib.mosaic_bsa_workspace_bytes(1, 49152, 12, 3, 64, 64, 24, 0)
+    nb = 49152 // 64
+    expect = nb * 12 * 128 * 2 + nb * 3 * 128 * 2 + nb * 3 * 24 * 8
+    assert expect <= b <= expect + 5 * 256
+    assert lib.mosaic_bsa_workspace_bytes(1, 49152, 12, 3, 64, 64, 24, 1) > b + 49152 * 15 * 128 - 1
+
+
+FAKE = ctypes.c_void_p(0x10000)  # 16-byte aligned, never dereferenced: validation fails first
+
+
+def _sparse(**kw):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, idx=FAKE, out=FAKE, lse=None, status=None, B=1, N=1024, Hq=8, Hk=2, D=64,
+             bs=64, K=4, scale=0.0)
+    a.update(kw)
+    return _lib.load().mosaic_sparse_attn_fwd(a["q"], a["k"], a["v"], a["idx"], a["out"], a["lse"], a["status"],
+                                             a["B"], a["N"], a["Hq"], a["Hk"], a["D"], a["bs"], a["K"],
+                                             a["scale"], None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(idx=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(k=ctypes.c_void_p(0x10008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # misaligned
+    (dict(D=128), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(Hq=6, Hk=2), _lib.MOSAIC_ERR_UNSUPPORTED),          # G = 3
+    (dict(Hq=7, Hk=2), _lib.MOSAIC_ERR_INVALID_ARGUMENT),     # not a multiple
+    (dict(bs=32), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(N=1000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),         # N % bs
+    (dict(K=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(B=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+])
+def test_sparse_attn_rejects_bad_arguments(kw, code):
+    assert _sparse(**kw) == code
+
+
+def test_empty_inputs_are_a_no_op():
+    assert _sparse(B=0) == _lib.MOSAIC_OK
+    assert _sparse(N=0) == _lib.MOSAIC_OK
+
+
+def _bsa(**kw):
+    a = _lib.MosaicBsaArgs()
+    a.q = a.k = a.v = a.gates = a.out = 0x10000
+    a.workspace, a.workspace_bytes = 0x20000, 1 << 40
+    a.batch, a.seq_len, a.num_q_heads, a.num_kv_heads, a.head_dim = 1, 3072, 4, 1, 64
+    a.block_attn_size, a.sparse_block_size, a.sparse_block_count = 1024, 64, 8
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return _lib.load().mosaic_bsa_fwd(ctypes.byref(a), None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(gates=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(block_attn_size=1000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),     # N % bas
+    (dict(sparse_block_count=49), _lib.MOSAIC_ERR_INVALID_ARGUMENT),    # K > nb
+    (dict(sparse_block_count=0, no_compression=1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(workspace=None), _lib.MOSAIC_ERR_WORKSPACE),
+    (dict(workspace_bytes=16), _lib.MOSAIC_ERR_WORKSPACE),
+    (dict(rope_cos=0x10000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),         # cos without sin
+    (dict(head_dim=32), _lib.MOSAIC_ERR_UNSUPPORTED),
+])
+def test_bsa_rejects_bad_arguments(kw, code):
+    assert _bsa(**kw) == code
+
+
+def test_bsa_null_args():
+    assert _lib.load().mosaic_bsa_fwd(None, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+
+
+def test_topk_rejects_bad_arguments():
+    lib = _lib.load()
+    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 49, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 129, None) != _lib.MOSAIC_OK
+    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 0, None) == _lib.MOSAIC_OK

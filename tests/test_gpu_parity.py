@@ -1,0 +1,285 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle and the golden
+fixtures of the reference. Tolerances: bf16 outputs within
+max-abs 2e-2 / mean-abs 2e-3 of the fp32 reference; pooled tensors and rotated
+q/k bit-exact; top-k indices exact except inside score ties (1e-3 relative)."""
+import pytest
+import torch
+
+import mosaic_b200 as M
+from mosaic_b200 import ops as mops
+from oracle import bsa_oracle as O
+from tests import golden_util as GU
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+DEV = "cuda"
+
+
+def close(got, ref, max_abs=MAX_ABS, mean_abs=MEAN_ABS):
+    d = (got.float().cpu() - ref.float().cpu()).abs()
+    assert torch.isfinite(got.float()).all(), "non-finite output"
+    assert d.max().item() <= max_abs and d.mean().item() <= mean_abs, (d.max().item(), d.mean().item())
+
+
+def cuda(*ts):
+    return [t.to(DEV) if t is not None else None for t in ts]
+
+
+def run_checked(fn, *args, **kw):
+    status = mops.status_buffer(DEV)
+    out = fn(*args, status=status, **kw)
+    torch.cuda.synchronize()
+    assert mops.check_status(status) == 0
+    return out
+
+
+# ----------------------------------------------------------------------------- (a) pool + RoPE
+@pytest.mark.parametrize("cfg", [(1, 768, 4, 1, 64), (2, 3072, 8, 2, 128), (1, 12288, 16, 4, 64),
+                                 (1, 3072, 20, 5, 64)])
+def test_pool_bit_exact(cfg):
+    B, N, Hq, Hk, bs = cfg
+    x = O.make_inputs(B, N, Hq, Hk, seed=3, rope=False)
+    q, k, v = cuda(x["q"], x["k"], x["v"])
+    qc, kc, vc = M.block_pool(q, k, v, bs)
+    assert torch.equal(qc.cpu(), O.pool_mean(x["q"], bs))
+    assert torch.equal(kc.cpu(), O.pool_mean(x["k"], bs))
+    assert torch.equal(vc.cpu(), O.pool_mean(x["v"], bs))
+
+
+@pytest.mark.parametrize("cfg", [(1, 768, 4, 1, 64), (1, 3072, 12, 3, 128)])
+def test_rope_pool_bit_exact(cfg):
+    B, N, Hq, Hk, bs = cfg
+    x = O.make_inputs(B, N, Hq, Hk, seed=4, rope=True)
+    q, k, v, cos, sin = cuda(x["q_raw"], x["k_raw"], x["v"], x["cos"], x["sin"])
+    qc, kc, vc, q_rot, k_rot = M.block_pool(q, k, v, bs, rope_tables=(cos, sin))
+    assert torch.equal(q_rot.cpu(), x["q"]) and torch.equal(k_rot.cpu(), x["k"])
+    assert torch.equal(qc.cpu(), O.pool_mean(x["q"], bs))
+    assert torch.equal(kc.cpu(), O.pool_mean(x["k"], bs))
+
+
+# ----------------------------------------------------------------------------- (b) top-k
+@pytest.mark.parametrize("cfg", [(1, 48, 4, 1, 8), (2, 192, 16, 4, 20), (1, 768, 12, 3, 24), (1, 1536, 8, 2, 64),
+                                 (1, 3072, 12, 3, 24)])
+def test_topk_matches_oracle(cfg):
+    B, nb, Hq, Hk, K = cfg
+    g = torch.Generator().manual_seed(nb)
+    qc = torch.randn(B, nb, Hq, 64, generator=g).bfloat16() * 0.3
+    kc = torch.randn(B, nb, Hk, 64, generator=g).bfloat16() * 0.3
+    idx = M.attn_topk(*cuda(qc, kc), K).cpu()
+    ref = O.attn_topk(qc, kc, K)
+    ok, ndiff = O.topk_matches(idx, ref, O.topk_scores(qc, kc))
+    assert ok, f"{ndiff} rows differ beyond ties"
+    # sorted by score, descending
+    sc = torch.gather(O.topk_scores(qc, kc).float(), -1, idx)
+    assert (sc[..., :-1] >= sc[..., 1:]).all()
+
+
+def test_topk_ties_go_to_lower_index():
+    qc = torch.zeros(1, 64, 4, 64).bfloat16()
+    kc = torch.zeros(1, 64, 1, 64).bfloat16()  # every score is 0: one big tie
+    idx = M.attn_topk(*cuda(qc, kc), 8).cpu()
+    assert torch.equal(idx, torch.arange(8).expand(1, 64, 1, 8))
+
+
+@pytest.mark.parametrize("name", GU.fixture_names())
+def test_topk_matches_golden(name):
+    d = GU.load(name)
+    x = GU.inputs(d)
+    qc, kc = O.pool_mean(x["q"], d["bs"]), O.pool_mean(x["k"], d["bs"])
+    idx = M.attn_topk(*cuda(qc, kc), d["K"]).cpu()
+    ok, _ = O.topk_matches(idx, torch.from_numpy(d["block_indices"]).long(), O.topk_scores(qc, kc))
+    assert ok
+
+
+# ----------------------------------------------------------------------------- coarse + local attention
+@pytest.mark.parametrize("cfg", [(1, 48, 4, 1), (1, 24, 20, 5), (2, 192, 16, 4), (1, 768, 12, 3), (1, 100, 8, 2)])
+def test_cmp_attention(cfg):
+    B, nb, Hq, Hk = cfg
+    x = O.make_inputs(B, nb, Hq, Hk, seed=5, rope=False)
+    got = run_checked(M.cmp_attention, *cuda(x["q"], x["k"], x["v"]))
+    close(got, O.dense_attention(x["q"], x["k"], x["v"]))
+
+
+@pytest.mark.parametrize("cfg", [(1, 3072, 4, 1, 1024), (2, 2048, 8, 2, 256), (1, 1024, 12, 3, 64),
+                                 (1, 768, 4, 1, 768), (1, 3840, 12, 3, 192)])
+def test_block_attention(cfg):
+    B, N, Hq, Hk, bas = cfg
+    x = O.make_inputs(B, N, Hq, Hk, seed=6, rope=False)
+    got = run_checked(M.block_attention, *cuda(x["q"], x["k"], x["v"]), bas)
+    close(got, O.block_attention(x["q"], x["k"], x["v"], bas))
+
+
+# ----------------------------------------------------------------------------- (c) selected-block attention
+def random_indices(B, nb, Hk, K, seed, duplicates=False):
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.stack([torch.randperm(nb, generator=g)[:K] for _ in range(B * nb * Hk)]).reshape(B, nb, Hk, K)
+    if duplicates:
+        idx[..., -1] = idx[..., 0]
+    return idx
+
+
+@pytest.mark.parametrize("cfg", [(1, 768, 4, 1, 64, 4), (2, 1024, 8, 2, 128, 3), (1, 3072, 12, 3, 64, 24),
+                                 (1, 2048, 4, 1, 256, 2), (1, 1024, 4, 1, 64, 5), (1, 512, 4, 1, 64, 8)])
+def test_sparse_attention(cfg):
+    B, N, Hq, Hk, bs, K = cfg
+    x = O.make_inputs(B, N, Hq, Hk, seed=7, rope=False)
+    idx = random_indices(B, N // bs, Hk, K, seed=N + K)
+    status = mops.status_buffer(DEV)
+    out, lse = M.mosaic_sparse_attn_with_lse(*cuda(x["q"], x["k"], x["v"], idx), bs, status=status)
+    torch.cuda.synchronize()
+    assert mops.check_status(status) == 0
+    ref, rlse = O.sparse_attention(x["q"], x["k"], x["v"], idx, bs, return_lse=True)
+    close(out, ref)
+    assert (lse.cpu() - rlse).abs().max() < 3e-2
+    # the drop-in entry point gives the same bits
+    out2 = M.mosaic_sparse_attn(*cuda(x["q"], x["k"], x["v"], idx), bs)
+    assert torch.equal(out, out2)
+
+
+def test_sparse_attention_duplicates_and_dtype():
+    B, N, Hq, Hk, bs, K = 1, 1024, 4, 1, 64, 4
+    x = O.make_inputs(B, N, Hq, Hk, seed=8, rope=False)
+    idx = random_indices(B, N // bs, Hk, K, seed=1, duplicates=True)
+    out = M.mosaic_sparse_attn(*cuda(x["q"].float(), x["k"].float(), x["v"].float(), idx), bs)
+    assert out.dtype == torch.float32  # returned in q's dtype like ops.py:538
+    close(out, O.sparse_attention(x["q"], x["k"], x["v"], idx, bs))
+
+
+@pytest.mark.parametrize("name", GU.fixture_names())
+def test_sparse_attention_matches_golden(name):
+    d = GU.load(name)
+    x = GU.inputs(d)
+    rows = torch.from_numpy(d["rows"]).long()
+    idx = torch.from_numpy(d["block_indices"]).long()
+    out, lse = M.mosaic_sparse_attn_with_lse(*cuda(x["q"], x["k"], x["v"], idx), d["bs"])
+    close(out.cpu()[:, rows], GU.t(d["o_slc_rows"]))
+    assert (lse.cpu()[:, rows] - GU.t(d["lse_rows"])).abs().max() < 3e-2
+
+
+def test_bad_index_is_reported_not_faulted():
+    B, N, Hq, Hk, bs, K = 1, 512, 4, 1, 64, 2
+    x = O.make_inputs(B, N, Hq, Hk, seed=9, rope=False)
+    idx = random_indices(B, N // bs, Hk, K, seed=2)
+    idx[0, 3, 0, 1] = 10_000  # planted on the host: out of range
+    status = mops.status_buffer(DEV)
+    M.mosaic_sparse_attn_with_lse(*cuda(x["q"], x["k"], x["v"], idx), bs, status=status)
+    torch.cuda.synchronize()
+    assert status.item() & 2
+    with pytest.raises(RuntimeError):
+        mops.check_status(status)
+
+
+# ----------------------------------------------------------------------------- full op
+def full_check(x, bas, bs, K, block_attn_only=False, no_compression=False, rope=False):
+    q, k, v, w = cuda(x["q"], x["k"], x["v"], x["w"])
+    kw = {}
+    if rope:
+        q, k = cuda(x["q_raw"], x["k_raw"])
+        kw["rope_tables"] = tuple(cuda(x["cos"], x["sin"]))
+    status = mops.status_buffer(DEV)
+    res = M.mosaic_attn_func(q, k, v, w, bas, bs, K, block_attn_only, no_compression,
+                             return_block_indices=True, status=status, **kw)
+    torch.cuda.synchronize()
+    assert mops.check_status(status) == 0
+    out, idx = res
+    sel = None
+    if idx is not None:
+        idx = idx.cpu()
+        qc, kc = O.pool_mean(x["q"], bs), O.pool_mean(x["k"], bs)
+        ok, _ = O.topk_matches(idx, O.attn_topk(qc, kc, K), O.topk_scores(qc, kc))
+        assert ok
+        sel = idx
+    ref = O.mosaic_attn_func(x["q"], x["k"], x["v"], x["w"], bas, bs, K, block_attn_only, no_compression,
+                             block_indices=sel)
+    close(out, ref)
+    return out
+
+
+@pytest.mark.parametrize("cfg", [
+    (1, 768, 4, 1, 256, 64, 4),        # golden g1 shape
+    (1, 3072, 4, 1, 1024, 64, 8),      # BASELINE config 1 (C1)
+    (1, 3072, 20, 5, 1024, 64, 20),    # BN
+    (2, 3072, 8, 2, 512, 128, 4),      # reference-preset block size 128
+    (1, 12288, 16, 4, 1024, 64, 20),   # S2
+])
+def test_mosaic_attn_func(cfg):
+    B, N, Hq, Hk, bas, bs, K = cfg
+    x = O.make_inputs(B, N, Hq, Hk, seed=10 + N, rope=True)
+    full_check(x, bas, bs, K)
+
+
+@pytest.mark.parametrize("mode", ["block_attn_only", "no_compression", "k0"])
+def test_mosaic_attn_func_modes(mode):
+    x = O.make_inputs(1, 3072, 8, 2, seed=11, rope=True)
+    if mode == "block_attn_only":
+        full_check(x, 1024, 64, 8, block_attn_only=True)
+    elif mode == "no_compression":
+        full_check(x, 1024, 64, 8, no_compression=True)
+    else:
+        full_check(x, 1024, 64, 0)
+
+
+def test_fused_rope_equals_prerotated():
+    x = O.make_inputs(1, 3072, 12, 3, seed=12, rope=True)
+    a = full_check(x, 1024, 64, 8, rope=False)
+    b = full_check(x, 1024, 64, 8, rope=True)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("name", GU.fixture_names())
+def test_mosaic_attn_func_matches_golden(name):
+    d = GU.load(name)
+    x = GU.inputs(d)
+    rows = torch.from_numpy(d["rows"]).long()
+    out, idx = M.mosaic_attn_func(*cuda(x["q"], x["k"], x["v"], x["w"]), d["bas"], d["bs"], d["K"], False,
+                                  return_block_indices=True)
+    qc, kc = O.pool_mean(x["q"], d["bs"]), O.pool_mean(x["k"], d["bs"])
+    gold_idx = torch.from_numpy(d["block_indices"]).long()
+    ok, _ = O.topk_matches(idx.cpu(), gold_idx, O.topk_scores(qc, kc))
+    assert ok
+    if torch.equal(torch.sort(idx.cpu(), -1).values, torch.sort(gold_idx, -1).values):
+        close(out.cpu()[:, rows], GU.t(d["out_rows"]))
+    out_k0 = M.mosaic_attn_func(*cuda(x["q"], x["k"], x["v"], x["w"]), d["bas"], d["bs"], 0, False)
+    close(out_k0.cpu()[:, rows], GU.t(d["out_k0_rows"]))
+
+
+def test_stage1_full_size():
+    """BASELINE config 2 (S1): N=49152, 12/3 heads, bs 64, K 24, local window 1024."""
+    x = O.make_inputs(1, 49152, 12, 3, seed=0, rope=True)
+    full_check(x, 1024, 64, 24)
+
+
+def test_constant_values_property_full_size():
+    """Size-independent property at S1 and at Nside 128: with v constant per kv head
+    every branch returns that constant, so out = (w0 + w1 + w2) * c exactly up to bf16."""
+    for N in (49152, 196608):
+        B, Hq, Hk = 1, 12, 3
+        g = torch.Generator().manual_seed(N)
+        q = torch.randn(B, N, Hq, 64, generator=g).bfloat16()
+        k = torch.randn(B, N, Hk, 64, generator=g).bfloat16()
+        c = torch.tensor([0.5, -1.25, 2.0]).bfloat16()
+        v = c.view(1, 1, Hk, 1).expand(B, N, Hk, 64).contiguous()
+        w = torch.sigmoid(torch.randn(3, B, N, Hq, 1, generator=g)).bfloat16()
+        out = run_checked(M.mosaic_attn_func, *cuda(q, k, v, w), 1024, 64, 24, False).float().cpu()
+        expect = (w.float().sum(0)[..., 0].unsqueeze(-1) * c.float().repeat_interleave(4).view(1, 1, Hq, 1))
+        assert (out - expect).abs().max() < 2e-2
+
+
+def test_empty_batch():
+    q = torch.empty(0, 768, 4, 64, dtype=torch.bfloat16, device=DEV)
+    k = torch.empty(0, 768, 1, 64, dtype=torch.bfloat16, device=DEV)
+    w = torch.empty(3, 0, 768, 4, 1, dtype=torch.bfloat16, device=DEV)
+    out = M.mosaic_attn_func(q, k, k, w, 256, 64, 4, False)
+    assert out.shape == (0, 768, 4, 64)
+
+
+def test_host_errors_raise():
+    x = O.make_inputs(1, 768, 4, 1, seed=13, rope=False)
+    q, k, v, w = cuda(x["q"], x["k"], x["v"], x["w"])
+    with pytest.raises(ValueError):
+        M.mosaic_attn_func(q, k, v, w, 256, 64, 13, False)       # K > nb
+    with pytest.raises(RuntimeError):
+        M.mosaic_attn_func(q, k, v, w, 100, 64, 4, False)        # N % bas
+    with pytest.raises(ValueError):
+        M.mosaic_sparse_attn(x["q"], x["k"], x["v"], torch.zeros(1, 12, 1, 2, dtype=torch.long), 64)  # CPU

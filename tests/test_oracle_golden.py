@@ -1,0 +1,93 @@
+"""The CPU oracle against fixtures produced by running the reference code itself
+(tests/golden/make_golden.py). This pins the oracle before it is trusted as the
+checker of the CUDA path."""
+import pytest
+import torch
+
+from oracle import bsa_oracle as O
+from tests import golden_util as GU
+
+NAMES = GU.fixture_names()
+
+
+def test_fixtures_present():
+    assert len(NAMES) >= 3
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_rope_and_pool_bit_exact(name):
+    d = GU.load(name)
+    x = GU.inputs(d)
+    rows = torch.from_numpy(d["rows"]).long()
+    # RoPE.forward of the reference == oracle.rope_apply, bit for bit (bf16 -> fp16 storage is exact here)
+    assert torch.equal(x["q"][:, rows].float().half().float(), GU.t(d["q_rot_rows"]))
+    assert torch.equal(x["k"][:, rows].float().half().float(), GU.t(d["k_rot_rows"]))
+    # reference einops mean-pool == oracle.pool_mean
+    assert torch.equal(O.pool_mean(x["q"], d["bs"]).float(), GU.t(d["q_cmp"]))
+    assert torch.equal(O.pool_mean(x["k"], d["bs"]).float(), GU.t(d["k_cmp"]))
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_topk_matches_reference(name):
+    d = GU.load(name)
+    x = GU.inputs(d)
+    qc, kc = O.pool_mean(x["q"], d["bs"]), O.pool_mean(x["k"], d["bs"])
+    idx = O.attn_topk(qc, kc, d["K"])
+    ref = torch.from_numpy(d["block_indices"]).long()
+    ok, ndiff = O.topk_matches(idx, ref, O.topk_scores(qc, kc))
+    assert ok, f"{ndiff} rows differ beyond score ties"
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_branches_and_combine_match_reference(name):
+    d = GU.load(name)
+    x = GU.inputs(d)
+    rows = torch.from_numpy(d["rows"]).long()
+    idx = torch.from_numpy(d["block_indices"]).long()
+    parts = {}
+    out = O.mosaic_attn_func(x["q"], x["k"], x["v"], x["w"], d["bas"], d["bs"], d["K"], False,
+                             block_indices=idx, parts=parts)
+    # fp32 vs fp32 (fp16 storage) for the dense branches
+    torch.testing.assert_close(parts["o_ba"][:, rows], GU.t(d["o_ba_rows"]), atol=2e-3, rtol=2e-3)
+    o_cmp_small = O.dense_attention(O.pool_mean(x["q"], d["bs"]), O.pool_mean(x["k"], d["bs"]),
+                                    O.pool_mean(x["v"], d["bs"]))
+    torch.testing.assert_close(o_cmp_small, GU.t(d["o_cmp"]), atol=2e-3, rtol=2e-3)
+    # the reference sparse branch is the Triton kernel, which rounds q*scale*log2e and P to bf16
+    diff = (parts["o_slc"][:, rows] - GU.t(d["o_slc_rows"])).abs()
+    assert diff.max() < 2e-2 and diff.mean() < 2e-3, (diff.max(), diff.mean())
+    diff = (out[:, rows] - GU.t(d["out_rows"])).abs()
+    assert diff.max() < 2e-2 and diff.mean() < 2e-3, (diff.max(), diff.mean())
+    # whole-tensor sums (fp64) of the reference outputs
+    for key, val in (("out_sums", out), ("o_ba_sums", parts["o_ba"]), ("o_slc_sums", parts["o_slc"])):
+        s = val.double().sum(dim=(1, 3))
+        torch.testing.assert_close(s, torch.from_numpy(d[key]), atol=0.05 * d["N"] ** 0.5, rtol=1e-3)
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_sparse_lse_and_modes_match_reference(name):
+    d = GU.load(name)
+    x = GU.inputs(d)
+    rows = torch.from_numpy(d["rows"]).long()
+    idx = torch.from_numpy(d["block_indices"]).long()
+    _, lse = O.sparse_attention(x["q"], x["k"], x["v"], idx, d["bs"], return_lse=True)
+    assert (lse[:, rows] - GU.t(d["lse_rows"])).abs().max() < 3e-2
+    out_nocmp = O.mosaic_attn_func(x["q"], x["k"], x["v"], x["w"], d["bas"], d["bs"], d["K"], False, True,
+                                   block_indices=idx)
+    diff = (out_nocmp[:, rows] - GU.t(d["out_nocmp_rows"])).abs()
+    assert diff.max() < 2e-2 and diff.mean() < 2e-3
+    out_k0 = O.mosaic_attn_func(x["q"], x["k"], x["v"], x["w"], d["bas"], d["bs"], 0, False)
+    torch.testing.assert_close(out_k0[:, rows], GU.t(d["out_k0_rows"]), atol=2e-3, rtol=2e-3)
+
+
+def test_topk_checker_rejects_wrong_selection():
+    # a mistake planted in the oracle's output must be caught by the parity checker
+    d = GU.load(NAMES[0])
+    x = GU.inputs(d)
+    qc, kc = O.pool_mean(x["q"], d["bs"]), O.pool_mean(x["k"], d["bs"])
+    sc = O.topk_scores(qc, kc)
+    idx = O.attn_topk(qc, kc, d["K"])
+    bad = idx.clone()
+    worst = sc.float().argmin(dim=-1)
+    bad[..., -1] = worst
+    ok, _ = O.topk_matches(bad, idx, sc)
+    assert not ok
