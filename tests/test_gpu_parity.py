@@ -70,9 +70,9 @@ def test_topk_matches_oracle(cfg):
     ref = O.attn_topk(qc, kc, K)
     ok, ndiff = O.topk_matches(idx, ref, O.topk_scores(qc, kc))
     assert ok, f"{ndiff} rows differ beyond ties"
-    # sorted by score, descending
+    # sorted by score, descending (scores recomputed on the CPU may differ by one bf16 ulp)
     sc = torch.gather(O.topk_scores(qc, kc).float(), -1, idx)
-    assert (sc[..., :-1] >= sc[..., 1:]).all()
+    assert (sc[..., 1:] - sc[..., :-1] <= 2 ** -7 * sc[..., :-1].abs() + 1e-6).all()
 
 
 def test_topk_ties_go_to_lower_index():
