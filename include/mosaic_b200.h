@@ -83,6 +83,18 @@ MOSAIC_API size_t mosaic_bsa_workspace_bytes(int batch, int seq_len, int num_q_h
  * (ops.py:557-566) it makes. */
 MOSAIC_API int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream);
 
+/* mosaic_bsa_fwd for callers that cannot allocate device memory (a foreign-language
+ * host with no device allocator, or a service with a fixed memory budget that must
+ * not call cudaMalloc/cudaFree per request). It has no counterpart in the reference.
+ * args->workspace / workspace_bytes are ignored: the scratch is an 8 MiB array
+ * compiled into the library (held on every device that loads it until exit), so
+ * calls needing more than 8 MiB of scratch (mosaic_bsa_workspace_bytes) return
+ * MOSAIC_ERR_WORKSPACE, and fused RoPE (rope_cos/rope_sin) returns
+ * MOSAIC_ERR_UNSUPPORTED. The first call on a device looks up the array's address;
+ * make it before any stream capture. All calls on a device share the array: calls
+ * that overlap on the GPU race and must be serialised by the caller. */
+MOSAIC_API int mosaic_bsa_fwd_noalloc(const MosaicBsaArgs* args, void* stream);
+
 /* The fused attention stage of mosaic_bsa_fwd on its own: local-window attention
  * + selected-block attention over the given block_indices + the gated combine
  * with the coarse-attention rows o_cmp ([B, N/bs, Hq, 64] bf16, NULL when

@@ -42,6 +42,7 @@ SIGNATURES = {
     "mosaic_error_string": ([_i], ctypes.c_char_p),
     "mosaic_bsa_workspace_bytes": ([_i, _i, _i, _i, _i, _i, _i, _i], _sz),
     "mosaic_bsa_fwd": ([ctypes.POINTER(MosaicBsaArgs), _vp], _i),
+    "mosaic_bsa_fwd_noalloc": ([ctypes.POINTER(MosaicBsaArgs), _vp], _i),
     "mosaic_bsa_attend_fwd": ([_vp] * 8 + [_i] * 9 + [_f, _vp], _i),
     "mosaic_sparse_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp], _i),
     "mosaic_block_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp], _i),
