@@ -4,7 +4,7 @@
 // of that kv group. The four heads are packed into two M = 128 MMA tiles
 // ("M-tiles": rows 0-63 = head 4h+2m, rows 64-127 = head 4h+2m+1), so every K/V
 // tile that TMA brings into shared memory is used by 4 heads x 64 queries.
-// Keys stream in tiles of 128 (two 64-row TMA boxes):
+// Keys stream in tiles of 64 (one TMA box each for K and V, 8-stage ring):
 //   * local branch   (primitives.block_attention, primitives.py:28-32): the
 //     window [w*win, (w+1)*win) that contains the query tile;
 //   * selected branch (ops.mosaic_attn_fwd_kernel, ops.py:94-128): the 64-row
@@ -15,15 +15,21 @@
 // coarse-attention row o_cmp[b, n/bs, head] (the repeat_interleave of
 // primitives.py:78 becomes an index).
 //
-// Warp roles (320 threads): warp 0 issues TMA, warp 1 issues tcgen05.mma (one
-// thread) and owns the TMEM allocation, warps 2-5 run the softmax + epilogue of
-// M-tile 0 and warps 6-9 those of M-tile 1. The two M-tiles ping-pong on the
-// tensor core: while one softmax warpgroup turns S into P, the MMA warp runs
-// the other M-tile's P*V and Q*K^T.
+// Warp roles (384 threads): warp 0 issues TMA, warps 1 and 2 issue the
+// tcgen05.mma of M-tile 0 and 1 (converged warps, one elected lane; warp 1 also
+// owns the TMEM allocation), warp 3 idles, warps 4-7 run the softmax + epilogue
+// of M-tile 0 and warps 8-11 those of M-tile 1.
 //
-// TMEM (512 columns, fp32): S/P of M-tile m at [128m, 128m+128) (P overwrites the
-// first 64 columns of S as packed bf16 pairs), O_local of M-tile m at
-// 256+128m, O_selected at 320+128m.
+// Pipeline: S is double-buffered per M-tile, so Q*K^T of tile t+2 is issued as
+// soon as P*V of tile t has been issued, and a softmax warpgroup never waits for
+// the tensor core between tiles; the two M-tiles interleave on the tensor core.
+// The softmax splits its exponentials between MUFU (ex2.approx) and a software
+// exp2 on the FMA pipe, because at head_dim 64 the MUFU rate, not the tensor
+// core, is the first limit.
+//
+// TMEM (512 columns, fp32): S/P buffer b of M-tile m at 64*(2m+b) (P overwrites
+// the first 32 columns of its S buffer as packed bf16 pairs and feeds P*V from
+// TMEM), O_local of M-tile m at 256+128m, O_selected at 320+128m.
 #include <cmath>
 #include <cstring>
 
@@ -31,16 +37,38 @@
 #include "ptx.cuh"
 
 namespace mosaic {
+
+#ifdef MOSAIC_TRACE
+// Development timeline (off in the library build): clock64() stamps of one CTA's
+// pipeline events, read back by a tracing build's host code.
+__device__ long long g_engine_trace[4096];
+#define MOSAIC_TRACE_AT(cond, slot) \
+  do {                              \
+    if (cond) g_engine_trace[(slot)] = clock64(); \
+  } while (0)
+#else
+#define MOSAIC_TRACE_AT(cond, slot) \
+  do {                              \
+    (void)(cond);                   \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int kQTile = 64;
-constexpr int kStages = 4;
-constexpr int kSegBytes = 64 * 128;       // one 64-row x 64-col bf16 box
-constexpr int kTileBytes = 2 * kSegBytes;  // 128 rows
-constexpr int kThreads = 320;
+constexpr int kStages = 8;
+constexpr int kBoxBytes = 64 * 128;        // one 64-row x 64-col bf16 box (8 KB)
+constexpr int kQTileBytes = 2 * kBoxBytes;  // one M-tile of Q: 128 rows
+constexpr int kThreads = 384;
 constexpr int kMaxSel = 1024;  // max selected blocks per query block
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: keep a stale max while p <= 2^8
-
+// Of every kPolyDen pairs of scores, the last kPolyNum take the software exp2
+// (FMA pipe) and the others ex2.approx (MUFU), so both pipes share the work.
+#ifndef MOSAIC_POLY_NUM
+#define MOSAIC_POLY_NUM 3
+#endif
+constexpr int kPolyDen = 8;
+constexpr int kPolyNum = MOSAIC_POLY_NUM;
 struct EngineParams {
   CUtensorMap tm_q, tm_k, tm_v;
   const int64_t* block_idx;
@@ -59,68 +87,78 @@ struct EngineSmem {
   uint64_t q_full;
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t s_full[2][2];  // [M-tile][S buffer]
+  // [M-tile][S buffer]: one per buffer, because a softmax warpgroup may finish
+  // tiles t and t+1 before the MMA warp consumes P(t); it can never get two tiles
+  // ahead on the same buffer (S(t+2) is issued only after P(t)*V(t)).
+  uint64_t p_full[2][2];
+  uint64_t o_done[2];
   uint64_t o_final[2];
-  uint64_t drain;
+  uint64_t drain[2];
   uint32_t tmem_base;
   int abort_flag;
   int sel[kMaxSel];
 };
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + 2 * kStages * kTileBytes + sizeof(EngineSmem);
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kQTileBytes + 2 * kStages * kBoxBytes + sizeof(EngineSmem);
 
-// Geometry of key tile t (shared by the producer, the MMA issuer and the softmax).
+// TMEM columns (fp32, 128 lanes): S/P buffer b of M-tile m at 64*(2m+b);
+// O_local of M-tile m at 256+128m, O_selected at 320+128m.
+__device__ __forceinline__ uint32_t col_s(int m, int b) { return 64u * (2 * m + b); }
+__device__ __forceinline__ uint32_t col_ol(int m) { return 256u + 128u * m; }
+__device__ __forceinline__ uint32_t col_os(int m) { return 320u + 128u * m; }
+
+// Key tile t = 64 keys: local-window tiles first, then one tile per 64-row
+// segment of the selected blocks (block size is a multiple of 64).
 struct KeyTile {
-  int nseg;   // 1 or 2 boxes of 64 keys
-  int valid;  // keys in the tile that take part (<= 64*nseg)
-  int row0, row1;  // key rows (within the batch) of the two boxes
+  int row;    // first key row within the batch
+  int valid;  // keys of the tile that take part (< 64 only at the end of a short window)
 };
 
 __device__ __forceinline__ KeyTile key_tile(const EngineParams& p, const int* sel, int t, int T_loc, int wstart,
                                             int wend) {
   KeyTile kt;
   if (t < T_loc) {
-    const int start = wstart + t * 128;
-    kt.valid = min(128, wend - start);
-    kt.row0 = start;
-    kt.row1 = start + 64;
+    kt.row = wstart + 64 * t;
+    kt.valid = min(64, wend - kt.row);
   } else {
-    const int pos = (t - T_loc) * 128;
-    const int total = p.K * p.bs;
-    kt.valid = min(128, total - pos);
-    kt.row0 = sel[pos / p.bs] * p.bs + pos % p.bs;
-    const int pos1 = pos + 64;
-    kt.row1 = pos1 < total ? sel[pos1 / p.bs] * p.bs + pos1 % p.bs : 0;
+    const int pos = (t - T_loc) * 64;
+    kt.row = sel[pos / p.bs] * p.bs + pos % p.bs;
+    kt.valid = 64;
   }
-  kt.nseg = kt.valid > 64 ? 2 : 1;
   return kt;
 }
 
-// Online-softmax step for one 128-row S tile held in TMEM: each thread owns one
-// row. Reads NK scores, updates (m_run, l_run), rescales this row's O accumulator
-// when the running max grows by more than kRescaleThreshold, and writes
-// P = exp2(S*c - m) as packed bf16 pairs over the first NK/2 columns of S.
-template <int NK>
-__device__ __forceinline__ void softmax_tile(uint32_t tS, uint32_t tO, int valid, bool first, float c,
-                                             float& m_run, float& l_run) {
-  uint32_t s[NK];
-#pragma unroll
-  for (int i = 0; i < NK / 32; ++i) tmem_ld32(tS + 32 * i, s + 32 * i);
+// Online-softmax step of one 64-key tile; each thread owns one row of the M-tile.
+// Reads the 64 scores from TMEM, updates (m_run, l_run), rescales this row's O
+// accumulator when the running max grows by more than kRescaleThreshold (after
+// waiting for the previous P*V on `o_done`), and writes P = 2^(S*c - m) as 32
+// packed bf16 pairs over the first 32 columns of the S buffer.
+__device__ __forceinline__ bool softmax_tile(uint32_t tS, uint32_t tO, int valid, bool first, float c,
+                                             float& m_run, float& l_run, uint64_t* o_done, uint32_t o_parity,
+                                             volatile int* abort_flag, int* status, int tslot) {
+  uint32_t s[64];
+  tmem_ld32(tS, s);
+  tmem_ld32(tS + 32, s + 32);
   tmem_ld_wait();
-  reg_fence<NK>(s);
-  if (valid < NK) {
+  reg_fence<64>(s);
+  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 0);
+  if (valid < 64) {
 #pragma unroll
-    for (int i = 0; i < NK; ++i)
+    for (int i = 0; i < 64; ++i)
       if (i >= valid) s[i] = __float_as_uint(-INFINITY);
   }
-  float mx0 = __uint_as_float(s[0]), mx1 = __uint_as_float(s[1]);
+  float mx[8];
 #pragma unroll
-  for (int i = 2; i < NK; i += 2) {
-    mx0 = fmaxf(mx0, __uint_as_float(s[i]));
-    mx1 = fmaxf(mx1, __uint_as_float(s[i + 1]));
+  for (int j = 0; j < 8; ++j) {
+    float a = fmax3(__uint_as_float(s[j]), __uint_as_float(s[j + 8]), __uint_as_float(s[j + 16]));
+    a = fmax3(a, __uint_as_float(s[j + 24]), __uint_as_float(s[j + 32]));
+    a = fmax3(a, __uint_as_float(s[j + 40]), __uint_as_float(s[j + 48]));
+    mx[j] = fmaxf(a, __uint_as_float(s[j + 56]));
   }
-  const float m_new = fmaxf(m_run, fmaxf(mx0, mx1) * c);
+  const float rmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7])));
+  const float m_new = fmaxf(m_run, rmax * c);
+  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 1);
   float m_use = m_run, alpha = 1.0f;
   bool need = false;
   if (first) {
@@ -130,8 +168,11 @@ __device__ __forceinline__ void softmax_tile(uint32_t tS, uint32_t tO, int valid
     m_use = m_new;
     alpha = ex2_approx(m_run - m_new);
   }
+  bool ok = true;
   if (__any_sync(0xffffffffu, need)) {
-    // Rare path; 8 columns at a time so that the 128 live scores do not spill.
+    // Rare path: the previous P*V must have landed in O before O is scaled.
+    ok = bounded_wait(o_done, o_parity, abort_flag, status);
+    tc_fence_after();
 #pragma unroll 1
     for (int c8 = 0; c8 < 64; c8 += 8) {
       uint32_t o[8];
@@ -144,22 +185,36 @@ __device__ __forceinline__ void softmax_tile(uint32_t tS, uint32_t tO, int valid
     }
   }
   l_run *= alpha;
-  const float nm = -m_use;
-  float sum0 = 0.f, sum1 = 0.f;
+  const uint64_t c2 = f2_pack(c, c);
+  const uint64_t nm2 = f2_pack(-m_use, -m_use);
+  uint64_t acc[4] = {0, 0, 0, 0};
   // P pairs are packed in place over the scores they came from (s[i] <- s[2i], s[2i+1]).
 #pragma unroll
-  for (int i = 0; i < NK / 2; ++i) {
-    const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * i]), c, nm));
-    const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * i + 1]), c, nm));
-    sum0 += p0;
-    sum1 += p1;
-    s[i] = pack_bf16x2(p0, p1);
+  for (int i = 0; i < 32; ++i) {
+    const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nm2);
+    uint64_t e;
+    if ((i % kPolyDen) >= kPolyDen - kPolyNum) {
+      e = exp2_poly2(x);
+    } else {
+      float x0, x1;
+      f2_unpack(x, x0, x1);
+      e = f2_pack(ex2_approx(x0), ex2_approx(x1));
+    }
+    acc[i & 3] = f2_add(acc[i & 3], e);
+    float e0, e1;
+    f2_unpack(e, e0, e1);
+    s[i] = pack_bf16x2(e0, e1);
   }
-#pragma unroll
-  for (int h = 0; h < NK / 64; ++h) tmem_st32(tS + 32 * h, s + 32 * h);
+  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 2);
+  tmem_st32(tS, s);
+  float a0, a1, b0, b1;
+  f2_unpack(f2_add(acc[0], acc[1]), a0, a1);
+  f2_unpack(f2_add(acc[2], acc[3]), b0, b1);
   tmem_st_wait();
-  l_run += sum0 + sum1;
+  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 3);
+  l_run += (a0 + a1) + (b0 + b1);
   m_run = m_use;
+  return ok;
 }
 
 __device__ __forceinline__ bool wait_noabort(uint64_t* bar, uint32_t parity, int* status) {
@@ -171,37 +226,42 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = tiles;
-  uint8_t* sK = tiles + 2 * kTileBytes;
-  uint8_t* sV = sK + kStages * kTileBytes;
-  EngineSmem& sm = *reinterpret_cast<EngineSmem*>(sV + kStages * kTileBytes);
+  uint8_t* sK = tiles + 2 * kQTileBytes;
+  uint8_t* sV = sK + kStages * kBoxBytes;
+  EngineSmem& sm = *reinterpret_cast<EngineSmem*>(sV + kStages * kBoxBytes);
   volatile int* abort_flag = &sm.abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int n0 = qt * kQTile;
+  const bool traced = blockIdx.x == 5 && blockIdx.y == 1 && blockIdx.z == 0;
+  MOSAIC_TRACE_AT(traced && threadIdx.x == 0, 2000);
   const int G = p.Hq / p.Hk;
 
   int T_loc = 0, wstart = 0, wend = 0;
   if (p.win > 0) {
     wstart = (n0 / p.win) * p.win;
     wend = min(wstart + p.win, p.Nk);
-    T_loc = (wend - wstart + 127) / 128;
+    T_loc = (wend - wstart + 63) / 64;
   }
-  const int T_slc = p.K > 0 ? (p.K * p.bs + 127) / 128 : 0;
+  const int T_slc = p.K > 0 ? (p.K * p.bs) / 64 : 0;
   const int T = T_loc + T_slc;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.kv_empty[s], 2);  // released by both MMA warps
     }
     for (int m = 0; m < 2; ++m) {
-      mbar_init(&sm.s_full[m], 1);
-      mbar_init(&sm.p_full[m], 128);
+      mbar_init(&sm.s_full[m][0], 1);
+      mbar_init(&sm.s_full[m][1], 1);
+      mbar_init(&sm.p_full[m][0], 128);
+      mbar_init(&sm.p_full[m][1], 128);
+      mbar_init(&sm.o_done[m], 1);
       mbar_init(&sm.o_final[m], 1);
+      mbar_init(&sm.drain[m], 1);
     }
-    mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
     fence_mbar_init();
   }
@@ -229,33 +289,29 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (converged warp)
     if (lane == 0) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
-      mbar_arrive_expect_tx(&sm.q_full, 4 * kSegBytes);
-      for (int m = 0; m < 2; ++m)
-        for (int u = 0; u < 2; ++u)
-          tma_load_2d(sQ + m * kTileBytes + u * kSegBytes, &p.tm_q, &sm.q_full, (h * G + 2 * m + u) * 64,
-                      b * p.Nq + n0);
-      int issued = 0;
-      for (int t = 0; t < T; ++t) {
-        const int st = t % kStages, r = t / kStages;
-        if (r > 0 && !bounded_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) break;
-        const KeyTile kt = key_tile(p, sm.sel, t, T_loc, wstart, wend);
-        mbar_arrive_expect_tx(&sm.kv_full[st], kt.nseg * 2 * kSegBytes);
-        uint8_t* dk = sK + st * kTileBytes;
-        uint8_t* dv = sV + st * kTileBytes;
-        tma_load_2d(dk, &p.tm_k, &sm.kv_full[st], h * 64, b * p.Nk + kt.row0);
-        tma_load_2d(dv, &p.tm_v, &sm.kv_full[st], h * 64, b * p.Nk + kt.row0);
-        if (kt.nseg == 2) {
-          tma_load_2d(dk + kSegBytes, &p.tm_k, &sm.kv_full[st], h * 64, b * p.Nk + kt.row1);
-          tma_load_2d(dv + kSegBytes, &p.tm_v, &sm.kv_full[st], h * 64, b * p.Nk + kt.row1);
-        }
-        issued = t + 1;
-      }
-      // Drain: every TMA write into shared memory must land before the CTA exits.
+    }
+    mbar_arrive_expect_tx_elect(&sm.q_full, 4 * kBoxBytes);
+    for (int m = 0; m < 2; ++m)
+      for (int u = 0; u < 2; ++u)
+        tma_load_2d_elect(sQ + m * kQTileBytes + u * kBoxBytes, &p.tm_q, &sm.q_full, (h * G + 2 * m + u) * 64,
+                          b * p.Nq + n0);
+    int issued = 0;
+    for (int t = 0; t < T; ++t) {
+      const int st = t % kStages, r = t / kStages;
+      if (r > 0 && !warp_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) break;
+      const KeyTile kt = key_tile(p, sm.sel, t, T_loc, wstart, wend);
+      mbar_arrive_expect_tx_elect(&sm.kv_full[st], 2 * kBoxBytes);
+      tma_load_2d_elect(sK + st * kBoxBytes, &p.tm_k, &sm.kv_full[st], h * 64, b * p.Nk + kt.row);
+      tma_load_2d_elect(sV + st * kBoxBytes, &p.tm_v, &sm.kv_full[st], h * 64, b * p.Nk + kt.row);
+      issued = t + 1;
+    }
+    // Drain: every TMA write into shared memory must land before the CTA exits.
+    if (lane == 0) {
       wait_noabort(&sm.q_full, 0, p.status);
       for (int s = 0; s < kStages && s < issued; ++s) {
         const int t_last = s + kStages * ((issued - 1 - s) / kStages);
@@ -263,74 +319,74 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc_s64 = make_idesc_bf16(128, 64, false);
-      const uint32_t idesc_s128 = make_idesc_bf16(128, 128, false);
-      const uint32_t idesc_pv = make_idesc_bf16(128, 64, true);
-      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
-      bool ok = bounded_wait(&sm.q_full, 0, abort_flag, p.status);
-      tc_fence_after();
-      int prev_nseg = 0;
-      for (int t = 0; ok && t <= T; ++t) {
-        const int st = t % kStages;
-        int nseg = 0;
-        if (t < T) {
-          if (!bounded_wait(&sm.kv_full[st], (t / kStages) & 1, abort_flag, p.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          nseg = key_tile(p, sm.sel, t, T_loc, wstart, wend).nseg;
-        }
-        for (int m = 0; m < 2; ++m) {
-          const uint32_t tS = tmem + 128 * m;
-          if (t > 0) {
-            if (!bounded_wait(&sm.p_full[m], (t - 1) & 1, abort_flag, p.status)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const int pt = t - 1;
-            const uint32_t tO = tmem + 256 + 128 * m + (pt < T_loc ? 0 : 64);
-            const uint32_t acc0 = (pt == 0 || pt == T_loc) ? 0u : 1u;
-            const uint64_t vdesc = sw128_desc(sVa + (pt % kStages) * kTileBytes, 1024, 16384);
-            for (int ks = 0; ks < prev_nseg * 4; ++ks)
-              mma_ts(tO, tS + ks * 8, vdesc + static_cast<uint64_t>(ks * 128), idesc_pv, ks > 0 ? 1u : acc0);
-          }
-          if (t < T) {
-            const uint64_t qdesc = sw128_desc(sQa + m * kTileBytes, 1024, 16);
-            const uint64_t kdesc = sw128_desc(sKa + st * kTileBytes, 1024, 16);
-            const uint32_t idesc = nseg == 2 ? idesc_s128 : idesc_s64;
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers (converged warps)
+    // Warp 1 issues every MMA of M-tile 0 and warp 2 those of M-tile 1, so the two
+    // issue chains overlap on the tensor core.
+    const int m = warp - 1;
+    const uint32_t idesc_s = make_idesc_bf16(128, 64, false);
+    const uint32_t idesc_pv = make_idesc_bf16(128, 64, true);
+    const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV);
+    const uint64_t qdesc = sw128_desc(smem_u32(sQ) + m * kQTileBytes, 1024, 16);
+    // S_m(t) = Q_m K(t)^T into S buffer t%2 of M-tile m
+    auto issue_s = [&](int t) {
+      const uint64_t kdesc = sw128_desc(sKa + (t % kStages) * kBoxBytes, 1024, 16);
+      const uint32_t tS = tmem + col_s(m, t & 1);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              mma_ss(tS, qdesc + static_cast<uint64_t>(2 * ks), kdesc + static_cast<uint64_t>(2 * ks), idesc,
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ss_elect(tS, qdesc + static_cast<uint64_t>(2 * ks), kdesc + static_cast<uint64_t>(2 * ks), idesc_s,
                      ks > 0 ? 1u : 0u);
-            tc_commit(&sm.s_full[m]);
-          }
-        }
-        if (!ok) break;
-        if (t > 0) tc_commit(&sm.kv_empty[(t - 1) % kStages]);
-        prev_nseg = nseg;
-      }
-      if (ok) {
-        tc_commit(&sm.o_final[0]);
-        tc_commit(&sm.o_final[1]);
-      }
-      tc_commit(&sm.drain);
-      wait_noabort(&sm.drain, 0, p.status);
+      tc_commit_elect(&sm.s_full[m][t & 1]);
+    };
+    bool ok = warp_wait(&sm.q_full, 0, abort_flag, p.status);
+    tc_fence_after();
+    for (int j = 0; ok && j < 2 && j < T; ++j) {
+      ok = warp_wait(&sm.kv_full[j % kStages], (j / kStages) & 1, abort_flag, p.status);
+      tc_fence_after();
+      if (ok) issue_s(j);
     }
+    for (int t = 0; ok && t < T; ++t) {
+      const uint32_t col_o_off = t < T_loc ? 0u : 64u;
+      const uint32_t acc0 = (t == 0 || t == T_loc) ? 0u : 1u;
+      const uint64_t vdesc = sw128_desc(sVa + (t % kStages) * kBoxBytes, 1024, 16384);
+      MOSAIC_TRACE_AT(traced && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 0);
+      if (!warp_wait(&sm.p_full[m][t & 1], (t >> 1) & 1, abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
+      MOSAIC_TRACE_AT(traced && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 1);
+      tc_fence_after();
+      const uint32_t tO = tmem + col_ol(m) + col_o_off;
+      const uint32_t tP = tmem + col_s(m, t & 1);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ts_elect(tO, tP + ks * 8, vdesc + static_cast<uint64_t>(ks * 128), idesc_pv, ks > 0 ? 1u : acc0);
+      tc_commit_elect(&sm.o_done[m]);
+      if (t + 2 < T) {
+        if (!warp_wait(&sm.kv_full[(t + 2) % kStages], ((t + 2) / kStages) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_s(t + 2);
+      }
+      tc_commit_elect(&sm.kv_empty[t % kStages]);
+      MOSAIC_TRACE_AT(traced && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 2);
+    }
+    if (ok) tc_commit_elect(&sm.o_final[m]);
+    tc_commit_elect(&sm.drain[m]);
+    if (lane == 0) wait_noabort(&sm.drain[m], 0, p.status);
     __syncwarp();
+  } else if (warp == 3) {
+    // idle warp (keeps the softmax warpgroups aligned to TMEM lane quadrants)
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int wg = (warp - 2) >> 2;  // M-tile
+    const int wg = (warp - 4) >> 2;  // M-tile
     const int qd = warp & 3;         // TMEM lane quadrant this warp can access
     const int row = qd * 32 + lane;  // row of the M-tile
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 128 * wg;
-    const uint32_t tOl = tmem + lane_off + 256 + 128 * wg;
-    const uint32_t tOs = tOl + 64;
+    const uint32_t tOl = tmem + lane_off + col_ol(wg);
+    const uint32_t tOs = tmem + lane_off + col_os(wg);
     const int head = h * G + 2 * wg + (row >> 6);
     const int n = n0 + (row & 63);
     const bool live = n < p.Nq;
@@ -371,20 +427,23 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
         m_run = -INFINITY;
         l_run = 0.f;
       }
-      if (!bounded_wait(&sm.s_full[wg], t & 1, abort_flag, p.status)) {
+      const bool rec = traced && row == 0 && t < 64;
+      MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 0);
+      if (!bounded_wait(&sm.s_full[wg][t & 1], (t >> 1) & 1, abort_flag, p.status)) {
         ok = false;
         break;
       }
+      MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 1);
       tc_fence_after();
-      const KeyTile kt = key_tile(p, sm.sel, t, T_loc, wstart, wend);
+      const int valid = key_tile(p, sm.sel, t, T_loc, wstart, wend).valid;
       const bool first = (t == 0) || (t == T_loc);
-      const uint32_t tO = t < T_loc ? tOl : tOs;
-      if (kt.nseg == 2)
-        softmax_tile<128>(tS, tO, kt.valid, first, p.scale_log2, m_run, l_run);
-      else
-        softmax_tile<64>(tS, tO, kt.valid, first, p.scale_log2, m_run, l_run);
+      const uint32_t tS = tmem + lane_off + col_s(wg, t & 1);
+      ok = softmax_tile(tS, t < T_loc ? tOl : tOs, valid, first, p.scale_log2, m_run, l_run, &sm.o_done[wg],
+                        (t - 1) & 1, abort_flag, p.status, rec ? wg * 64 + t : -1);
+      MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 4);
       tc_fence_before();
-      mbar_arrive(&sm.p_full[wg]);
+      mbar_arrive(&sm.p_full[wg][t & 1]);
+      if (!ok) break;
     }
     if (T_slc > 0) {
       l_slc = l_run;
@@ -393,6 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       l_loc = l_run;
     }
 
+    MOSAIC_TRACE_AT(traced && row == 0, 2002 + wg);
     if (ok) ok = bounded_wait(&sm.o_final[wg], 0, abort_flag, p.status);
     tc_fence_after();
     if (ok) {
@@ -454,8 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
     }
   }
 
+  MOSAIC_TRACE_AT(traced && (threadIdx.x == 64 || threadIdx.x == 192), 2004 + (threadIdx.x == 192));
   tc_fence_before();
   __syncthreads();
+  MOSAIC_TRACE_AT(traced && threadIdx.x == 0, 2001);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);

@@ -219,4 +219,116 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+
+// ---------------------------------------------------------------- single-lane issue from a converged warp
+// tcgen05.mma / tcgen05.commit / TMA issued by one lane chosen with elect.sync
+// inside the same asm block, so the issuing warp stays converged (issuing from a
+// divergent single-lane loop costs ~3x more cycles per tcgen05.mma).
+__device__ __forceinline__ void mma_ss_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_elect(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n\t}" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_elect(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+// Bounded wait for a whole warp: lane 0 polls, the result is broadcast, and the
+// warp leaves converged.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = bounded_wait(bar, parity, abort_flag, status);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// ---------------------------------------------------------------- packed fp32 (sm_100)
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Software 2^x for x <= 0 on the FMA/ALU pipes, for two values at once.
+// Cody-Waite style reduction x = j + f with j = rint(x) (the 1.5*2^23 shifter
+// trick) and f in [-1/2, 1/2], then 2^f by a degree-3 polynomial whose
+// coefficients are a relative-error minimax fit computed for this library by the
+// Remez exchange algorithm (max relative error 7.5e-5, far below the 2^-9 of
+// the bf16 rounding that P undergoes next), and 2^j added into the exponent
+// field. x is clamped at -125 so that the exponent cannot underflow.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992807f, kC1 = 0.69326099f, kC2 = 0.24261112f, kC3 = 0.05517167f;
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
+  const uint64_t xc = f2_pack(x0, x1);
+  const uint64_t t = f2_add(xc, f2_pack(kShift, kShift));        // low mantissa bits hold rint(x)
+  const uint64_t j = f2_add(t, f2_pack(-kShift, -kShift));       // rint(x) as a float
+  const uint64_t f = f2_fma(j, f2_pack(-1.0f, -1.0f), xc);       // x - rint(x), exact
+  uint64_t p = f2_fma(f, f2_pack(kC3, kC3), f2_pack(kC2, kC2));
+  p = f2_fma(p, f, f2_pack(kC1, kC1));
+  p = f2_fma(p, f, f2_pack(kC0, kC0));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  // (bits of t) << 23 == rint(x) << 23 modulo 2^32, because 1.5*2^23 has nine zero low bits
+  const float r0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  const float r1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+  return f2_pack(r0, r1);
+}
+
 }  // namespace mosaic
