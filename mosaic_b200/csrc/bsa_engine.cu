@@ -230,6 +230,10 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
   uint8_t* sV = sK + kStages * kBoxBytes;
   EngineSmem& sm = *reinterpret_cast<EngineSmem*>(sV + kStages * kBoxBytes);
   volatile int* abort_flag = &sm.abort_flag;
+  // A kernel launched after this one with programmatic stream serialization (the
+  // top-k kernel after the coarse attention) may start right away: it does not
+  // read anything this kernel writes.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;

@@ -63,6 +63,10 @@ struct TopkLaunch {
   const void* k_cmp;  // [B, nb, Hk, 64] bf16
   int64_t* idx;       // [B, nb, Hk, K]
   int B, nb, Hq, Hk, K;
+  // Launch with programmatic stream serialization, so that the kernel may start
+  // while the previous kernel of the stream (which must not produce this
+  // kernel's inputs) is still running.
+  bool overlap_previous;
 };
 
 int launch_engine(const EngineLaunch& a, cudaStream_t stream);

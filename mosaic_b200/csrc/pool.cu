@@ -58,7 +58,7 @@ __device__ __forceinline__ uint4 rope_chunk(uint4 x, const float* cos_row, const
 }
 
 template <bool kRope>
-__global__ void __launch_bounds__(1024) pool_kernel(const PoolParams p) {
+__global__ void __launch_bounds__(512, 1) pool_kernel(const PoolParams p) {
   extern __shared__ float part[];  // [rg][C][8]
   const int C = p.cq + p.ck + p.cv;
   const int blk = blockIdx.x, b = blockIdx.y;
@@ -82,19 +82,31 @@ __global__ void __launch_bounds__(1024) pool_kernel(const PoolParams p) {
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     const int row0 = blk * p.bs;
     const size_t base = (static_cast<size_t>(b) * p.N + row0) * cpr + cc;
-#pragma unroll 4
-    for (int r = g; r < p.bs; r += p.rg) {
-      uint4 x = __ldg(src + base + static_cast<size_t>(r) * cpr);
-      if (rotate) {
-        x = rope_chunk(x, p.cos + static_cast<size_t>(row0 + r) * 32, p.sin + static_cast<size_t>(row0 + r) * 32, p0);
-        rot[base + static_cast<size_t>(r) * cpr] = x;
-      }
-      const __nv_bfloat162* xv = reinterpret_cast<const __nv_bfloat162*>(&x);
+    // 8 rows per step, all loads issued before any is used, so that each thread
+    // keeps 128 bytes in flight (the kernel is bound by HBM latency x bandwidth).
+    for (int r0 = g; r0 < p.bs; r0 += 8 * p.rg) {
+      uint4 x[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(xv[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u * p.rg;
+        x[u] = r < p.bs ? __ldg(src + base + static_cast<size_t>(r) * cpr) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u * p.rg;
+        if (r >= p.bs) continue;
+        uint4 xv = x[u];
+        if (rotate) {
+          xv = rope_chunk(xv, p.cos + static_cast<size_t>(row0 + r) * 32, p.sin + static_cast<size_t>(row0 + r) * 32, p0);
+          rot[base + static_cast<size_t>(r) * cpr] = xv;
+        }
+        const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(xh[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
       }
     }
 #pragma unroll
@@ -155,8 +167,8 @@ int launch_pool(const PoolLaunch& a, cudaStream_t stream) {
   p.cv = a.v_cmp != nullptr ? a.Hk * 8 : 0;
   if (p.cq > 0 && a.q_cmp == nullptr) return MOSAIC_ERR_INVALID_ARGUMENT;
   const int C = p.cq + p.ck + p.cv;
-  if (C > 1024) return MOSAIC_ERR_UNSUPPORTED;
-  p.rg = 1024 / C < 4 ? 1024 / C : 4;
+  if (C > 512) return MOSAIC_ERR_UNSUPPORTED;
+  p.rg = 512 / C < 4 ? 512 / C : 4;
   const int threads = ((C * p.rg + 31) / 32) * 32;
   const size_t smem = static_cast<size_t>(p.rg) * C * 8 * sizeof(float);
   dim3 grid(p.nb, a.B);

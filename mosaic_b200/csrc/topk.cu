@@ -10,13 +10,21 @@
 // then uses idx[..., h, :] for the contiguous heads h*G .. h*G+G-1 (ops.py:49);
 // this kernel reproduces it on purpose.
 //
-// One CTA handles 16 query blocks of one (b, h) and streams the nb key blocks in
-// chunks of 256: 8 warps compute the 16 x 256 T chunk with mma.sync (the score
-// GEMM is 0.9 GFLOP at Nside 64, far below the tensor pipe; the kernel is bound
-// by reading q_cmp/k_cmp), then each warp merges 2 rows' candidates into the
-// running top-K list. A candidate is the 32-bit key (order-preserving bf16 bits
-// << 16) | (65535 - block): its maximum is the largest score, ties going to the
-// lower block index, so the output is sorted descending like torch.topk.
+// Each score becomes the 32-bit key (order-preserving bf16 bits << 16) |
+// (65535 - block): keys are unique, their order is score descending with ties to
+// the lower block index (torch.topk's usual order), and the top-K of a row is
+// exactly the K largest keys.
+//
+// One CTA = 16 query blocks of one (b, h), 16 warps. The keys stream in chunks of
+// up to kChunk blocks:
+//   A) scores of the chunk -> shared memory (mma.sync m16n8k16; each warp owns
+//      whole 8-key column groups for all G heads, so the strided-group mean needs
+//      no cross-warp reduction);
+//   B) warp r owns row r: it finds the K-th largest key among the chunk and its
+//      running top list by a binary search on the key value (warp reductions),
+//      keeps the keys >= that one, and sorts them descending.
+// The work is tiny (0.9 GFLOP of scores at Nside 64); the kernel is latency-bound,
+// so the point of this layout is to keep many independent loads and warps in flight.
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -24,8 +32,9 @@ namespace mosaic {
 namespace {
 
 constexpr int kRows = 16;
-constexpr int kChunk = 256;
-constexpr int kThreads = 256;
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr int kChunk = 1024;  // key blocks scored per pass
 constexpr int kMaxG = 8;
 constexpr int kMaxK = 128;
 
@@ -35,6 +44,23 @@ struct TopkParams {
   int64_t* idx;
   int B, nb, Hq, Hk, K, G;
 };
+
+struct TopkSmem {
+  __nv_bfloat16 qs[kMaxG][kRows][64];  // 16 KB
+  uint32_t keys[kRows][kChunk];        // 64 KB
+  uint32_t top[kRows][kMaxK];          // 8 KB  running top list per row (sorted descending)
+  uint32_t buf[kWarps][kMaxK];         // 8 KB  per-warp selection buffers
+};
+
+// Logical k index of the m16n8k16 fragments -> physical head-dim index. Thread
+// (lane & 3) == gc holds logical k in {16ks + 2gc + {0,1,8,9}} (ks = 0..3); they map
+// to the contiguous physical range [16gc, 16gc + 16).
+__device__ __forceinline__ int perm_d(int kk) {
+  const int ks = kk >> 4, w = kk & 15;
+  const int gc = (w & 7) >> 1;
+  const int q = (w & 1) | ((w >> 3) << 1);  // e in {0,1,8,9} -> 0..3
+  return 16 * gc + 4 * ks + q;
+}
 
 __device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -53,105 +79,163 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(kThreads) topk_kernel(const TopkParams p) {
-  __shared__ __align__(16) __nv_bfloat16 qs[kMaxG][kRows][64];
-  __shared__ uint32_t tile[kRows][kChunk];
-  __shared__ uint32_t top[kRows][kMaxK];
+// A fragments of the 16 rows for head slot g (loaded once per chunk).
+// For G > 4 the fragments would not fit the register budget next to the B
+// fragments, so they are cached for G <= 4 only.
+template <int G>
+struct AFrags {
+  uint32_t a[G <= 4 ? G : 1][4][4];
+};
 
+template <int G>
+__device__ __forceinline__ void load_afrags(const TopkSmem& sm, AFrags<G>& f, int lane) {
+  if (G > 4) return;
+  const int gr = lane >> 2, gc = (lane & 3) * 2;
+#pragma unroll
+  for (int g = 0; g < (G <= 4 ? G : 1); ++g)
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      f.a[g][ks][0] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr][ks * 16 + gc]);
+      f.a[g][ks][1] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr + 8][ks * 16 + gc]);
+      f.a[g][ks][2] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr][ks * 16 + gc + 8]);
+      f.a[g][ks][3] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr + 8][ks * 16 + gc + 8]);
+    }
+}
+
+// Scores of key group [kb0, kb0+8) for the CTA's 16 rows into keys[][col0..col0+8).
+template <int G>
+__device__ __forceinline__ void score_group(const TopkParams& p, TopkSmem& sm, const AFrags<G>& f, int b, int h,
+                                            int kb0, int col0, int lane) {
+  const int gr = lane >> 2, gq = lane & 3;
+  const int key = kb0 + gr;
+  // physical head-dim range [16 gq, 16 gq + 16) of this thread's key row = its whole B fragment
+  uint4 raw[G][2];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int kv = (g * p.Hk + h) / G;
+    const uint4* src =
+        reinterpret_cast<const uint4*>(p.k_cmp + ((static_cast<size_t>(b) * p.nb + key) * p.Hk + kv) * 64 + 16 * gq);
+    raw[g][0] = key < p.nb ? __ldg(src) : make_uint4(0, 0, 0, 0);
+    raw[g][1] = key < p.nb ? __ldg(src + 1) : make_uint4(0, 0, 0, 0);
+  }
+  float tacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(raw[g]);  // 8 words: (ks, q-pair)
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      if (G <= 4) {
+        mma_bf16_16816(d, f.a[G <= 4 ? g : 0][ks], w[2 * ks], w[2 * ks + 1]);
+      } else {
+        const int gr = lane >> 2, gc = gq * 2;
+        uint32_t a[4];
+        a[0] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr][ks * 16 + gc]);
+        a[1] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr + 8][ks * 16 + gc]);
+        a[2] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr][ks * 16 + gc + 8]);
+        a[3] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr + 8][ks * 16 + gc + 8]);
+        mma_bf16_16816(d, a, w[2 * ks], w[2 * ks + 1]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) tacc[e] += round_bf16(d[e]);
+  }
+  const float fg = static_cast<float>(G);
+  const int gc = gq * 2;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int r = gr + (e >= 2 ? 8 : 0);
+    const int c = gc + (e & 1);
+    const int kb = kb0 + c;
+    sm.keys[r][col0 + c] = kb < p.nb ? order_key(__fdiv_rn(tacc[e], fg), kb) : 0u;
+  }
+}
+
+// Warp-wide: the K-th largest of the distinct candidate keys held in registers
+// (lane l holds candidates l, l+32, ...; absent ones are 0, below every real key),
+// by binary search on the key value: 32 steps, each a count of the keys >= mid
+// reduced over the warp. No shared-memory atomics, so skewed score distributions
+// cost nothing extra.
+template <int NV>
+__device__ __forceinline__ uint32_t kth_largest(const uint32_t (&v)[NV], int K) {
+  uint32_t lo = 0, hi = 0xFFFFFFFFu;  // invariant: count(>= lo) >= K, count(>= hi + 1) < K
+#pragma unroll 1
+  for (int step = 0; step < 32 && lo < hi; ++step) {
+    const uint32_t mid = lo + ((hi - lo) >> 1) + 1;
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cnt += v[i] >= mid ? 1u : 0u;
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (cnt >= static_cast<uint32_t>(K))
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  TopkSmem& sm = *reinterpret_cast<TopkSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i0 = blockIdx.x * kRows, h = blockIdx.y, b = blockIdx.z;
 
-  // q_cmp rows of the strided group {h, h+Hk, ...} for this CTA's 16 query blocks.
-  for (int e = threadIdx.x; e < p.G * kRows * 8; e += kThreads) {
-    const int g = e / (kRows * 8), r = (e / 8) % kRows, c = e % 8;
+  // q_cmp rows of the strided group {h, h+Hk, ...}, stored with the head dimension
+  // permuted by perm_d() so that every thread's B-fragment values of a key row are
+  // 32 contiguous bytes (the dot products are invariant to a shared permutation).
+  for (int e = threadIdx.x; e < G * kRows * 64; e += kThreads) {
+    const int g = e / (kRows * 64), r = (e / 64) % kRows, kk = e % 64;
     const int i = i0 + r;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (i < p.nb) {
-      const int j = g * p.Hk + h;
-      val = *reinterpret_cast<const uint4*>(p.q_cmp + ((static_cast<size_t>(b) * p.nb + i) * p.Hq + j) * 64 + c * 8);
-    }
-    *reinterpret_cast<uint4*>(&qs[g][r][c * 8]) = val;
+    __nv_bfloat16 val = __float2bfloat16(0.f);
+    if (i < p.nb) val = p.q_cmp[((static_cast<size_t>(b) * p.nb + i) * p.Hq + g * p.Hk + h) * 64 + perm_d(kk)];
+    sm.qs[g][r][kk] = val;
   }
-  int count = 0;  // entries in the running top list (same in every warp)
+  int count = 0;  // entries of the running top list (same in every warp)
   __syncthreads();
 
-  const int gr = lane >> 2, gc = (lane & 3) * 2;  // mma fragment coordinates
   for (int c0 = 0; c0 < p.nb; c0 += kChunk) {
-    // ---- T chunk: warp w covers keys c0 + 32w .. c0 + 32w + 31 (4 n-tiles of 8)
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int key = c0 + warp * 32 + nt * 8 + gr;  // B-fragment column of this thread
-      float tacc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int g = 0; g < p.G; ++g) {
-        const int j = g * p.Hk + h;
-        const int kv = j / p.G;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t* krow =
-            key < p.nb ? reinterpret_cast<const uint32_t*>(p.k_cmp + ((static_cast<size_t>(b) * p.nb + key) * p.Hk + kv) * 64)
-                       : nullptr;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          uint32_t a[4];
-          a[0] = *reinterpret_cast<const uint32_t*>(&qs[g][gr][ks * 16 + gc]);
-          a[1] = *reinterpret_cast<const uint32_t*>(&qs[g][gr + 8][ks * 16 + gc]);
-          a[2] = *reinterpret_cast<const uint32_t*>(&qs[g][gr][ks * 16 + gc + 8]);
-          a[3] = *reinterpret_cast<const uint32_t*>(&qs[g][gr + 8][ks * 16 + gc + 8]);
-          const uint32_t b0 = krow ? __ldg(krow + (ks * 16 + gc) / 2) : 0u;
-          const uint32_t b1 = krow ? __ldg(krow + (ks * 16 + gc + 8) / 2) : 0u;
-          mma_bf16_16816(d, a, b0, b1);
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) tacc[e] += round_bf16(d[e]);
-      }
-      // d[e]: row gr (+8 for e >= 2), key column nt*8 + gc + (e & 1)
-      const float fg = static_cast<float>(p.G);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = gr + (e >= 2 ? 8 : 0);
-        const int col = warp * 32 + nt * 8 + gc + (e & 1);
-        const int kb = c0 + col;
-        tile[r][col] = kb < p.nb ? order_key(__fdiv_rn(tacc[e], fg), kb) : 0u;
-      }
+    const int width = min(kChunk, p.nb - c0);
+    // ---- A: scores of this chunk
+    {
+      AFrags<G> f;
+      load_afrags<G>(sm, f, lane);
+      for (int grp = warp; grp * 8 < width; grp += kWarps) score_group<G>(p, sm, f, b, h, c0 + grp * 8, grp * 8, lane);
     }
     __syncthreads();
 
-    // ---- merge: warp w owns rows 2w and 2w+1
+    // ---- B: warp `warp` merges row `warp`
+    const int r = warp;
+    uint32_t* top = sm.top[r];
+    uint32_t* row = sm.keys[r];
+    const int K = p.K;
+    constexpr int NV = (kChunk + kMaxK) / 32;  // candidates per lane
+    uint32_t v[NV];
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const int r = 2 * warp + rr;
-      uint32_t cand[kChunk / 32 + kMaxK / 32];
-#pragma unroll
-      for (int s = 0; s < kChunk / 32; ++s) cand[s] = tile[r][lane + 32 * s];
-#pragma unroll
-      for (int s = 0; s < kMaxK / 32; ++s) {
-        const int e = lane + 32 * s;
-        cand[kChunk / 32 + s] = e < count ? top[r][e] : 0u;
-      }
-      // Skip the merge when no new candidate beats the current K-th entry.
-      bool any_new = true;
-      if (count >= p.K) {
-        const uint32_t kth = top[r][p.K - 1];
-        bool mine = false;
-#pragma unroll
-        for (int s = 0; s < kChunk / 32; ++s) mine |= cand[s] > kth;
-        any_new = __any_sync(0xffffffffu, mine);
-      }
-      __syncwarp();
-      if (any_new) {
-        for (int e = 0; e < p.K; ++e) {
-          uint32_t best = 0;
-#pragma unroll
-          for (int s = 0; s < kChunk / 32 + kMaxK / 32; ++s) best = max(best, cand[s]);
-          best = __reduce_max_sync(0xffffffffu, best);
-#pragma unroll
-          for (int s = 0; s < kChunk / 32 + kMaxK / 32; ++s)
-            if (cand[s] == best) cand[s] = 0u;
-          if (lane == 0) top[r][e] = best;
-        }
-      }
-      __syncwarp();
+    for (int i = 0; i < NV; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < width ? row[e] : (e - width < count ? top[e - width] : 0u);
     }
-    count = min(p.K, count + kChunk);
+    const uint32_t kth = kth_largest<NV>(v, K);
+    // keep the keys >= kth (exactly K of them) in an unsorted buffer ...
+    uint32_t* buf = sm.buf[warp];
+    int base = 0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const bool keep = v[i] >= kth && v[i] != 0u;
+      const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      if (keep) buf[base + __popc(bal & ((1u << lane) - 1u))] = v[i];
+      base += __popc(bal);
+    }
+    __syncwarp();
+    // ... and write them to the top list sorted descending (rank = number of larger keys)
+    for (int e = lane; e < K; e += 32) {
+      const uint32_t x = buf[e];
+      int rank = 0;
+      for (int j = 0; j < K; ++j) rank += buf[j] > x ? 1 : 0;
+      top[rank] = x;
+    }
+    count = K;
     __syncthreads();
   }
 
@@ -161,8 +245,33 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const TopkParams p) {
     const int i = i0 + r;
     if (i < p.nb)
       p.idx[((static_cast<size_t>(b) * p.nb + i) * p.Hk + h) * p.K + s] =
-          static_cast<int64_t>(0xFFFFu - (top[r][s] & 0xFFFFu));
+          static_cast<int64_t>(0xFFFFu - (sm.top[r][s] & 0xFFFFu));
   }
+}
+
+template <int G>
+int launch_g(const TopkParams& p, cudaStream_t stream, bool overlap) {
+  const size_t smem = sizeof(TopkSmem);
+  static bool attr_done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOSAIC_ERR_CUDA;
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(topk_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return MOSAIC_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.nb + kRows - 1) / kRows, p.Hk, p.B);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, topk_kernel<G>, p) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
 }  // namespace
@@ -178,12 +287,14 @@ int launch_topk(const TopkLaunch& a, cudaStream_t stream) {
   p.Hk = a.Hk;
   p.K = a.K;
   p.G = a.Hq / a.Hk;
-  if (p.G > kMaxG || p.K > kMaxK || p.K > p.nb || p.nb > 65535) return MOSAIC_ERR_UNSUPPORTED;
-  dim3 grid((a.nb + kRows - 1) / kRows, a.Hk, a.B);
-  topk_kernel<<<grid, kThreads, 0, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  if (p.K > kMaxK || p.K > p.nb || p.nb > 65535) return MOSAIC_ERR_UNSUPPORTED;
+  switch (p.G) {
+    case 1: return launch_g<1>(p, stream, a.overlap_previous);
+    case 2: return launch_g<2>(p, stream, a.overlap_previous);
+    case 4: return launch_g<4>(p, stream, a.overlap_previous);
+    case 8: return launch_g<8>(p, stream, a.overlap_previous);
+    default: return MOSAIC_ERR_UNSUPPORTED;
+  }
 }
-
-int topk_max_k() { return kMaxK; }
 
 }  // namespace mosaic
