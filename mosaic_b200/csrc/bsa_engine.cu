@@ -81,10 +81,37 @@ struct EngineParams {
   int win, bs, K, nqb, nkb;
   int combine;
   float scale_log2;
+  int qtiles;  // 64-query tiles per (batch, kv head)
+  int units;   // B * Hk * qtiles work units
 };
 
+// One work unit: (batch b, kv head h, 64-query tile starting at n0) and its key tiles.
+struct Unit {
+  int b, h, n0;
+  int wstart, wend;  // local window
+  int T_loc, T;      // local tiles, all tiles
+};
+
+__device__ __forceinline__ Unit decode_unit(const EngineParams& p, int u) {
+  Unit w;
+  const int qt = u % p.qtiles, rest = u / p.qtiles;
+  w.h = rest % p.Hk;
+  w.b = rest / p.Hk;
+  w.n0 = qt * kQTile;
+  w.T_loc = 0;
+  w.wstart = w.wend = 0;
+  if (p.win > 0) {
+    w.wstart = (w.n0 / p.win) * p.win;
+    w.wend = min(w.wstart + p.win, p.Nk);
+    w.T_loc = (w.wend - w.wstart + 63) / 64;
+  }
+  w.T = w.T_loc + (p.K > 0 ? (p.K * p.bs) / 64 : 0);
+  return w;
+}
+
 struct EngineSmem {
-  uint64_t q_full;
+  uint64_t q_full[2];   // Q double buffer: loaded
+  uint64_t q_empty[2];  // Q double buffer: every S of the unit issued (both MMA warps)
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[2][2];  // [M-tile][S buffer]
@@ -92,15 +119,16 @@ struct EngineSmem {
   // tiles t and t+1 before the MMA warp consumes P(t); it can never get two tiles
   // ahead on the same buffer (S(t+2) is issued only after P(t)*V(t)).
   uint64_t p_full[2][2];
-  uint64_t o_done[2];
-  uint64_t o_final[2];
+  uint64_t o_done[2];   // per P*V
+  uint64_t o_final[2];  // per work unit: its last P*V has completed
+  uint64_t o_empty[2];  // per work unit: the epilogue has read O
   uint64_t drain[2];
   uint32_t tmem_base;
   int abort_flag;
   int sel[kMaxSel];
 };
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kQTileBytes + 2 * kStages * kBoxBytes + sizeof(EngineSmem);
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + 4 * kQTileBytes + 2 * kStages * kBoxBytes + sizeof(EngineSmem);
 
 // TMEM columns (fp32, 128 lanes): S/P buffer b of M-tile m at 64*(2m+b);
 // O_local of M-tile m at 256+128m, O_selected at 320+128m.
@@ -225,8 +253,8 @@ __device__ __forceinline__ bool wait_noabort(uint64_t* bar, uint32_t parity, int
 __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_constant__ EngineParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = tiles;
-  uint8_t* sK = tiles + 2 * kQTileBytes;
+  uint8_t* sQ = tiles;  // two buffers of 2 M-tiles
+  uint8_t* sK = tiles + 4 * kQTileBytes;
   uint8_t* sV = sK + kStages * kBoxBytes;
   EngineSmem& sm = *reinterpret_cast<EngineSmem*>(sV + kStages * kBoxBytes);
   volatile int* abort_flag = &sm.abort_flag;
@@ -236,23 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int n0 = qt * kQTile;
-  const bool traced = blockIdx.x == 5 && blockIdx.y == 1 && blockIdx.z == 0;
-  MOSAIC_TRACE_AT(traced && threadIdx.x == 0, 2000);
+  const bool traced_cta = blockIdx.x == 5;
+  MOSAIC_TRACE_AT(traced_cta && threadIdx.x == 0, 2000);
   const int G = p.Hq / p.Hk;
 
-  int T_loc = 0, wstart = 0, wend = 0;
-  if (p.win > 0) {
-    wstart = (n0 / p.win) * p.win;
-    wend = min(wstart + p.win, p.Nk);
-    T_loc = (wend - wstart + 63) / 64;
-  }
-  const int T_slc = p.K > 0 ? (p.K * p.bs) / 64 : 0;
-  const int T = T_loc + T_slc;
-
   if (threadIdx.x == 0) {
-    mbar_init(&sm.q_full, 1);
+    for (int qb = 0; qb < 2; ++qb) {
+      mbar_init(&sm.q_full[qb], 1);
+      mbar_init(&sm.q_empty[qb], 2);  // both MMA warps
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 2);  // released by both MMA warps
@@ -264,24 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       mbar_init(&sm.p_full[m][1], 128);
       mbar_init(&sm.o_done[m], 1);
       mbar_init(&sm.o_final[m], 1);
+      mbar_init(&sm.o_empty[m], 128);
       mbar_init(&sm.drain[m], 1);
     }
     sm.abort_flag = 0;
     fence_mbar_init();
-  }
-  if (warp == 0 && p.K > 0) {
-    // Stage this query block's selected kv blocks; out-of-range entries are
-    // reported and clamped so that no load leaves the batch.
-    const int qb = n0 / p.bs;
-    const int64_t* src = p.block_idx + ((static_cast<int64_t>(b) * p.nqb + qb) * p.Hk + h) * p.K;
-    for (int s = lane; s < p.K; s += 32) {
-      int64_t v = src[s];
-      if (v < 0 || v >= p.nkb) {
-        if (p.status) atomicOr(p.status, MOSAIC_STATUS_BAD_INDEX);
-        v = 0;
-      }
-      sm.sel[s] = static_cast<int>(v);
-    }
   }
   if (warp == 1) {
     tmem_alloc(&sm.tmem_base, 512);
@@ -292,6 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
+  // Every role walks the same units in the same order; `g` counts key tiles
+  // across units so that ring stages, S buffers and barrier phases continue.
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (converged warp)
     if (lane == 0) {
@@ -299,27 +308,58 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
     }
-    mbar_arrive_expect_tx_elect(&sm.q_full, 4 * kBoxBytes);
-    for (int m = 0; m < 2; ++m)
-      for (int u = 0; u < 2; ++u)
-        tma_load_2d_elect(sQ + m * kQTileBytes + u * kBoxBytes, &p.tm_q, &sm.q_full, (h * G + 2 * m + u) * 64,
-                          b * p.Nq + n0);
-    int issued = 0;
-    for (int t = 0; t < T; ++t) {
-      const int st = t % kStages, r = t / kStages;
-      if (r > 0 && !warp_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) break;
-      const KeyTile kt = key_tile(p, sm.sel, t, T_loc, wstart, wend);
-      mbar_arrive_expect_tx_elect(&sm.kv_full[st], 2 * kBoxBytes);
-      tma_load_2d_elect(sK + st * kBoxBytes, &p.tm_k, &sm.kv_full[st], h * 64, b * p.Nk + kt.row);
-      tma_load_2d_elect(sV + st * kBoxBytes, &p.tm_v, &sm.kv_full[st], h * 64, b * p.Nk + kt.row);
-      issued = t + 1;
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
+      const Unit w = decode_unit(p, u);
+      if (p.K > 0) {
+        // This query block's selected kv blocks; out-of-range entries are
+        // reported and clamped so that no load leaves the batch. Only this warp
+        // reads sel[], so it is rewritten per unit.
+        const int qb = w.n0 / p.bs;
+        const int64_t* src = p.block_idx + ((static_cast<int64_t>(w.b) * p.nqb + qb) * p.Hk + w.h) * p.K;
+        __syncwarp();
+        for (int s = lane; s < p.K; s += 32) {
+          int64_t v = src[s];
+          if (v < 0 || v >= p.nkb) {
+            if (p.status) atomicOr(p.status, MOSAIC_STATUS_BAD_INDEX);
+            v = 0;
+          }
+          sm.sel[s] = static_cast<int>(v);
+        }
+        __syncwarp();
+      }
+      const int qbuf = it & 1;
+      if (it >= 2 && !warp_wait(&sm.q_empty[qbuf], ((it - 2) >> 1) & 1, abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx_elect(&sm.q_full[qbuf], 4 * kBoxBytes);
+      for (int m = 0; m < 2; ++m)
+        for (int v = 0; v < 2; ++v)
+          tma_load_2d_elect(sQ + (2 * qbuf + m) * kQTileBytes + v * kBoxBytes, &p.tm_q, &sm.q_full[qbuf],
+                            (w.h * G + 2 * m + v) * 64, w.b * p.Nq + w.n0);
+      for (int t = 0; t < w.T; ++t, ++g) {
+        const int st = g % kStages, r = g / kStages;
+        if (r > 0 && !warp_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        const KeyTile kt = key_tile(p, sm.sel, t, w.T_loc, w.wstart, w.wend);
+        mbar_arrive_expect_tx_elect(&sm.kv_full[st], 2 * kBoxBytes);
+        tma_load_2d_elect(sK + st * kBoxBytes, &p.tm_k, &sm.kv_full[st], w.h * 64, w.b * p.Nk + kt.row);
+        tma_load_2d_elect(sV + st * kBoxBytes, &p.tm_v, &sm.kv_full[st], w.h * 64, w.b * p.Nk + kt.row);
+      }
     }
     // Drain: every TMA write into shared memory must land before the CTA exits.
     if (lane == 0) {
-      wait_noabort(&sm.q_full, 0, p.status);
-      for (int s = 0; s < kStages && s < issued; ++s) {
-        const int t_last = s + kStages * ((issued - 1 - s) / kStages);
-        wait_noabort(&sm.kv_full[s], (t_last / kStages) & 1, p.status);
+      for (int qb = 0; qb < 2 && qb < it; ++qb) {
+        const int last_it = qb + 2 * ((it - 1 - qb) / 2);
+        wait_noabort(&sm.q_full[qb], (last_it >> 1) & 1, p.status);
+      }
+      for (int s = 0; s < kStages && s < g; ++s) {
+        const int g_last = s + kStages * ((g - 1 - s) / kStages);
+        wait_noabort(&sm.kv_full[s], (g_last / kStages) & 1, p.status);
       }
     }
     __syncwarp();
@@ -330,54 +370,69 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
     const int m = warp - 1;
     const uint32_t idesc_s = make_idesc_bf16(128, 64, false);
     const uint32_t idesc_pv = make_idesc_bf16(128, 64, true);
-    const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV);
-    const uint64_t qdesc = sw128_desc(smem_u32(sQ) + m * kQTileBytes, 1024, 16);
-    // S_m(t) = Q_m K(t)^T into S buffer t%2 of M-tile m
-    auto issue_s = [&](int t) {
-      const uint64_t kdesc = sw128_desc(sKa + (t % kStages) * kBoxBytes, 1024, 16);
-      const uint32_t tS = tmem + col_s(m, t & 1);
+    const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sQa = smem_u32(sQ);
+    // S_m(gt) = Q_m K(gt)^T into S buffer gt%2 of M-tile m
+    auto issue_s = [&](uint64_t qdesc, int gt) {
+      const uint64_t kdesc = sw128_desc(sKa + (gt % kStages) * kBoxBytes, 1024, 16);
+      const uint32_t tS = tmem + col_s(m, gt & 1);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_ss_elect(tS, qdesc + static_cast<uint64_t>(2 * ks), kdesc + static_cast<uint64_t>(2 * ks), idesc_s,
                      ks > 0 ? 1u : 0u);
-      tc_commit_elect(&sm.s_full[m][t & 1]);
+      tc_commit_elect(&sm.s_full[m][gt & 1]);
     };
-    bool ok = warp_wait(&sm.q_full, 0, abort_flag, p.status);
-    tc_fence_after();
-    for (int j = 0; ok && j < 2 && j < T; ++j) {
-      ok = warp_wait(&sm.kv_full[j % kStages], (j / kStages) & 1, abort_flag, p.status);
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
+      const Unit w = decode_unit(p, u);
+      const int qbuf = it & 1;
+      const uint64_t qdesc = sw128_desc(sQa + (2 * qbuf + m) * kQTileBytes, 1024, 16);
+      ok = warp_wait(&sm.q_full[qbuf], (it >> 1) & 1, abort_flag, p.status);
       tc_fence_after();
-      if (ok) issue_s(j);
-    }
-    for (int t = 0; ok && t < T; ++t) {
-      const uint32_t col_o_off = t < T_loc ? 0u : 64u;
-      const uint32_t acc0 = (t == 0 || t == T_loc) ? 0u : 1u;
-      const uint64_t vdesc = sw128_desc(sVa + (t % kStages) * kBoxBytes, 1024, 16384);
-      MOSAIC_TRACE_AT(traced && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 0);
-      if (!warp_wait(&sm.p_full[m][t & 1], (t >> 1) & 1, abort_flag, p.status)) {
-        ok = false;
-        break;
+      for (int j = 0; ok && j < 2 && j < w.T; ++j) {
+        ok = warp_wait(&sm.kv_full[(g + j) % kStages], ((g + j) / kStages) & 1, abort_flag, p.status);
+        tc_fence_after();
+        if (ok) issue_s(qdesc, g + j);
       }
-      MOSAIC_TRACE_AT(traced && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 1);
-      tc_fence_after();
-      const uint32_t tO = tmem + col_ol(m) + col_o_off;
-      const uint32_t tP = tmem + col_s(m, t & 1);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        mma_ts_elect(tO, tP + ks * 8, vdesc + static_cast<uint64_t>(ks * 128), idesc_pv, ks > 0 ? 1u : acc0);
-      tc_commit_elect(&sm.o_done[m]);
-      if (t + 2 < T) {
-        if (!warp_wait(&sm.kv_full[(t + 2) % kStages], ((t + 2) / kStages) & 1, abort_flag, p.status)) {
+      // The epilogue of the previous unit must have read O before P*V overwrites it.
+      if (ok && it > 0) {
+        ok = warp_wait(&sm.o_empty[m], (it - 1) & 1, abort_flag, p.status);
+        tc_fence_after();
+      }
+      for (int t = 0; ok && t < w.T; ++t) {
+        const int gt = g + t;
+        const uint32_t col_o_off = t < w.T_loc ? 0u : 64u;
+        const uint32_t acc0 = (t == 0 || t == w.T_loc) ? 0u : 1u;
+        const uint64_t vdesc = sw128_desc(sVa + (gt % kStages) * kBoxBytes, 1024, 16384);
+        MOSAIC_TRACE_AT(traced_cta && it == 0 && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 0);
+        if (!warp_wait(&sm.p_full[m][gt & 1], (gt >> 1) & 1, abort_flag, p.status)) {
           ok = false;
           break;
         }
+        MOSAIC_TRACE_AT(traced_cta && it == 0 && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 1);
         tc_fence_after();
-        issue_s(t + 2);
+        const uint32_t tO = tmem + col_ol(m) + col_o_off;
+        const uint32_t tP = tmem + col_s(m, gt & 1);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_ts_elect(tO, tP + ks * 8, vdesc + static_cast<uint64_t>(ks * 128), idesc_pv, ks > 0 ? 1u : acc0);
+        tc_commit_elect(&sm.o_done[m]);
+        if (t + 2 < w.T) {
+          if (!warp_wait(&sm.kv_full[(gt + 2) % kStages], ((gt + 2) / kStages) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(qdesc, gt + 2);
+        }
+        tc_commit_elect(&sm.kv_empty[gt % kStages]);
+        MOSAIC_TRACE_AT(traced_cta && it == 0 && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 2);
       }
-      tc_commit_elect(&sm.kv_empty[t % kStages]);
-      MOSAIC_TRACE_AT(traced && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 2);
+      if (!ok) break;
+      tc_commit_elect(&sm.q_empty[qbuf]);  // every S of this unit has been issued
+      tc_commit_elect(&sm.o_final[m]);
+      g += w.T;
     }
-    if (ok) tc_commit_elect(&sm.o_final[m]);
     tc_commit_elect(&sm.drain[m]);
     if (lane == 0) wait_noabort(&sm.drain[m], 0, p.status);
     __syncwarp();
@@ -391,88 +446,102 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
     const uint32_t tOl = tmem + lane_off + col_ol(wg);
     const uint32_t tOs = tmem + lane_off + col_os(wg);
-    const int head = h * G + 2 * wg + (row >> 6);
-    const int n = n0 + (row & 63);
-    const bool live = n < p.Nq;
-
-    // Gates of this output row (the reference's weight_ba_cmp_slc[:, b, n, head]).
-    float c0 = 0.f, c1 = 0.f, c2 = 0.f;
-    if (p.combine == kCombineLocal) {
-      c0 = 1.f;
-    } else if (p.combine == kCombineSel) {
-      c2 = 1.f;
-    } else if (live) {
-      const size_t plane = static_cast<size_t>(p.B) * p.Nq * p.Hq;
-      const size_t gi = (static_cast<size_t>(b) * p.Nq + n) * p.Hq + head;
-      const float w0 = __bfloat162float(p.gates[gi]);
-      const float w1 = __bfloat162float(p.gates[plane + gi]);
-      const float w2 = __bfloat162float(p.gates[2 * plane + gi]);
-      if (p.combine == kCombineGated) {
-        c0 = w0;
-        c1 = w1;
-        c2 = w2;
-      } else if (p.combine == kCombineNoCmp) {
-        const float ws = w0 + w2 + 1e-8f;
-        c0 = w0 / ws;
-        c2 = w2 / ws;
-      } else {  // kCombineNoSlc
-        const float ws = w0 + w1 + 1e-8f;
-        c0 = w0 / ws;
-        c1 = w1 / ws;
-      }
-    }
-
-    float m_run = -INFINITY, l_run = 0.f;
-    float l_loc = 1.f, l_slc = 1.f, m_slc = 0.f;
+    int g = 0, it = 0;
     bool ok = true;
-    for (int t = 0; t < T; ++t) {
-      if (t == T_loc && t > 0) {
-        l_loc = l_run;
-        m_run = -INFINITY;
-        l_run = 0.f;
+    for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
+      const Unit w = decode_unit(p, u);
+      const int T_slc = w.T - w.T_loc;
+      const int head = w.h * G + 2 * wg + (row >> 6);
+      const int n = w.n0 + (row & 63);
+      const bool live = n < p.Nq;
+
+      // Gates of this output row (the reference's weight_ba_cmp_slc[:, b, n, head]).
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+      if (p.combine == kCombineLocal) {
+        c0 = 1.f;
+      } else if (p.combine == kCombineSel) {
+        c2 = 1.f;
+      } else if (live) {
+        const size_t plane = static_cast<size_t>(p.B) * p.Nq * p.Hq;
+        const size_t gi = (static_cast<size_t>(w.b) * p.Nq + n) * p.Hq + head;
+        const float w0 = __bfloat162float(p.gates[gi]);
+        const float w1 = __bfloat162float(p.gates[plane + gi]);
+        const float w2 = __bfloat162float(p.gates[2 * plane + gi]);
+        if (p.combine == kCombineGated) {
+          c0 = w0;
+          c1 = w1;
+          c2 = w2;
+        } else if (p.combine == kCombineNoCmp) {
+          const float ws = w0 + w2 + 1e-8f;
+          c0 = w0 / ws;
+          c2 = w2 / ws;
+        } else {  // kCombineNoSlc
+          const float ws = w0 + w1 + 1e-8f;
+          c0 = w0 / ws;
+          c1 = w1 / ws;
+        }
       }
-      const bool rec = traced && row == 0 && t < 64;
-      MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 0);
-      if (!bounded_wait(&sm.s_full[wg][t & 1], (t >> 1) & 1, abort_flag, p.status)) {
+
+      float m_run = -INFINITY, l_run = 0.f;
+      float l_loc = 1.f, l_slc = 1.f, m_slc = 0.f;
+      for (int t = 0; t < w.T; ++t) {
+        const int gt = g + t;
+        if (t == w.T_loc && t > 0) {
+          l_loc = l_run;
+          m_run = -INFINITY;
+          l_run = 0.f;
+        }
+        const bool rec = traced_cta && it == 0 && row == 0 && t < 64;
+        MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 0);
+        if (!bounded_wait(&sm.s_full[wg][gt & 1], (gt >> 1) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 1);
+        tc_fence_after();
+        const int valid = t < w.T_loc ? min(64, w.wend - (w.wstart + 64 * t)) : 64;
+        const bool first = (t == 0) || (t == w.T_loc);
+        const uint32_t tS = tmem + lane_off + col_s(wg, gt & 1);
+        ok = softmax_tile(tS, t < w.T_loc ? tOl : tOs, valid, first, p.scale_log2, m_run, l_run, &sm.o_done[wg],
+                          (gt - 1) & 1, abort_flag, p.status, rec ? wg * 64 + t : -1);
+        MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 4);
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[wg][gt & 1]);
+        if (!ok) break;
+      }
+      if (!ok) break;
+      if (T_slc > 0) {
+        l_slc = l_run;
+        m_slc = m_run;
+      } else {
+        l_loc = l_run;
+      }
+
+      // Start the coarse-attention row loads before waiting for the last P*V.
+      const uint4* cmp_row =
+          (live && c1 != 0.f)
+              ? reinterpret_cast<const uint4*>(p.o_cmp + ((static_cast<size_t>(w.b) * p.nqb + n / p.bs) * p.Hq + head) * 64)
+              : nullptr;
+      uint4 cmpv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cmpv[i] = cmp_row != nullptr ? __ldg(cmp_row + i) : make_uint4(0, 0, 0, 0);
+
+      MOSAIC_TRACE_AT(traced_cta && it == 0 && row == 0, 2002 + wg);
+      if (!bounded_wait(&sm.o_final[wg], it & 1, abort_flag, p.status)) {
         ok = false;
         break;
       }
-      MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 1);
       tc_fence_after();
-      const int valid = key_tile(p, sm.sel, t, T_loc, wstart, wend).valid;
-      const bool first = (t == 0) || (t == T_loc);
-      const uint32_t tS = tmem + lane_off + col_s(wg, t & 1);
-      ok = softmax_tile(tS, t < T_loc ? tOl : tOs, valid, first, p.scale_log2, m_run, l_run, &sm.o_done[wg],
-                        (t - 1) & 1, abort_flag, p.status, rec ? wg * 64 + t : -1);
-      MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 4);
-      tc_fence_before();
-      mbar_arrive(&sm.p_full[wg][t & 1]);
-      if (!ok) break;
-    }
-    if (T_slc > 0) {
-      l_slc = l_run;
-      m_slc = m_run;
-    } else {
-      l_loc = l_run;
-    }
-
-    MOSAIC_TRACE_AT(traced && row == 0, 2002 + wg);
-    if (ok) ok = bounded_wait(&sm.o_final[wg], 0, abort_flag, p.status);
-    tc_fence_after();
-    if (ok) {
-      const float f0 = T_loc > 0 ? c0 / l_loc : 0.f;
+      const float f0 = w.T_loc > 0 ? c0 / l_loc : 0.f;
       const float f2 = T_slc > 0 ? c2 / l_slc : 0.f;
-      const uint4* cmp_row =
-          (live && c1 != 0.f)
-              ? reinterpret_cast<const uint4*>(p.o_cmp + ((static_cast<size_t>(b) * p.nqb + n / p.bs) * p.Hq + head) * 64)
-              : nullptr;
-      uint4* dst = reinterpret_cast<uint4*>(p.out + ((static_cast<size_t>(b) * p.Nq + (live ? n : 0)) * p.Hq + head) * 64);
+      uint4* dst =
+          reinterpret_cast<uint4*>(p.out + ((static_cast<size_t>(w.b) * p.Nq + (live ? n : 0)) * p.Hq + head) * 64);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         float acc[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-        if (T_loc > 0) {
+        if (w.T_loc > 0) {
           uint32_t o[32];
           tmem_ld32(tOl + 32 * half, o);
           tmem_ld_wait();
@@ -491,8 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
         if (cmp_row != nullptr) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            uint4 u = __ldg(cmp_row + 4 * half + i);
-            const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(&u);
+            const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(&cmpv[4 * half + i]);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float2 f2v = __bfloat1622float2(bv[j]);
@@ -504,24 +572,28 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
         if (live) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            uint4 u;
-            u.x = pack_bf16x2(acc[8 * i + 0], acc[8 * i + 1]);
-            u.y = pack_bf16x2(acc[8 * i + 2], acc[8 * i + 3]);
-            u.z = pack_bf16x2(acc[8 * i + 4], acc[8 * i + 5]);
-            u.w = pack_bf16x2(acc[8 * i + 6], acc[8 * i + 7]);
-            dst[4 * half + i] = u;
+            uint4 v;
+            v.x = pack_bf16x2(acc[8 * i + 0], acc[8 * i + 1]);
+            v.y = pack_bf16x2(acc[8 * i + 2], acc[8 * i + 3]);
+            v.z = pack_bf16x2(acc[8 * i + 4], acc[8 * i + 5]);
+            v.w = pack_bf16x2(acc[8 * i + 6], acc[8 * i + 7]);
+            dst[4 * half + i] = v;
           }
         }
       }
+      // O has been read: the next unit's first P*V may overwrite it.
+      tc_fence_before();
+      mbar_arrive(&sm.o_empty[wg]);
       if (live && p.lse != nullptr && T_slc > 0)
-        p.lse[(static_cast<size_t>(b) * p.Nq + n) * p.Hq + head] = m_slc + log2f(l_slc);
+        p.lse[(static_cast<size_t>(w.b) * p.Nq + n) * p.Hq + head] = m_slc + log2f(l_slc);
+      g += w.T;
     }
   }
 
-  MOSAIC_TRACE_AT(traced && (threadIdx.x == 64 || threadIdx.x == 192), 2004 + (threadIdx.x == 192));
+  MOSAIC_TRACE_AT(traced_cta && (threadIdx.x == 128 || threadIdx.x == 256), 2004 + (threadIdx.x == 256));
   tc_fence_before();
   __syncthreads();
-  MOSAIC_TRACE_AT(traced && threadIdx.x == 0, 2001);
+  MOSAIC_TRACE_AT(traced_cta && threadIdx.x == 0, 2001);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -555,6 +627,8 @@ int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
   p.nkb = a.Nk / p.bs;
   p.combine = a.combine;
   p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+  p.qtiles = (a.Nq + kQTile - 1) / kQTile;
+  p.units = a.B * a.Hk * p.qtiles;
 
   // The shared-memory opt-in is a per-device function attribute: set it once per device.
   static bool attr_done[64] = {};
@@ -566,7 +640,13 @@ int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
       return MOSAIC_ERR_CUDA;
     attr_done[dev] = true;
   }
-  dim3 grid((a.Nq + kQTile - 1) / kQTile, a.Hk, a.B);
+  // Persistent: one CTA per SM (TMEM and shared memory allow no more), each
+  // walking work units blockIdx.x, blockIdx.x + gridDim.x, ...
+  static int sm_count[64] = {};
+  if (sm_count[dev] == 0 &&
+      cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  const int grid = p.units < sm_count[dev] ? p.units : sm_count[dev];
   bsa_engine_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
