@@ -61,7 +61,6 @@ constexpr int kBoxBytes = 64 * 128;        // one 64-row x 64-col bf16 box (8 KB
 constexpr int kQTileBytes = 2 * kBoxBytes;  // one M-tile of Q: 128 rows
 constexpr int kThreads = 384;
 constexpr int kMaxSel = 1024;  // max selected blocks per query block
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: keep a stale max while p <= 2^8
 // Of every kPolyDen pairs of scores, the last kPolyNum take the software exp2
 // (FMA pipe) and the others ex2.approx (MUFU), so both pipes share the work.
 #ifndef MOSAIC_POLY_NUM
@@ -157,66 +156,13 @@ __device__ __forceinline__ KeyTile key_tile(const EngineParams& p, const int* se
   return kt;
 }
 
-// Online-softmax step of one 64-key tile; each thread owns one row of the M-tile.
-// Reads the 64 scores from TMEM, updates (m_run, l_run), rescales this row's O
-// accumulator when the running max grows by more than kRescaleThreshold (after
-// waiting for the previous P*V on `o_done`), and writes P = 2^(S*c - m) as 32
-// packed bf16 pairs over the first 32 columns of the S buffer.
-__device__ __forceinline__ bool softmax_tile(uint32_t tS, uint32_t tO, int valid, bool first, float c,
-                                             float& m_run, float& l_run, uint64_t* o_done, uint32_t o_parity,
-                                             volatile int* abort_flag, int* status, int tslot) {
-  uint32_t s[64];
-  tmem_ld32(tS, s);
-  tmem_ld32(tS + 32, s + 32);
-  tmem_ld_wait();
-  reg_fence<64>(s);
-  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 0);
-  if (valid < 64) {
-#pragma unroll
-    for (int i = 0; i < 64; ++i)
-      if (i >= valid) s[i] = __float_as_uint(-INFINITY);
-  }
-  float mx[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float a = fmax3(__uint_as_float(s[j]), __uint_as_float(s[j + 8]), __uint_as_float(s[j + 16]));
-    a = fmax3(a, __uint_as_float(s[j + 24]), __uint_as_float(s[j + 32]));
-    a = fmax3(a, __uint_as_float(s[j + 40]), __uint_as_float(s[j + 48]));
-    mx[j] = fmaxf(a, __uint_as_float(s[j + 56]));
-  }
-  const float rmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7])));
-  const float m_new = fmaxf(m_run, rmax * c);
-  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 1);
-  float m_use = m_run, alpha = 1.0f;
-  bool need = false;
-  if (first) {
-    m_use = m_new;
-  } else if (m_new > m_run + kRescaleThreshold) {
-    need = true;
-    m_use = m_new;
-    alpha = ex2_approx(m_run - m_new);
-  }
-  bool ok = true;
-  if (__any_sync(0xffffffffu, need)) {
-    // Rare path: the previous P*V must have landed in O before O is scaled.
-    ok = bounded_wait(o_done, o_parity, abort_flag, status);
-    tc_fence_after();
-#pragma unroll 1
-    for (int c8 = 0; c8 < 64; c8 += 8) {
-      uint32_t o[8];
-      tmem_ld8(tO + c8, o);
-      tmem_ld_wait();
-      reg_fence<8>(o);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-      tmem_st8(tO + c8, o);
-    }
-  }
-  l_run *= alpha;
+// exp2 of 64 scores against max m, packed in place as 32 bf16 pairs (s[i] <- s[2i],
+// s[2i+1]); returns the fp32 row sum. Of every kPolyDen pairs the last kPolyNum
+// use the software exp2, the others ex2.approx.
+__device__ __forceinline__ float exp_pack_tile(uint32_t (&s)[64], float c, float m) {
   const uint64_t c2 = f2_pack(c, c);
-  const uint64_t nm2 = f2_pack(-m_use, -m_use);
+  const uint64_t nm2 = f2_pack(-m, -m);
   uint64_t acc[4] = {0, 0, 0, 0};
-  // P pairs are packed in place over the scores they came from (s[i] <- s[2i], s[2i+1]).
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nm2);
@@ -233,15 +179,91 @@ __device__ __forceinline__ bool softmax_tile(uint32_t tS, uint32_t tO, int valid
     f2_unpack(e, e0, e1);
     s[i] = pack_bf16x2(e0, e1);
   }
-  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 2);
-  tmem_st32(tS, s);
   float a0, a1, b0, b1;
   f2_unpack(f2_add(acc[0], acc[1]), a0, a1);
   f2_unpack(f2_add(acc[2], acc[3]), b0, b1);
+  return (a0 + a1) + (b0 + b1);
+}
+
+__device__ __forceinline__ void load_scores(uint32_t tS, uint32_t (&s)[64], int valid) {
+  tmem_ld32(tS, s);
+  tmem_ld32(tS + 32, s + 32);
+  tmem_ld_wait();
+  reg_fence<64>(s);
+  if (valid < 64) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      if (i >= valid) s[i] = __float_as_uint(-INFINITY);
+  }
+}
+
+// Online-softmax step of one 64-key tile; each thread owns one row of the M-tile.
+// The common path exponentiates against the running max m_run without looking at
+// this tile's max: the result is exact after the final normalisation as long as
+// no p grows too large, which the tile sum bounds (sum <= 2^14 => every p <= 2^14,
+// far inside bf16/fp32 range). A row whose sum exceeds that (its max grew), the
+// first tile of a branch, and any non-finite sum take the exact path: reload S,
+// take the row max, rescale this row's O accumulator (after the previous P*V has
+// landed, `o_done`) and l, and exponentiate again. P is written as 32 packed
+// bf16 pairs over the first 32 columns of the S buffer.
+__device__ __forceinline__ bool softmax_tile(uint32_t tS, uint32_t tO, int valid, bool first, float c,
+                                             float& m_run, float& l_run, uint64_t* o_done, uint32_t o_parity,
+                                             volatile int* abort_flag, int* status, int tslot) {
+  constexpr float kSumLimit = 16384.0f;
+  uint32_t s[64];
+  load_scores(tS, s, valid);
+  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 0);
+  float sum = 0.f;
+  bool exact = first;
+  if (!first) {
+    sum = exp_pack_tile(s, c, m_run);
+    exact = !(sum <= kSumLimit);  // also catches NaN / inf
+  }
+  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 1);
+  bool ok = true;
+  if (__any_sync(0xffffffffu, exact)) {
+    // Exact path for the rows that need it (the warp runs it together).
+    load_scores(tS, s, valid);
+    float mx[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a = fmax3(__uint_as_float(s[j]), __uint_as_float(s[j + 8]), __uint_as_float(s[j + 16]));
+      a = fmax3(a, __uint_as_float(s[j + 24]), __uint_as_float(s[j + 32]));
+      a = fmax3(a, __uint_as_float(s[j + 40]), __uint_as_float(s[j + 48]));
+      mx[j] = fmaxf(a, __uint_as_float(s[j + 56]));
+    }
+    const float rmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7])));
+    const float m_new = first ? rmax * c : fmaxf(m_run, rmax * c);
+    const float alpha = first ? 1.0f : ex2_approx(m_run - m_new);
+    const bool rescale = exact && !first;
+    if (__any_sync(0xffffffffu, rescale)) {
+      // The previous P*V must have landed in O before O is scaled.
+      ok = bounded_wait(o_done, o_parity, abort_flag, status);
+      tc_fence_after();
+#pragma unroll 1
+      for (int c8 = 0; c8 < 64; c8 += 8) {
+        uint32_t o[8];
+        tmem_ld8(tO + c8, o);
+        tmem_ld_wait();
+        reg_fence<8>(o);
+        const float f = rescale ? alpha : 1.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+        tmem_st8(tO + c8, o);
+      }
+    }
+    if (exact) {
+      if (!first) l_run *= alpha;
+      m_run = m_new;
+    }
+    const float sum2 = exp_pack_tile(s, c, m_run);  // rows not on the exact path recompute the same values
+    if (exact) sum = sum2;
+  }
+  tmem_st32(tS, s);
+  MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 2);
   tmem_st_wait();
   MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 3);
-  l_run += (a0 + a1) + (b0 + b1);
-  m_run = m_use;
+  l_run += sum;
   return ok;
 }
 

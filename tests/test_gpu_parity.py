@@ -283,3 +283,39 @@ def test_host_errors_raise():
         M.mosaic_attn_func(q, k, v, w, 100, 64, 4, False)        # N % bas
     with pytest.raises(ValueError):
         M.mosaic_sparse_attn(x["q"], x["k"], x["v"], torch.zeros(1, 12, 1, 2, dtype=torch.long), 64)  # CPU
+
+
+@pytest.mark.parametrize("direction", ["growing", "shrinking"])
+def test_running_max_drifts(direction):
+    """Key magnitudes ramp along every window (and so across the selected blocks),
+    so the running row max drifts between tiles by several log2 units: stale-max
+    exponentials (growing) and deep underflow against a high early max (shrinking)."""
+    B, N, Hq, Hk = 1, 3072, 8, 2
+    x = O.make_inputs(B, N, Hq, Hk, seed=21, rope=False)
+    pos = torch.arange(N) % 1024
+    ramp = 1.0 + 2.0 * (pos / 1023.0) if direction == "growing" else 3.0 - 2.0 * (pos / 1023.0)
+    k = (x["k"].float() * ramp.view(1, N, 1, 1)).bfloat16()
+    status = mops.status_buffer(DEV)
+    out, idx = M.mosaic_attn_func(*cuda(x["q"], k, x["v"], x["w"]), 1024, 64, 8, False, return_block_indices=True,
+                                  status=status)
+    torch.cuda.synchronize()
+    assert mops.check_status(status) == 0
+    ref = O.mosaic_attn_func(x["q"], k, x["v"], x["w"], 1024, 64, 8, False, block_indices=idx.cpu())
+    close(out, ref)
+
+
+def test_score_spike_forces_exact_path():
+    """One key per window (position 1000) is scaled by 60, so for many queries its
+    score exceeds everything before it by far more than the 2^14 budget of the
+    stale-max path: the optimistic exponentials overflow and only the exact
+    re-exponentiation with the O rescale gives the (near one-hot) right answer."""
+    B, N, Hq, Hk = 1, 2048, 4, 1
+    x = O.make_inputs(B, N, Hq, Hk, seed=22, rope=False)
+    k = x["k"].float()
+    k[:, torch.arange(N) % 1024 == 1000] *= 60.0
+    k = k.bfloat16()
+    status = mops.status_buffer(DEV)
+    out = M.block_attention(*cuda(x["q"], k, x["v"]), 1024, status=status)
+    torch.cuda.synchronize()
+    assert mops.check_status(status) == 0
+    close(out, O.block_attention(x["q"], k, x["v"], 1024))
