@@ -70,6 +70,14 @@ MOSAIC_API int mosaic_abi_version(void);
 /* Human-readable text for a MOSAIC_ERR_* code. */
 MOSAIC_API const char* mosaic_error_string(int code);
 
+/* Self-test of the device-side failure detection used by every pipeline kernel:
+ * a single warp waits (up to timeout_us microseconds) on a barrier that nothing
+ * arrives on; the bounded wait gives up, OR-s MOSAIC_STATUS_TIMEOUT into *status
+ * and writes result[0] = 0 (wait succeeded: 1) and result[1] = 1 (abort flag
+ * raised). Both pointers are device memory. No counterpart in the reference,
+ * which has no failure detection. */
+MOSAIC_API int mosaic_selftest_wait_timeout(int* status, int* result, int timeout_us, void* stream);
+
 /* Scratch bytes mosaic_bsa_fwd needs for these sizes (pooled q/k/v, coarse
  * attention output, block indices and, with RoPE, rotated q/k). */
 MOSAIC_API size_t mosaic_bsa_workspace_bytes(int batch, int seq_len, int num_q_heads, int num_kv_heads, int head_dim,

@@ -40,6 +40,7 @@ class MosaicBsaArgs(ctypes.Structure):
 SIGNATURES = {
     "mosaic_abi_version": ([], _i),
     "mosaic_error_string": ([_i], ctypes.c_char_p),
+    "mosaic_selftest_wait_timeout": ([_vp, _vp, _i, _vp], _i),
     "mosaic_bsa_workspace_bytes": ([_i, _i, _i, _i, _i, _i, _i, _i], _sz),
     "mosaic_bsa_fwd": ([ctypes.POINTER(MosaicBsaArgs), _vp], _i),
     "mosaic_bsa_fwd_noalloc": ([ctypes.POINTER(MosaicBsaArgs), _vp], _i),

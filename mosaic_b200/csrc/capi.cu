@@ -35,6 +35,26 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 
 namespace {
 
+// Self-test of the bounded-wait machinery every pipeline kernel uses: one warp
+// waits, with a short limit, on an mbarrier that nothing ever arrives on. The
+// wait must give up, raise the CTA abort flag and record MOSAIC_STATUS_TIMEOUT;
+// the kernel then returns normally (no trap, no hang).
+__global__ void selftest_wait_kernel(int* status, uint64_t timeout_ns, int* result) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = bounded_wait(&bar, 0, &abort_flag, status, timeout_ns);
+    result[0] = ok ? 1 : 0;
+    result[1] = abort_flag;
+  }
+}
+
 constexpr int kMaxTopK = 128;    // topk.cu kMaxK
 constexpr int kMaxSelect = 1024;  // bsa_engine.cu kMaxSel
 
@@ -78,6 +98,14 @@ using namespace mosaic;
 extern "C" {
 
 int mosaic_abi_version(void) { return 1; }
+
+int mosaic_selftest_wait_timeout(int* status, int* result, int timeout_us, void* stream) {
+  if (status == nullptr || result == nullptr || timeout_us <= 0 || timeout_us > 10000000)
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<uint64_t>(timeout_us) * 1000ull, result);
+  return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
 
 const char* mosaic_error_string(int code) {
   switch (code) {

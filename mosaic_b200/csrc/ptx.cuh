@@ -59,13 +59,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // exceeds kWaitTimeoutNs; in the latter case it raises the flag itself and
 // records MOSAIC_STATUS_TIMEOUT in `status` (which may be null).
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                             int* status) {
+                                             int* status, uint64_t timeout_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > timeout_ns) {
       *abort_flag = 1;
       if (status) atomicOr(status, MOSAIC_STATUS_TIMEOUT);
       return false;
