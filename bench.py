@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the Mosaic block-sparse attention forward on B200.
 
-Workload ("S1"): one mosaic_attn_func forward at Nside 64 —
+Default workload ("S1", the stage-1 attention of the headline metric): one
+mosaic_attn_func forward at Nside 64 —
 B=1 per GPU, N=49152 tokens, 12 query / 3 kv heads, head_dim 64, sparse block 64,
 top-k 24, local window 1024, bf16, synthetic q/k/v ~ N(0,1) and gates
 sigmoid(N(0,1)). A step = the four kernels of the op on one member's inputs:
@@ -11,11 +12,15 @@ attention with the gated combine. Ensemble members are independent, so with
 
 Timing: W untimed warm-up steps, then K steps of `mosaic_bsa_fwd` (the C-ABI
 entry point of the whole op) between barrier + synchronize, CUDA events on the
-launching stream, max over ranks. Three input sets (3 x 117 MB > 126 MB L2)
-rotate so no step reads inputs left in L2 by the previous one. Per-kernel
+launching stream, max over ranks. Several input sets (S1: 4 x 117 MB against the
+126 MB L2) rotate so no step reads inputs left in L2 by the previous ones. Per-kernel
 durations come from a second loop of K steps right after the timed one that
 launches the same kernels one entry point at a time with CUDA events between
 them; `roofline` uses the fused kernel (c) from that loop.
+
+--workload S2 | BN | X128 | X256 runs the other configurations (deeper U-Net stages,
+Nside 128 / 256 stress cases) instead; X128 / X256 also time cuDNN dense SDPA on the
+same inputs (`dense_sdpa`).
 
 `--impl reference` times the reference algorithm on the host cores instead: the
 reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
@@ -40,6 +45,27 @@ sys.path.insert(0, ROOT)
 METRIC = "BSA fwd tokens/s/GPU @Nside64 (N=49152,12h,d64,k24); 24-member step/s @1-8 GPU"
 UNIT = "tokens/s"
 S1 = dict(B=1, N=49152, Hq=12, Hk=3, D=64, bs=64, K=24, bas=1024)
+# The metric's configurations as bench workloads. S1 is the default and the headline; the
+# others are opt-in (--workload) lines: S2 / BN are the deeper U-Net stages, X128 /
+# X256 the resolution-scaling stress cases, which also time cuDNN dense SDPA on the
+# same inputs.
+WORKLOADS = {
+    "S1": dict(S1, nside=64),
+    "S2": dict(B=1, N=12288, Hq=16, Hk=4, D=64, bs=64, K=20, bas=1024, nside=32),
+    "BN": dict(B=1, N=3072, Hq=20, Hk=5, D=64, bs=64, K=20, bas=1024, nside=16),
+    "X128": dict(B=1, N=196608, Hq=12, Hk=3, D=64, bs=64, K=24, bas=1024, nside=128),
+    "X256": dict(B=1, N=786432, Hq=12, Hk=3, D=64, bs=64, K=24, bas=1024, nside=256),
+}
+# dram__bytes_read.sum + dram__bytes_write.sum of one bsa_engine_kernel attend launch
+# at S1, from an `ncu --set full --clock-control none -k regex:bsa_engine` capture of
+# this script (--steps 3 --warmup 3 --no-e2e --no-cpu-baseline); updated with the kernel.
+ATTEND_TRAFFIC_BYTES = {"S1": 127_683_328 + 48_043_008}
+L2_BYTES = 126 * 2**20
+
+
+def describe(name, c):
+    return (f"{name} mosaic_attn_func forward, Nside {c['nside']}: N={c['N']}, {c['Hq']}/{c['Hk']} heads, "
+            f"d{c['D']}, sparse block {c['bs']}, top-k {c['K']}, window {c['bas']}; one ensemble member per GPU")
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 MEMBERS = 24
 
@@ -50,6 +76,7 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="S1")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     return p.parse_args()
@@ -154,22 +181,30 @@ def cpu_sample(c, windows, reps, warm=1):
     return tok * reps / sum(times), torch.get_num_threads(), sum(times)
 
 
+def sample_windows(c, count):
+    """`count` local windows spread over the sequence (first and last included)."""
+    nw = c["N"] // c["bas"]
+    count = min(count, nw)
+    return sorted({round(i * (nw - 1) / max(count - 1, 1)) for i in range(count)})
+
+
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    c = S1
-    windows = [0, 17, 30, 47]
+    name = args.workload
+    c = WORKLOADS[name]
+    windows = sample_windows(c, 4)
     value, cores, secs = cpu_sample(c, windows, reps=args.steps, warm=args.warmup)
-    sample = (f"per step: oracle port (fp32 torch) of mosaic_attn_func on S1 inputs, global pooling/coarse "
-              f"attention/top-k over all 49152 tokens, local + selected branches for 4 of 48 windows "
-              f"({len(windows) * c['bas']} query tokens); {args.steps} steps after {args.warmup} warm-up")
+    sample = (f"per step: oracle port (fp32 torch) of mosaic_attn_func on {name} inputs, global pooling/coarse "
+              f"attention/top-k over all {c['N']} tokens, local + selected branches for {len(windows)} of "
+              f"{c['N'] // c['bas']} windows ({len(windows) * c['bas']} query tokens); {args.steps} steps after "
+              f"{args.warmup} warm-up")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "S1 mosaic_attn_func forward, Nside 64 (N=49152, 12/3 heads, d64, bs64, k24, "
-                               "window 1024), CPU sample", "B": c["B"], "N": c["N"]},
+        "config": {"workload": describe(name, c) + " (CPU sample)", "B": c["B"], "N": c["N"]},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -238,6 +273,38 @@ STAGE_NAMES = ["pool", "cmp_attn", "topk", "attend"]
 LAUNCHES_PER_STEP = 4
 
 
+def dense_sdpa(x, c, reps=3):
+    """Times torch SDPA on the cuDNN backend (dense, non-causal) over the same q, k, v:
+    the dense attention that block-sparse attention replaces. k and v are expanded to
+    the query heads beforehand (outside the timing), so cuDNN runs plain MHA."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    import torch.nn.functional as F
+
+    G = c["Hq"] // c["Hk"]
+    q = x["q"].transpose(1, 2).contiguous()
+    k = x["k"].repeat_interleave(G, dim=2).transpose(1, 2).contiguous()
+    v = x["v"].repeat_interleave(G, dim=2).transpose(1, 2).contiguous()
+    out = None
+    for backend, name in ((SDPBackend.CUDNN_ATTENTION, "cudnn"), (SDPBackend.FLASH_ATTENTION, "flash")):
+        try:
+            with sdpa_kernel(backend):
+                out = F.scaled_dot_product_attention(q, k, v)
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(reps):
+                    out = F.scaled_dot_product_attention(q, k, v)
+                b.record()
+                torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / reps
+            flop = 4 * c["B"] * c["N"] * c["N"] * c["Hq"] * c["D"]
+            del q, k, v, out
+            return {"backend": name, "ms": ms, "tflops": flop / (ms / 1000) / 1e12, "reps": reps}
+        except RuntimeError as e:  # backend not available for this shape: try the next one
+            err = str(e).splitlines()[0][:120]
+    return {"backend": None, "error": err}
+
+
 def b200_arm(args):
     from mosaic_b200 import _lib
     import mosaic_b200 as M
@@ -254,13 +321,17 @@ def b200_arm(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     lib = _lib.load()
-    c = S1
+    name = args.workload
+    c = WORKLOADS[name]
     B, N, Hq, Hk, D = c["B"], c["N"], c["Hq"], c["Hk"], c["D"]
 
-    # three input sets per rank (member = rank), rotated so inputs are never L2-resident
+    # input sets per rank (member = rank), rotated so that a set is re-read only after
+    # more than 2 x L2 of other inputs went through the cache
+    set_bytes = B * N * (Hq + 2 * Hk) * D * 2 + 3 * B * N * Hq * 2
+    nsets = max(2, min(32, -(-3 * L2_BYTES // set_bytes)))
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     sets = []
-    for _ in range(3):
+    for _ in range(nsets):
         sets.append(dict(
             q=torch.randn(B, N, Hq, D, generator=g, device=dev).bfloat16(),
             k=torch.randn(B, N, Hk, D, generator=g, device=dev).bfloat16(),
@@ -274,7 +345,7 @@ def b200_arm(args):
             dist.barrier()
 
     for i in range(args.warmup):
-        st.run_fused(sets[i % 3], stream)
+        st.run_fused(sets[i % nsets], stream)
     torch.cuda.synchronize()
     barrier()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -282,7 +353,7 @@ def b200_arm(args):
         torch.cuda.synchronize()
         t_start.record(stream)
         for i in range(args.steps):
-            st.run_fused(sets[i % 3], stream)
+            st.run_fused(sets[i % nsets], stream)
         t_end.record(stream)
         torch.cuda.synchronize()
     barrier()
@@ -290,7 +361,7 @@ def b200_arm(args):
     # per-kernel attribution: the same kernels launched one entry point at a time
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     for i in range(args.steps):
-        st.run(sets[i % 3], stream, events[i])
+        st.run(sets[i % nsets], stream, events[i])
     torch.cuda.synchronize()
     stage_ms = [sum(events[i][s].elapsed_time(events[i][s + 1]) for i in range(args.steps)) / args.steps
                 for s in range(4)]
@@ -337,15 +408,24 @@ def b200_arm(args):
             e_ms = float(t.item())
         e2e = {"value": world * B * N * n_e2e / (e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": n_e2e}
+        del host, out_host, dbuf
+
+    sdpa = None
+    if name.startswith("X") and rank == 0:
+        sdpa = dense_sdpa(sets[0], c)
+        if sdpa.get("ms"):
+            sdpa["bsa_speedup"] = sdpa["ms"] / (ms / args.steps)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        windows = [0, 9, 17, 25, 30, 38, 41, 47]
-        v_cpu, cores, secs = cpu_sample(c, windows, reps=3)
+        windows = sample_windows(c, 8)
+        reps = 3 if N <= 49152 else 1
+        v_cpu, cores, secs = cpu_sample(c, windows, reps=reps)
         cpu = {"value": v_cpu, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"oracle port (fp32 torch) of mosaic_attn_func on S1: global pooling/coarse attention/"
-                         f"top-k over all tokens, local + selected branches for {len(windows)} of 48 windows "
-                         f"({len(windows) * c['bas']} query tokens), 3 timed reps after 1 warm-up, {secs:.1f} s"}
+               "sample": f"oracle port (fp32 torch) of mosaic_attn_func on {name}: global pooling/coarse "
+                         f"attention/top-k over all tokens, local + selected branches for {len(windows)} of "
+                         f"{N // c['bas']} windows ({len(windows) * c['bas']} query tokens), {reps} timed rep(s) "
+                         f"after 1 warm-up, {secs:.1f} s"}
 
     hbm, tf, src = peaks()
     t_att = stage_ms[3] / 1000.0
@@ -354,15 +434,14 @@ def b200_arm(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "S1 mosaic_attn_func forward, Nside 64: N=49152, 12/3 heads, d64, sparse block 64, "
-                               "top-k 24, window 1024; one ensemble member per GPU",
+        "config": {"workload": describe(name, c),
                    "B_per_gpu": B, "N": N, "Hq": Hq, "Hk": Hk, "head_dim": D, "sparse_block": c["bs"],
                    "topk": c["K"], "window": c["bas"], "parallelism": f"members x{world}",
-                   "l2": "3 rotating input sets, 351 MB > 126 MB L2"},
+                   "l2": f"{nsets} rotating input sets of {set_bytes / 1e6:.0f} MB (L2 126 MB)"},
         "ensemble_step_per_s": value / (MEMBERS * N),
         "roofline": {"bound": "tensor", "kernel": "bsa_engine_kernel (c: local + selected + gated combine)",
                      "achieved": achieved, "peak": tf, "unit": "TFLOP/s", "frac": achieved / tf,
-                     "peak_source": src + " bf16_tflops (burst)", "traffic": None,
+                     "peak_source": src + " bf16_tflops (burst)", "traffic": ATTEND_TRAFFIC_BYTES.get(name),
                      "flop_per_launch": flops_attend(c)},
         "kernels_us": {n: 1000 * t for n, t in zip(STAGE_NAMES, stage_ms)},
         "pool_hbm": {"achieved_gbs": bytes_pool(c) / (stage_ms[0] / 1000) / 1e9, "peak_gbs": hbm,
@@ -374,6 +453,8 @@ def b200_arm(args):
         "e2e": e2e,
         "cpu_baseline": cpu,
     }
+    if sdpa is not None:
+        line["dense_sdpa"] = sdpa
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:

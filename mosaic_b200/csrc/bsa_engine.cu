@@ -1,7 +1,9 @@
 // Fused block-sparse attention engine for sm_100a (tcgen05 + TMEM + TMA).
 //
-// One CTA owns one (batch b, kv head h, 64-query tile) and all G = 4 query heads
-// of that kv group. The four heads are packed into two M = 128 MMA tiles
+// A work unit is one (batch b, kv head h, 64-query tile) with all G = 4 query heads
+// of that kv group; the grid is persistent (one CTA per SM) and CTA i walks units
+// i, i + grid, ... with Q double-buffered so that the next unit's Q loads while
+// the current one finishes. The four heads are packed into two M = 128 MMA tiles
 // ("M-tiles": rows 0-63 = head 4h+2m, rows 64-127 = head 4h+2m+1), so every K/V
 // tile that TMA brings into shared memory is used by 4 heads x 64 queries.
 // Keys stream in tiles of 64 (one TMA box each for K and V, 8-stage ring):
