@@ -5,8 +5,9 @@ Public API (same signatures as the reference's ops.py / primitives.py):
     mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size,
                      sparse_block_count, block_attn_only, no_compression=False)
     attn_topk(q, k, block_count), block_attention(q, k, v, block_size)
-plus get_healpix_grid / rope_tables for the RoPE tables and `ensemble` for
-member-sharded multi-GPU runs.
+plus get_healpix_grid / rope_tables for the RoPE tables, `ensemble` for
+member-sharded multi-GPU runs and `streaming.StreamedAttention` for host-resident
+batches with their PCIe copies overlapped with the attention.
 """
 from .healpix import get_healpix_grid, healpix_rope_tables, pix2ang_nest, rope_tables
 from .ops import mosaic_sparse_attn, mosaic_sparse_attn_with_lse
