@@ -18,9 +18,10 @@ durations come from a second loop of K steps right after the timed one that
 launches the same kernels one entry point at a time with CUDA events between
 them; `roofline` uses the fused kernel (c) from that loop.
 
---workload S2 | BN | X128 | X256 runs the other configurations (deeper U-Net stages,
-Nside 128 / 256 stress cases) instead; X128 / X256 also time cuDNN dense SDPA on the
-same inputs (`dense_sdpa`).
+--workload S1_bas64 | S1_bs128 | S2 | BN | X128 | X256 runs the other configurations
+(S1 with a 64-token local window or the reference preset's 128-token blocks, the
+deeper U-Net stages, the Nside 128 / 256 stress cases) instead; X128 / X256 also
+time cuDNN dense SDPA on the same inputs (`dense_sdpa`).
 
 `--impl reference` times the reference algorithm on the host cores instead: the
 reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
@@ -51,6 +52,8 @@ S1 = dict(B=1, N=49152, Hq=12, Hk=3, D=64, bs=64, K=24, bas=1024)
 # same inputs.
 WORKLOADS = {
     "S1": dict(S1, nside=64),
+    "S1_bas64": dict(S1, bas=64, nside=64),
+    "S1_bs128": dict(S1, bs=128, nside=64),
     "S2": dict(B=1, N=12288, Hq=16, Hk=4, D=64, bs=64, K=20, bas=1024, nside=32),
     "BN": dict(B=1, N=3072, Hq=20, Hk=5, D=64, bs=64, K=20, bas=1024, nside=16),
     "X128": dict(B=1, N=196608, Hq=12, Hk=3, D=64, bs=64, K=24, bas=1024, nside=128),

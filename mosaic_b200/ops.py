@@ -103,8 +103,13 @@ class MosaicAttnFunction(torch.autograd.Function):
 
 
 def mosaic_sparse_attn(q, k, v, block_indices, block_size, softmax_scale=None):
-    """Selected-block attention forward (ops.py:557-566)."""
+    """Selected-block attention forward (ops.py:557-566). Under torch.compile the
+    call becomes the opaque custom op torch.ops.mosaic_b200.sparse_attn."""
     softmax_scale = q.shape[-1] ** -0.5 if softmax_scale is None else softmax_scale
+    if torch.compiler.is_compiling():
+        from . import torch_ops  # noqa: F401  (registers the op)
+
+        return torch.ops.mosaic_b200.sparse_attn(q, k, v, block_indices, int(block_size), float(softmax_scale))
     return MosaicAttnFunction.apply(q, k, v, block_indices, block_size, softmax_scale)
 
 

@@ -51,7 +51,23 @@ def mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_s
       o_slc = attention over the sparse_block_count blocks of highest pooled score.
     `block_attn_only` returns o_ba; `no_compression` drops o_cmp and renormalises
     (w0, w2); sparse_block_count == 0 drops o_slc and renormalises (w0, w1).
+    Under torch.compile the call becomes the opaque custom op
+    torch.ops.mosaic_b200.attn_func (see torch_ops.py).
     """
+    if (torch.compiler.is_compiling() and rope_tables is None and not return_block_indices and status is None):
+        from . import torch_ops  # noqa: F401  (registers the op)
+
+        return torch.ops.mosaic_b200.attn_func(q, k, v, weight_ba_cmp_slc, int(block_attn_size),
+                                               int(sparse_block_size), int(sparse_block_count),
+                                               bool(block_attn_only), bool(no_compression))
+    return _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size,
+                                   sparse_block_count, block_attn_only, no_compression, rope_tables=rope_tables,
+                                   return_block_indices=return_block_indices, status=status)
+
+
+def _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,
+                            block_attn_only, no_compression=False, *, rope_tables=None, return_block_indices=False,
+                            status=None):
     _require_cuda(q, k, v)
     _check_qkv(q, k, v)
     B, N, Hq, D = q.shape

@@ -48,3 +48,4 @@ def test_streamed_shape_change():
 def test_depth_must_allow_overlap():
     with pytest.raises(ValueError):
         StreamedAttention("cuda", 1024, 64, 8, depth=1)
+
