@@ -266,6 +266,7 @@ int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indice
   TopkLaunch a;
   a.q_cmp = q_cmp; a.k_cmp = k_cmp; a.idx = block_indices;
   a.B = batch; a.nb = num_blocks; a.Hq = num_q_heads; a.Hk = num_kv_heads; a.K = block_count;
+  a.status = nullptr;
   a.overlap_previous = false;
   return launch_topk(a, static_cast<cudaStream_t>(stream));
 }
@@ -346,6 +347,7 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
     TopkLaunch t;
     t.q_cmp = q_cmp; t.k_cmp = k_cmp; t.idx = idx;
     t.B = B; t.nb = nb; t.Hq = Hq; t.Hk = Hk; t.K = K;
+    t.status = A.status;
     t.overlap_previous = want_cmp;  // runs beside the coarse attention (both only read the pooled tensors)
     if ((rc = launch_topk(t, st))) return rc;
   }

@@ -63,6 +63,7 @@ struct TopkLaunch {
   const void* k_cmp;  // [B, nb, Hk, 64] bf16
   int64_t* idx;       // [B, nb, Hk, K]
   int B, nb, Hq, Hk, K;
+  int* status;  // device status word or null (timeouts of the tensor-core variant)
   // Launch with programmatic stream serialization, so that the kernel may start
   // while the previous kernel of the stream (which must not produce this
   // kernel's inputs) is still running.
@@ -72,6 +73,9 @@ struct TopkLaunch {
 int launch_engine(const EngineLaunch& a, cudaStream_t stream);
 int launch_pool(const PoolLaunch& a, cudaStream_t stream);
 int launch_topk(const TopkLaunch& a, cudaStream_t stream);
+// The tensor-core top-k (topk_tc.cu) for G <= 4 and K <= 32; launch_topk picks it.
+bool topk_tc_supported(const TopkLaunch& a);
+int launch_topk_tc(const TopkLaunch& a, cudaStream_t stream);
 
 // Encodes a 2D bf16 tensor map over `rows` x `cols` elements (row pitch = cols),
 // 64x64 boxes, 128-byte swizzle. Returns 0 on success.

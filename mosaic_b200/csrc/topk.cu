@@ -37,6 +37,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kChunk = 1024;  // key blocks scored per pass
 constexpr int kMaxG = 8;
 constexpr int kMaxK = 128;
+constexpr int kTcMinBlocks = 2048;
 
 struct TopkParams {
   const __nv_bfloat16* q_cmp;
@@ -277,6 +278,9 @@ int launch_g(const TopkParams& p, cudaStream_t stream, bool overlap) {
 }  // namespace
 
 int launch_topk(const TopkLaunch& a, cudaStream_t stream) {
+  // The score matrix grows as nb^2: from a few thousand blocks on, the tensor-core
+  // kernel (topk_tc.cu) wins; below, this one's 16-row CTAs fill the GPU better.
+  if (a.B > 0 && a.nb >= kTcMinBlocks && topk_tc_supported(a)) return launch_topk_tc(a, stream);
   TopkParams p;
   p.q_cmp = static_cast<const __nv_bfloat16*>(a.q_cmp);
   p.k_cmp = static_cast<const __nv_bfloat16*>(a.k_cmp);

@@ -60,7 +60,9 @@ def test_rope_pool_bit_exact(cfg):
 
 # ----------------------------------------------------------------------------- (b) top-k
 @pytest.mark.parametrize("cfg", [(1, 48, 4, 1, 8), (2, 192, 16, 4, 20), (1, 768, 12, 3, 24), (1, 1536, 8, 2, 64),
-                                 (1, 3072, 12, 3, 24)])
+                                 # from 2048 blocks on the tensor-core kernel runs: partial key tiles and
+                                 # row tiles, G = 4 / 2 / 1, best-list sizes 8 / 24 / 32
+                                 (1, 3072, 12, 3, 24), (1, 2600, 8, 4, 32), (2, 2100, 4, 4, 5), (1, 2049, 4, 1, 17)])
 def test_topk_matches_oracle(cfg):
     B, nb, Hq, Hk, K = cfg
     g = torch.Generator().manual_seed(nb)
@@ -75,11 +77,12 @@ def test_topk_matches_oracle(cfg):
     assert (sc[..., 1:] - sc[..., :-1] <= 2 ** -7 * sc[..., :-1].abs() + 1e-6).all()
 
 
-def test_topk_ties_go_to_lower_index():
-    qc = torch.zeros(1, 64, 4, 64).bfloat16()
-    kc = torch.zeros(1, 64, 1, 64).bfloat16()  # every score is 0: one big tie
+@pytest.mark.parametrize("nb", [64, 2112])
+def test_topk_ties_go_to_lower_index(nb):
+    qc = torch.zeros(1, nb, 4, 64).bfloat16()
+    kc = torch.zeros(1, nb, 1, 64).bfloat16()  # every score is 0: one big tie
     idx = M.attn_topk(*cuda(qc, kc), 8).cpu()
-    assert torch.equal(idx, torch.arange(8).expand(1, 64, 1, 8))
+    assert torch.equal(idx, torch.arange(8).expand(1, nb, 1, 8))
 
 
 @pytest.mark.parametrize("name", GU.fixture_names())
