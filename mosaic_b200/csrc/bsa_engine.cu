@@ -161,10 +161,16 @@ __device__ __forceinline__ KeyTile key_tile(const EngineParams& p, const int* se
 // exp2 of 64 scores against max m, packed in place as 32 bf16 pairs (s[i] <- s[2i],
 // s[2i+1]); returns the fp32 row sum. Of every kPolyDen pairs the last kPolyNum
 // use the software exp2, the others ex2.approx.
+#ifndef MOSAIC_NACC
+#define MOSAIC_NACC 8
+#endif
 __device__ __forceinline__ float exp_pack_tile(uint32_t (&s)[64], float c, float m) {
   const uint64_t c2 = f2_pack(c, c);
   const uint64_t nm2 = f2_pack(-m, -m);
-  uint64_t acc[4] = {0, 0, 0, 0};
+  constexpr int kAcc = MOSAIC_NACC;  // independent partial sums (packed pairs)
+  uint64_t acc[kAcc];
+#pragma unroll
+  for (int i = 0; i < kAcc; ++i) acc[i] = 0;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nm2);
@@ -176,15 +182,18 @@ __device__ __forceinline__ float exp_pack_tile(uint32_t (&s)[64], float c, float
       f2_unpack(x, x0, x1);
       e = f2_pack(ex2_approx(x0), ex2_approx(x1));
     }
-    acc[i & 3] = f2_add(acc[i & 3], e);
+    acc[i % kAcc] = f2_add(acc[i % kAcc], e);
     float e0, e1;
     f2_unpack(e, e0, e1);
     s[i] = pack_bf16x2(e0, e1);
   }
-  float a0, a1, b0, b1;
-  f2_unpack(f2_add(acc[0], acc[1]), a0, a1);
-  f2_unpack(f2_add(acc[2], acc[3]), b0, b1);
-  return (a0 + a1) + (b0 + b1);
+#pragma unroll
+  for (int w = kAcc / 2; w > 0; w /= 2)
+#pragma unroll
+    for (int i = 0; i < w; ++i) acc[i] = f2_add(acc[i], acc[i + w]);
+  float a0, a1;
+  f2_unpack(acc[0], a0, a1);
+  return a0 + a1;
 }
 
 __device__ __forceinline__ void load_scores(uint32_t tS, uint32_t (&s)[64], int valid) {
