@@ -156,6 +156,27 @@ MOSAIC_API int mosaic_cmp_attn_fwd(const void* q_cmp, const void* k_cmp, const v
 MOSAIC_API int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indices, int batch, int num_blocks,
                      int num_q_heads, int num_kv_heads, int head_dim, int block_count, void* stream);
 
+/* Scratch bytes mosaic_sparse_attn_bwd needs for these sizes (row dot products
+ * D = rowsum(out * grad_out) and the inverted block index). */
+MOSAIC_API size_t mosaic_sparse_attn_bwd_workspace_bytes(int batch, int seq_len, int num_q_heads, int num_kv_heads,
+                                                         int head_dim, int block_size, int block_count);
+
+/* Backward of mosaic_sparse_attn_fwd: given the forward's out and lse (log2 units,
+ * as mosaic_sparse_attn_fwd writes it) and grad_out, writes grad_q [B,N,Hq,64],
+ * grad_k and grad_v [B,N,Hk,64] (bf16, every element written). grad_q sums over
+ * every selection of the query block (duplicates count twice, as in the forward);
+ * grad_k / grad_v sum over the distinct query blocks that selected each kv block.
+ * Replaces ops.mosaic_attn_bwd (ops.py:436-507) with its kernels
+ * mosaic_attn_bwd_q_kernel (ops.py:184-274), mosaic_block_mask (ops.py:277-297)
+ * and mosaic_attn_bwd_kv_kernel (ops.py:305-433), behind
+ * ops.MosaicAttnFunction.backward (ops.py:542-554). */
+MOSAIC_API int mosaic_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* out,
+                                      const void* grad_out, const float* lse, const int64_t* block_indices,
+                                      void* grad_q, void* grad_k, void* grad_v, void* workspace,
+                                      size_t workspace_bytes, int* status, int batch, int seq_len, int num_q_heads,
+                                      int num_kv_heads, int head_dim, int block_size, int block_count,
+                                      float softmax_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,7 +1,8 @@
-"""mosaic_b200: B200-native (sm_100a) block-sparse attention forward of Mosaic.
+"""mosaic_b200: B200-native (sm_100a) block-sparse attention of Mosaic.
 
 Public API (same signatures as the reference's ops.py / primitives.py):
     mosaic_sparse_attn(q, k, v, block_indices, block_size, softmax_scale=None)
+        (differentiable in q, k, v; mosaic_attn_fwd / mosaic_attn_bwd are its halves)
     mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size,
                      sparse_block_count, block_attn_only, no_compression=False)
     attn_topk(q, k, block_count), block_attention(q, k, v, block_size)
@@ -10,10 +11,10 @@ member-sharded multi-GPU runs and `streaming.StreamedAttention` for host-residen
 batches with their PCIe copies overlapped with the attention.
 """
 from .healpix import get_healpix_grid, healpix_rope_tables, pix2ang_nest, rope_tables
-from .ops import mosaic_sparse_attn, mosaic_sparse_attn_with_lse
+from .ops import mosaic_attn_bwd, mosaic_attn_fwd, mosaic_sparse_attn, mosaic_sparse_attn_with_lse
 from .primitives import attn_topk, block_attention, block_pool, cmp_attention, mosaic_attn_func
 
 __all__ = [
-    "mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "mosaic_attn_func", "attn_topk", "block_attention",
+    "mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "mosaic_attn_fwd", "mosaic_attn_bwd", "mosaic_attn_func", "attn_topk", "block_attention",
     "block_pool", "cmp_attention", "get_healpix_grid", "healpix_rope_tables", "pix2ang_nest", "rope_tables",
 ]

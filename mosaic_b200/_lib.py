@@ -50,6 +50,8 @@ SIGNATURES = {
     "mosaic_block_pool": ([_vp] * 10 + [_i] * 6 + [_vp], _i),
     "mosaic_cmp_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp], _i),
     "mosaic_attn_topk": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp], _i),
+    "mosaic_sparse_attn_bwd_workspace_bytes": ([_i] * 7, _sz),
+    "mosaic_sparse_attn_bwd": ([_vp] * 10 + [_vp, _sz, _vp] + [_i] * 7 + [_f, _vp], _i),
 }
 
 EXPECTED_ABI_VERSION = 1

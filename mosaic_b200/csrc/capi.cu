@@ -369,4 +369,46 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
   return launch_engine(e, st);
 }
 
+
+size_t mosaic_sparse_attn_bwd_workspace_bytes(int batch, int seq_len, int num_q_heads, int num_kv_heads,
+                                              int head_dim, int block_size, int block_count) {
+  (void)head_dim;
+  if (batch < 0 || seq_len < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || block_size <= 0 || block_count < 0)
+    return 0;
+  return sparse_bwd_workspace(batch, seq_len, num_q_heads, num_kv_heads, block_size, block_count).total;
+}
+
+int mosaic_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* out, const void* grad_out,
+                           const float* lse, const int64_t* block_indices, void* grad_q, void* grad_k, void* grad_v,
+                           void* workspace, size_t workspace_bytes, int* status, int batch, int seq_len,
+                           int num_q_heads, int num_kv_heads, int head_dim, int block_size, int block_count,
+                           float softmax_scale, void* stream) {
+  int rc = check_heads(batch, seq_len, num_q_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (block_size <= 0 || block_count <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_size % 64 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (seq_len % block_size != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (block_count > sparse_bwd_max_selected()) return MOSAIC_ERR_UNSUPPORTED;
+  if (batch == 0 || seq_len == 0) return MOSAIC_OK;
+  if (!q || !k || !v || !out || !grad_out || !lse || !block_indices || !grad_q || !grad_k || !grad_v)
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(grad_out) ||
+      !aligned16(grad_q) || !aligned16(grad_k) || !aligned16(grad_v))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  const size_t need =
+      sparse_bwd_workspace(batch, seq_len, num_q_heads, num_kv_heads, block_size, block_count).total;
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return MOSAIC_ERR_WORKSPACE;
+  SparseBwdLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = q; a.k = k; a.v = v; a.out = out; a.grad_out = grad_out; a.lse = lse;
+  a.block_idx = block_indices;
+  a.grad_q = grad_q; a.grad_k = grad_k; a.grad_v = grad_v;
+  a.workspace = workspace;
+  a.status = status;
+  a.B = batch; a.N = seq_len; a.Hq = num_q_heads; a.Hk = num_kv_heads; a.bs = block_size; a.K = block_count;
+  a.softmax_scale = default_scale(softmax_scale);
+  return launch_sparse_bwd(a, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

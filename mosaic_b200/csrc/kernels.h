@@ -70,6 +70,33 @@ struct TopkLaunch {
   bool overlap_previous;
 };
 
+// Backward of the selected-block attention (bsa_bwd.cu).
+struct SparseBwdLaunch {
+  const void* q;         // [B, N, Hq, 64] bf16
+  const void* k;         // [B, N, Hk, 64] bf16
+  const void* v;         // [B, N, Hk, 64] bf16
+  const void* out;       // [B, N, Hq, 64] bf16 forward output
+  const void* grad_out;  // [B, N, Hq, 64] bf16
+  const float* lse;      // [B, N, Hq] fp32, log2 units (forward)
+  const int64_t* block_idx;  // [B, N/bs, Hk, K]
+  void* grad_q;          // [B, N, Hq, 64] bf16
+  void* grad_k;          // [B, N, Hk, 64] bf16
+  void* grad_v;          // [B, N, Hk, 64] bf16
+  void* workspace;       // sparse_bwd_workspace(...).total bytes, 256-aligned
+  int* status;
+  int B, N, Hq, Hk, bs, K;
+  float softmax_scale;
+};
+
+// Byte offsets of the backward's scratch arrays inside its workspace.
+struct SparseBwdWorkspace {
+  size_t delta, count, cursor, offs, list, sorted, ucount, total;
+};
+
+SparseBwdWorkspace sparse_bwd_workspace(int B, int N, int Hq, int Hk, int bs, int K);
+int sparse_bwd_max_selected();
+int launch_sparse_bwd(const SparseBwdLaunch& a, cudaStream_t stream);
+
 int launch_engine(const EngineLaunch& a, cudaStream_t stream);
 int launch_pool(const PoolLaunch& a, cudaStream_t stream);
 int launch_topk(const TopkLaunch& a, cudaStream_t stream);

@@ -8,9 +8,9 @@ with softmax scale `softmax_scale` (default D ** -0.5). Like the reference
 kernel (ops.py:92,115-116) the arithmetic is bf16 with fp32 accumulation
 whatever the input dtype; the result is returned in q's dtype (ops.py:538).
 
-The work runs in `mosaic_sparse_attn_fwd` of libmosaic_b200.so on the current
-CUDA stream. There is no CPU path: CPU tensors raise, as the reference's
-Triton kernel would.
+The work runs in `mosaic_sparse_attn_fwd` (and, for gradients,
+`mosaic_sparse_attn_bwd`) of libmosaic_b200.so on the current CUDA stream.
+There is no CPU path: CPU tensors raise, as the reference's Triton kernel would.
 """
 import ctypes
 
@@ -18,7 +18,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "MosaicAttnFunction"]
+__all__ = ["mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "mosaic_attn_fwd", "mosaic_attn_bwd",
+           "MosaicAttnFunction"]
 
 
 def _stream_ptr(device):
@@ -88,27 +89,81 @@ def _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse, sta
     return out, lse
 
 
+def mosaic_attn_fwd(q, k, v, block_indices, block_size, softmax_scale, status=None):
+    """ops.mosaic_attn_fwd (ops.py:137-176): (output bf16, lse fp32 [B, N, Hq] in log2 units)."""
+    return _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=True, status=status)
+
+
+def mosaic_attn_bwd(q, k, v, output, lse, grad_o, softmax_scale, block_indices, block_size, status=None):
+    """ops.mosaic_attn_bwd (ops.py:436-507): (grad_q, grad_k, grad_v), bf16, through
+    `mosaic_sparse_attn_bwd` of libmosaic_b200.so on the current stream.
+
+    `output` and `lse` are the forward's (mosaic_attn_fwd). grad_q counts a block
+    selected twice twice, as the forward does; grad_k / grad_v take each selecting
+    query block once, like the reference's boolean block mask (ops.py:277-297).
+    Keys of blocks that no query block selected get zero gradients."""
+    _require_cuda(q, k, v, output, lse, grad_o, block_indices)
+    _check_qkv(q, k, v)
+    B, N, Hq, D = q.shape
+    Hk = k.shape[2]
+    if output.shape != q.shape or grad_o.shape != q.shape:
+        raise ValueError("output and grad_o must have q's shape")
+    if tuple(lse.shape) != (B, N, Hq):
+        raise ValueError(f"lse must be [B, N, Hq], got {tuple(lse.shape)}")
+    if block_indices.dim() != 4 or tuple(block_indices.shape[:3]) != (B, N // block_size, Hk):
+        raise ValueError(f"block_indices must be [B, N // block_size, Hk, K], got {tuple(block_indices.shape)}")
+    lib = _lib.load()
+    qb, kb, vb, ob, gb = _bf16(q), _bf16(k), _bf16(v), _bf16(output), _bf16(grad_o)
+    lse32 = lse.to(torch.float32).contiguous()
+    idx = block_indices.to(torch.int64).contiguous()
+    K = int(idx.shape[-1])
+    grad_q = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=q.device)
+    grad_k = torch.empty(B, N, Hk, D, dtype=torch.bfloat16, device=q.device)
+    grad_v = torch.empty(B, N, Hk, D, dtype=torch.bfloat16, device=q.device)
+    nbytes = lib.mosaic_sparse_attn_bwd_workspace_bytes(B, N, Hq, Hk, D, int(block_size), K)
+    ws = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.mosaic_sparse_attn_bwd(
+            _ptr(qb), _ptr(kb), _ptr(vb), _ptr(ob), _ptr(gb), _ptr(lse32), _ptr(idx),
+            _ptr(grad_q), _ptr(grad_k), _ptr(grad_v), _ptr(ws), ws.numel(), _ptr(status),
+            B, N, Hq, Hk, D, int(block_size), K, float(softmax_scale), _stream_ptr(q.device))
+    _lib.check("mosaic_sparse_attn_bwd", rc)
+    return grad_q, grad_k, grad_v
+
+
 class MosaicAttnFunction(torch.autograd.Function):
-    """Forward of ops.MosaicAttnFunction (ops.py:510-538). Backward is not part of
-    this library (inference forward only) and raises if reached."""
+    """ops.MosaicAttnFunction (ops.py:510-554). The forward keeps (q, k, v, output,
+    lse, block_indices) only when an input needs a gradient; the backward returns
+    the gradients in the inputs' dtypes."""
 
     @staticmethod
     def forward(ctx, q, k, v, block_indices, block_size, softmax_scale):
-        out, _ = _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=False)
+        need_grad = any(ctx.needs_input_grad[:3])
+        out, lse = _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=need_grad)
+        if need_grad:
+            ctx.save_for_backward(q, k, v, out, lse, block_indices)
+            ctx.block_size = block_size
+            ctx.softmax_scale = softmax_scale
         return out.to(q.dtype)
 
     @staticmethod
     def backward(ctx, grad_o):
-        raise NotImplementedError("mosaic_b200 implements the block-sparse attention forward only")
+        q, k, v, out, lse, block_indices = ctx.saved_tensors
+        dq, dk, dv = mosaic_attn_bwd(q, k, v, out, lse, grad_o, ctx.softmax_scale, block_indices, ctx.block_size)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None
 
 
 def mosaic_sparse_attn(q, k, v, block_indices, block_size, softmax_scale=None):
-    """Selected-block attention forward (ops.py:557-566). Under torch.compile the
-    call becomes the opaque custom op torch.ops.mosaic_b200.sparse_attn."""
+    """Selected-block attention (ops.py:557-566), differentiable in q, k, v. Under
+    torch.compile the call becomes the opaque custom op torch.ops.mosaic_b200.sparse_attn
+    (or sparse_attn_fwd, which has an autograd formula, when an input needs a gradient)."""
     softmax_scale = q.shape[-1] ** -0.5 if softmax_scale is None else softmax_scale
     if torch.compiler.is_compiling():
         from . import torch_ops  # noqa: F401  (registers the op)
 
+        if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+            return torch.ops.mosaic_b200.sparse_attn_fwd(q, k, v, block_indices, int(block_size),
+                                                         float(softmax_scale))[0]
         return torch.ops.mosaic_b200.sparse_attn(q, k, v, block_indices, int(block_size), float(softmax_scale))
     return MosaicAttnFunction.apply(q, k, v, block_indices, block_size, softmax_scale)
 

@@ -9,13 +9,19 @@ around them without running them: the ops stay opaque nodes that call the CUDA
 library at run time. Eagerly, `mosaic_attn_func` / `mosaic_sparse_attn` call the
 library directly and route through these ops only while being compiled, which
 keeps the dispatcher's overhead out of eager calls.
+
+For training graphs, `torch.ops.mosaic_b200.sparse_attn_fwd` (output and lse,
+ops.mosaic_attn_fwd, ops.py:137-176) carries an autograd formula that calls
+`torch.ops.mosaic_b200.sparse_attn_bwd` (ops.mosaic_attn_bwd, ops.py:436-507);
+mosaic_sparse_attn routes through it while being compiled when an input needs a
+gradient.
 """
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
-from torch.library import custom_op, register_fake
+from torch.library import custom_op, register_autograd, register_fake
 
-__all__ = ["attn_func", "sparse_attn"]
+__all__ = ["attn_func", "sparse_attn", "sparse_attn_fwd", "sparse_attn_bwd"]
 
 
 @custom_op("mosaic_b200::attn_func", mutates_args=(), device_types="cuda")
@@ -46,3 +52,50 @@ def sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices
 @register_fake("mosaic_b200::sparse_attn")
 def _sparse_attn_fake(q, k, v, block_indices, block_size, softmax_scale):
     return q.new_empty(q.shape)
+
+
+@custom_op("mosaic_b200::sparse_attn_fwd", mutates_args=(), device_types="cuda")
+def sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices: torch.Tensor,
+                    block_size: int, softmax_scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    from .ops import _sparse_fwd
+
+    out, lse = _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=True)
+    return out.to(q.dtype), lse
+
+
+@register_fake("mosaic_b200::sparse_attn_fwd")
+def _sparse_attn_fwd_fake(q, k, v, block_indices, block_size, softmax_scale):
+    return q.new_empty(q.shape), q.new_empty(q.shape[:3], dtype=torch.float32)
+
+
+@custom_op("mosaic_b200::sparse_attn_bwd", mutates_args=(), device_types="cuda")
+def sparse_attn_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,
+                    grad_out: torch.Tensor, block_indices: torch.Tensor, block_size: int,
+                    softmax_scale: float) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    from .ops import mosaic_attn_bwd
+
+    dq, dk, dv = mosaic_attn_bwd(q, k, v, out, lse, grad_out, softmax_scale, block_indices, block_size)
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
+@register_fake("mosaic_b200::sparse_attn_bwd")
+def _sparse_attn_bwd_fake(q, k, v, out, lse, grad_out, block_indices, block_size, softmax_scale):
+    return q.new_empty(q.shape), k.new_empty(k.shape), v.new_empty(v.shape)
+
+
+def _sparse_attn_fwd_setup(ctx, inputs, output):
+    q, k, v, block_indices, block_size, softmax_scale = inputs
+    out, lse = output
+    ctx.save_for_backward(q, k, v, out, lse, block_indices)
+    ctx.block_size = block_size
+    ctx.softmax_scale = softmax_scale
+
+
+def _sparse_attn_fwd_backward(ctx, grad_out, grad_lse):
+    q, k, v, out, lse, block_indices = ctx.saved_tensors
+    dq, dk, dv = torch.ops.mosaic_b200.sparse_attn_bwd(q, k, v, out, lse, grad_out.contiguous(), block_indices,
+                                                        ctx.block_size, ctx.softmax_scale)
+    return dq, dk, dv, None, None, None
+
+
+register_autograd("mosaic_b200::sparse_attn_fwd", _sparse_attn_fwd_backward, setup_context=_sparse_attn_fwd_setup)

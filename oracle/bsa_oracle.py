@@ -187,6 +187,60 @@ def sparse_attention(q, k, v, block_indices, block_size, softmax_scale=None, ret
     return (out, lse) if return_lse else out
 
 
+def sparse_attention_bwd(q, k, v, block_indices, block_size, grad_out, softmax_scale=None, out=None, lse=None):
+    """ops.mosaic_attn_bwd (ops.py:436-507) in fp32: returns (dq, dk, dv).
+
+    With c = scale*log2(e), S2 = (q c).k, P = exp2(S2 - lse), dP = dO.v and
+    D = rowsum(out * dO) (ops.py:461):
+      dq = scale * sum_keys P (dP - D) k over every selected slot, a block selected
+           twice counting twice (mosaic_attn_bwd_q_kernel, ops.py:184-274);
+      dk = scale * sum_queries P (dP - D) q and dv = sum_queries P dO over the
+           DISTINCT q blocks that selected the key's block (the boolean block mask
+           of mosaic_block_mask, ops.py:277-297, read by mosaic_attn_bwd_kv_kernel,
+           ops.py:305-433).
+    The reference folds LN_2 and LOG2_E into its bf16 operands (ops.py:249,267,
+    273,420,426); they cancel, so in exact arithmetic these are the same sums.
+    out / lse default to this module's sparse_attention forward."""
+    B, N, Hq, D = q.shape
+    Hk = k.shape[2]
+    G = Hq // Hk
+    K = block_indices.shape[-1]
+    scale = D ** -0.5 if softmax_scale is None else softmax_scale
+    nb = N // block_size
+    if out is None or lse is None:
+        out, lse = sparse_attention(q, k, v, block_indices, block_size, scale, return_lse=True)
+    qf, kf, vf, gof = q.float(), k.float(), v.float(), grad_out.float()
+    delta = (out.float() * gof).sum(-1)                               # B, N, Hq
+    dq = torch.zeros(B, N, Hq, D)
+    dk = torch.zeros(B, N, Hk, D)
+    dv = torch.zeros(B, N, Hk, D)
+    ar = torch.arange(block_size)
+    for b in range(B):
+        for h in range(Hk):
+            sel = block_indices[b, :, h, :].long()                    # nb, K
+            first = torch.ones(nb, K, dtype=torch.bool)               # first occurrence of each block in its row
+            for s in range(1, K):
+                first[:, s] = (sel[:, :s] != sel[:, s:s + 1]).all(dim=1)
+            rows = (sel.unsqueeze(-1) * block_size + ar).reshape(nb, K * block_size)
+            keep = first.repeat_interleave(block_size, dim=1).float()  # nb, K*bs
+            ks = kf[b, :, h][rows]                                    # nb, K*bs, D
+            vs = vf[b, :, h][rows]
+            for g in range(G):
+                j = h * G + g
+                qq = qf[b, :, j].reshape(nb, block_size, D)
+                s2 = (qq * (scale * LOG2_E)) @ ks.transpose(-1, -2)   # nb, bs, K*bs
+                p = torch.exp2(s2 - lse[b, :, j].reshape(nb, block_size, 1))
+                go = gof[b, :, j].reshape(nb, block_size, D)
+                dp = go @ vs.transpose(-1, -2)
+                ds = p * (dp - delta[b, :, j].reshape(nb, block_size, 1))
+                dq[b, :, j] = (scale * (ds @ ks)).reshape(N, D)
+                dk_slots = scale * (ds * keep.unsqueeze(1)).transpose(-1, -2) @ qq   # nb, K*bs, D
+                dv_slots = (p * keep.unsqueeze(1)).transpose(-1, -2) @ go
+                dk[b, :, h].index_add_(0, rows.reshape(-1), dk_slots.reshape(-1, D))
+                dv[b, :, h].index_add_(0, rows.reshape(-1), dv_slots.reshape(-1, D))
+    return dq, dk, dv
+
+
 def mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,
                      block_attn_only, no_compression=False, block_indices=None, parts=None):
     """primitives.mosaic_attn_func (primitives.py:54-89), fp32 arithmetic.

@@ -26,6 +26,14 @@ taken from the bf16 run of attn_topk on bf16 pooled tensors, which is the
 precision of the B200 path, and the fp32 run is driven with those indices.
 Fixtures keep the full indices, the small pooled outputs, 64 sampled query rows
 of every larger output (fp16) and fp64 per-head sums of the full outputs.
+
+The backward fixtures (bwd_*.npz) run ops.mosaic_attn_bwd's two Triton kernels
+(mosaic_attn_bwd_q_kernel, mosaic_attn_bwd_kv_kernel) in the interpreter on the
+forward kernel's own output and lse, with the block mask from ops.mosaic_block_mask
+(its eager function; the reference wraps it in torch.compile) and delta computed as
+ops.py:461 does. They keep 64 sampled rows of dq, dk, dv (fp16) and fp64 per-head
+sums. One config repeats a block inside some selections, which pins the
+reference's counting of repeated blocks (twice for dq, once for dk / dv).
 """
 import os
 import sys
@@ -94,6 +102,50 @@ CONFIGS = {
 }
 
 
+BWD_CONFIGS = {
+    # name: B, N, Hq, Hk, bs, K, seed, repeat_a_block
+    "bwd_n512_h8x2_bs64_k3": (1, 512, 8, 2, 64, 3, 10, False),
+    "bwd_n768_h4x1_bs128_k3_rep": (2, 768, 4, 1, 128, 3, 11, True),
+}
+
+
+def main_bwd(ops):
+    sys.path.insert(0, ROOT)
+    from tests.golden_util import draw_bwd_inputs
+    triton_sparse = make_triton_sparse(ops)
+    block_mask_fn = getattr(ops.mosaic_block_mask, "_torchdynamo_orig_callable", ops.mosaic_block_mask)
+    for name, (B, N, Hq, Hk, bs, K, seed, repeat) in BWD_CONFIGS.items():
+        q, k, v, go, idx = draw_bwd_inputs(B, N, Hq, Hk, bs, K, seed, repeat)
+        qf, kf, vf, gof = (t.float().contiguous() for t in (q, k, v, go))
+        scale = 64 ** -0.5
+        out = triton_sparse(qf, kf, vf, idx, bs)
+        lse = triton_sparse.last_lse
+        mask = block_mask_fn(idx)
+        delta = (out * gof).sum(dim=-1)
+        dq, dk, dv = torch.empty_like(qf), torch.empty_like(kf), torch.empty_like(vf)
+        ops.mosaic_attn_bwd_q_kernel.fn[(N // 64, Hq // Hk, B * Hk)](
+            q_ptr=qf, k_ptr=kf, v_ptr=vf, lse_ptr=lse, delta_ptr=delta, grad_o_ptr=gof, grad_q_ptr=dq,
+            block_indices_ptr=idx, softmax_scale=scale, seq_len=N, num_kv_heads=Hk, num_q_heads=Hq,
+            q_heads_per_kv_head=Hq // Hk, feature_dim=64, kv_block_size=bs, num_kv_blocks_per_q_block=K,
+            q_tile_size=64)
+        ops.mosaic_attn_bwd_kv_kernel.fn[(N // bs, B * Hk)](
+            q_ptr=qf, k_ptr=kf, v_ptr=vf, lse_ptr=lse, delta_ptr=delta, grad_o_ptr=gof, grad_k_ptr=dk,
+            grad_v_ptr=dv, block_mask_ptr=mask, softmax_scale=scale, seq_len=N, num_kv_heads=Hk,
+            num_q_heads=Hq, q_heads_per_kv_head=Hq // Hk, feature_dim=64, kv_block_size=bs, q_tile_size=64)
+        rows = torch.sort(torch.randperm(N, generator=torch.Generator().manual_seed(200 + seed))[:64]).values
+        f16 = lambda t: t[:, rows].to(torch.float16).numpy()
+        sums = lambda t: t.double().sum(dim=(1, 3)).numpy()
+        np.savez_compressed(
+            os.path.join(HERE, f"{name}.npz"),
+            meta=np.array([B, N, Hq, Hk, bs, K, seed, int(repeat)], dtype=np.int64),
+            rows=rows.numpy().astype(np.int32),
+            block_indices=idx.numpy().astype(np.int16),
+            dq_rows=f16(dq), dk_rows=f16(dk), dv_rows=f16(dv),
+            dq_sums=sums(dq), dk_sums=sums(dk), dv_sums=sums(dv),
+        )
+        print(name, "written")
+
+
 def main(ref_dir):
     sys.path.insert(0, ROOT)
     from oracle import bsa_oracle as O
@@ -148,6 +200,7 @@ def main(ref_dir):
             out_sums=sums(out), o_ba_sums=sums(o_ba), o_slc_sums=sums(o_slc),
         )
         print(name, "written")
+    main_bwd(ops)
 
 
 if __name__ == "__main__":

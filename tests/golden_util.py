@@ -12,7 +12,17 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
 def fixture_names():
-    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    """The forward fixtures."""
+    return sorted(n for n in _all_names() if not n.startswith("bwd_"))
+
+
+def bwd_fixture_names():
+    """The backward fixtures (bwd_*.npz)."""
+    return sorted(n for n in _all_names() if n.startswith("bwd_"))
+
+
+def _all_names():
+    return [os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))]
 
 
 def load(name):
@@ -21,6 +31,34 @@ def load(name):
     B, N, Hq, Hk, bs, K, bas, seed = (int(x) for x in d["meta"])
     d.update(B=B, N=N, Hq=Hq, Hk=Hk, bs=bs, K=K, bas=bas, seed=seed)
     return d
+
+
+def load_bwd(name):
+    z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
+    d = {k: z[k] for k in z.files}
+    B, N, Hq, Hk, bs, K, seed, repeat = (int(x) for x in d["meta"])
+    d.update(B=B, N=N, Hq=Hq, Hk=Hk, bs=bs, K=K, seed=seed, repeat=bool(repeat))
+    return d
+
+
+def bwd_inputs(d):
+    """A backward fixture's inputs (q, k, v, grad_out, block_indices)."""
+    return draw_bwd_inputs(d["B"], d["N"], d["Hq"], d["Hk"], d["bs"], d["K"], d["seed"], d["repeat"])
+
+
+def draw_bwd_inputs(B, N, Hq, Hk, bs, K, seed, repeat):
+    """Seeded bf16 inputs of a backward fixture; make_golden.py draws them with this
+    function too. `repeat`: every other q block selects its first block twice."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, N, Hq, 64, generator=g).bfloat16()
+    k = torch.randn(B, N, Hk, 64, generator=g).bfloat16()
+    v = torch.randn(B, N, Hk, 64, generator=g).bfloat16()
+    go = torch.randn(B, N, Hq, 64, generator=g).bfloat16()
+    nb = N // bs
+    idx = torch.stack([torch.randperm(nb, generator=g)[:K] for _ in range(B * nb * Hk)]).reshape(B, nb, Hk, K)
+    if repeat:
+        idx[:, ::2, :, 1] = idx[:, ::2, :, 0]
+    return q, k, v, go, idx
 
 
 def inputs(d):

@@ -126,3 +126,49 @@ def test_topk_rejects_bad_arguments():
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 49, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 129, None) != _lib.MOSAIC_OK
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 0, None) == _lib.MOSAIC_OK
+
+
+def _sparse_bwd(**kw):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, out=FAKE, go=FAKE, lse=FAKE, idx=FAKE, dq=FAKE, dk=FAKE, dv=FAKE,
+             ws=ctypes.c_void_p(0x100000), ws_bytes=1 << 30, status=None, B=1, N=1024, Hq=8, Hk=2, D=64, bs=64,
+             K=4, scale=0.0)
+    a.update(kw)
+    return _lib.load().mosaic_sparse_attn_bwd(
+        a["q"], a["k"], a["v"], a["out"], a["go"], a["lse"], a["idx"], a["dq"], a["dk"], a["dv"], a["ws"],
+        a["ws_bytes"], a["status"], a["B"], a["N"], a["Hq"], a["Hk"], a["D"], a["bs"], a["K"], a["scale"], None)
+
+
+def test_sparse_bwd_workspace_size():
+    lib = _lib.load()
+    B, N, Hq, Hk, bs, K = 2, 4096, 8, 2, 64, 16
+    b = lib.mosaic_sparse_attn_bwd_workspace_bytes(B, N, Hq, Hk, 64, bs, K)
+    nkb = N // bs
+    # D (fp32 per row and head) + counts, cursors, offsets, two list copies, per-tile union sizes
+    expect = B * N * Hq * 4 + B * Hk * (3 * nkb + 1 + 2 * nkb * K) * 4 + B * Hk * (N // 128) * 4
+    assert expect <= b <= expect + 7 * 256
+    assert lib.mosaic_sparse_attn_bwd_workspace_bytes(-1, N, Hq, Hk, 64, bs, K) == 0
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(lse=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(go=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(dv=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(dk=ctypes.c_void_p(0x10008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # misaligned
+    (dict(D=128), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(Hq=6, Hk=2), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(bs=32), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(N=1000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(K=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(K=1025), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(ws=None), _lib.MOSAIC_ERR_WORKSPACE),
+    (dict(ws_bytes=1024), _lib.MOSAIC_ERR_WORKSPACE),
+    (dict(ws=ctypes.c_void_p(0x100010)), _lib.MOSAIC_ERR_WORKSPACE),  # not 256-aligned
+])
+def test_sparse_bwd_rejects_bad_arguments(kw, code):
+    assert _sparse_bwd(**kw) == code
+
+
+def test_sparse_bwd_empty_inputs_are_a_no_op():
+    assert _sparse_bwd(B=0) == _lib.MOSAIC_OK
+    assert _sparse_bwd(N=0) == _lib.MOSAIC_OK

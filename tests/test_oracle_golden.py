@@ -91,3 +91,53 @@ def test_topk_checker_rejects_wrong_selection():
     bad[..., -1] = worst
     ok, _ = O.topk_matches(bad, idx, sc)
     assert not ok
+
+
+# ----------------------------------------------------------------------------- backward
+BWD_NAMES = GU.bwd_fixture_names()
+
+
+def test_bwd_fixtures_present():
+    assert len(BWD_NAMES) >= 2
+
+
+@pytest.mark.parametrize("name", BWD_NAMES)
+def test_backward_matches_reference(name):
+    """oracle.sparse_attention_bwd against the reference's two Triton backward kernels.
+    The reference rounds q*scale*log2e, P and dS to bf16 before its dots, hence the
+    bf16-level tolerance; one fixture repeats a block inside selections, so this also
+    pins the counting of repeats (twice for dq, once for dk / dv)."""
+    d = GU.load_bwd(name)
+    q, k, v, go, idx = GU.bwd_inputs(d)
+    assert torch.equal(idx, torch.from_numpy(d["block_indices"]).long())
+    dq, dk, dv = O.sparse_attention_bwd(q, k, v, idx, d["bs"], go)
+    rows = torch.from_numpy(d["rows"]).long()
+    for key, val in (("dq", dq), ("dk", dk), ("dv", dv)):
+        diff = (val[:, rows] - GU.t(d[key + "_rows"])).abs()
+        assert diff.max() < 3e-2 and diff.mean() < 3e-3, (key, diff.max(), diff.mean())
+        s = val.double().sum(dim=(1, 3))
+        torch.testing.assert_close(s, torch.from_numpy(d[key + "_sums"]), atol=0.5, rtol=2e-2)
+
+
+def test_backward_oracle_is_the_gradient_of_the_forward_oracle():
+    """With distinct selections the restated backward is autograd's gradient of the
+    forward restatement; with a repeated block only dq still is (dk / dv count the
+    repeat once, like the reference's boolean block mask)."""
+    torch.manual_seed(0)
+    B, N, Hq, Hk, bs, K = 2, 256, 8, 2, 64, 3
+    q, k, v, go = torch.randn(B, N, Hq, 64), torch.randn(B, N, Hk, 64), torch.randn(B, N, Hk, 64), \
+        torch.randn(B, N, Hq, 64)
+    nb = N // bs
+    idx = torch.stack([torch.randperm(nb)[:K] for _ in range(B * nb * Hk)]).reshape(B, nb, Hk, K)
+    for repeat in (False, True):
+        if repeat:
+            idx[..., 1] = idx[..., 0]
+        qa, ka, va = (t.clone().requires_grad_() for t in (q, k, v))
+        O.sparse_attention(qa, ka, va, idx, bs).backward(go)
+        dq, dk, dv = O.sparse_attention_bwd(q, k, v, idx, bs, go)
+        torch.testing.assert_close(dq, qa.grad, atol=1e-5, rtol=1e-5)
+        if not repeat:
+            torch.testing.assert_close(dk, ka.grad, atol=1e-5, rtol=1e-5)
+            torch.testing.assert_close(dv, va.grad, atol=1e-5, rtol=1e-5)
+        else:
+            assert (dk - ka.grad).abs().max() > 1e-2

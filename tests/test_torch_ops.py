@@ -31,3 +31,18 @@ def test_fake_sparse_attn_shapes():
         idx = torch.empty(1, 12, 3, 4, dtype=torch.int64, device="cuda")
         o = torch.ops.mosaic_b200.sparse_attn(q, k, k, idx, 64, 0.125)
         assert o.shape == q.shape and o.dtype == q.dtype
+
+
+def test_fake_sparse_attn_training_ops():
+    assert hasattr(torch.ops.mosaic_b200, "sparse_attn_fwd")
+    assert hasattr(torch.ops.mosaic_b200, "sparse_attn_bwd")
+    with FakeTensorMode():
+        q = torch.empty(2, 1024, 8, 64, dtype=torch.bfloat16, device="cuda")
+        k = torch.empty(2, 1024, 2, 64, dtype=torch.bfloat16, device="cuda")
+        idx = torch.empty(2, 16, 2, 3, dtype=torch.int64, device="cuda")
+        o, lse = torch.ops.mosaic_b200.sparse_attn_fwd(q, k, k, idx, 64, 0.125)
+        assert o.shape == q.shape and o.dtype == q.dtype
+        assert lse.shape == (2, 1024, 8) and lse.dtype == torch.float32
+        dq, dk, dv = torch.ops.mosaic_b200.sparse_attn_bwd(q, k, k, o, lse, o, idx, 64, 0.125)
+        assert dq.shape == q.shape and dk.shape == k.shape and dv.shape == k.shape
+        assert dq.dtype == dk.dtype == torch.bfloat16
