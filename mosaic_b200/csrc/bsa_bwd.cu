@@ -381,38 +381,41 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (both M-tiles)
+    // Software-pipelined: once the rows of M-tile m have turned tile t into dS, the
+    // warp issues dQ_m(t) and then S_m / dP_m of tile t + 1, so one warpgroup works on
+    // tile t + 1 while the other finishes tile t.
     const uint32_t id_s = make_idesc_bf16(128, 64, false);
     const uint32_t id_dq = make_idesc_bf16(128, 64, true);
     const uint32_t sQa = smem_u32(sQ), sDOa = smem_u32(sDO), sKa = smem_u32(sK), sVa = smem_u32(sV);
+    // S_m = Q_m K^T and dP_m = dO_m V^T of the tile in stage st
+    auto issue_sdp = [&](int m, int st) {
+      const uint64_t kd = sw128_desc(sKa + st * kBox, 1024, 16);
+      const uint64_t vd = sw128_desc(sVa + st * kBox, 1024, 16);
+      const uint64_t qd = sw128_desc(sQa + 2 * m * kBox, 1024, 16);
+      const uint64_t dod = sw128_desc(sDOa + 2 * m * kBox, 1024, 16);
+      const uint32_t tS = tmem + 192u * m;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ss_elect(tS, qd + static_cast<uint64_t>(2 * ks), kd + static_cast<uint64_t>(2 * ks), id_s,
+                     ks > 0 ? 1u : 0u);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ss_elect(tS + 64, dod + static_cast<uint64_t>(2 * ks), vd + static_cast<uint64_t>(2 * ks), id_s,
+                     ks > 0 ? 1u : 0u);
+      tc_commit_elect(&sm.sp_full[m]);
+    };
     int g = 0, it = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
-      ok = warp_wait(&sm.q_full, it & 1, abort_flag, p.status);
+      ok = warp_wait(&sm.q_full, it & 1, abort_flag, p.status) &&
+           warp_wait(&sm.kv_full[g % kStagesDq], (g / kStagesDq) & 1, abort_flag, p.status);
       tc_fence_after();
+      if (!ok) break;
+      issue_sdp(0, g % kStagesDq);
+      issue_sdp(1, g % kStagesDq);
+      if (T == 1) tc_commit_elect(&sm.q_empty);
       for (int t = 0; ok && t < T; ++t) {
         const int gt = g + t, st = gt % kStagesDq;
-        if (!warp_wait(&sm.kv_full[st], (gt / kStagesDq) & 1, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint64_t kd = sw128_desc(sKa + st * kBox, 1024, 16);
-        const uint64_t vd = sw128_desc(sVa + st * kBox, 1024, 16);
-        for (int m = 0; m < 2; ++m) {
-          const uint64_t qd = sw128_desc(sQa + 2 * m * kBox, 1024, 16);
-          const uint64_t dod = sw128_desc(sDOa + 2 * m * kBox, 1024, 16);
-          const uint32_t tS = tmem + 192u * m;
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_ss_elect(tS, qd + static_cast<uint64_t>(2 * ks), kd + static_cast<uint64_t>(2 * ks), id_s,
-                         ks > 0 ? 1u : 0u);
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_ss_elect(tS + 64, dod + static_cast<uint64_t>(2 * ks), vd + static_cast<uint64_t>(2 * ks), id_s,
-                         ks > 0 ? 1u : 0u);
-          tc_commit_elect(&sm.sp_full[m]);
-        }
-        if (t == T - 1) tc_commit_elect(&sm.q_empty);  // the last reads of Q and dO of this unit
         const uint64_t kmn = sw128_desc(sKa + st * kBox, 1024, 16384);  // K as the [keys x d] B operand
         for (int m = 0; ok && m < 2; ++m) {
           ok = warp_wait(&sm.ds_full[m], gt & 1, abort_flag, p.status);
@@ -424,7 +427,19 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
           for (int ks = 0; ks < 4; ++ks)
             mma_ts_elect(tS + 128, tS + ks * 8, kmn + static_cast<uint64_t>(ks * 128), id_dq,
                          (t > 0 || ks > 0) ? 1u : 0u);
-          if (t == T - 1) tc_commit_elect(&sm.dq_done[m]);
+          if (t == T - 1) {
+            tc_commit_elect(&sm.dq_done[m]);
+          } else {
+            if (m == 0) {
+              ok = warp_wait(&sm.kv_full[(gt + 1) % kStagesDq], ((gt + 1) / kStagesDq) & 1, abort_flag, p.status);
+              tc_fence_after();
+              if (!ok) break;
+            }
+            // S_m / dP_m of the next tile overwrite the dS that the dQ_m MMAs above read;
+            // tcgen05.mma executes in issue order, so those reads come first.
+            issue_sdp(m, (gt + 1) % kStagesDq);
+            if (m == 1 && t + 1 == T - 1) tc_commit_elect(&sm.q_empty);
+          }
         }
         if (ok) tc_commit_elect(&sm.kv_empty[st]);
       }

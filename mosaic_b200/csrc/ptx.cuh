@@ -268,12 +268,13 @@ __device__ __forceinline__ void mbar_arrive_expect_tx_elect(uint64_t* bar, uint3
       "r"(bytes)
       : "memory");
 }
-// Bounded wait for a whole warp: lane 0 polls, the result is broadcast, and the
-// warp leaves converged.
+// Bounded wait for a whole warp. Every lane polls (one instruction for the warp)
+// and the verdict is a warp vote, so the warp never branches on one lane's result:
+// an MMA-issuing warp whose loop held a lane-0-only poll followed by a broadcast
+// issued its tcgen05.mma instructions at less than half the rate it reaches this way.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
-  bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = bounded_wait(bar, parity, abort_flag, status);
-  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  const bool ok = bounded_wait(bar, parity, abort_flag, status);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------- packed fp32 (sm_100)
