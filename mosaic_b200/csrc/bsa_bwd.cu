@@ -49,6 +49,54 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+// Four consecutive fp32 values from shared memory (16-byte aligned).
+__device__ __forceinline__ float4 lds4(const float* ptr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(smem_u32(ptr)));
+  return v;
+}
+
+// P^T and dS^T of one key row over 32 query columns, packed in place as 16 bf16
+// pairs: p = exp2(s c - lse), ds = p (dp - D), with nlse = -lse and ndl = -D read
+// from shared memory. Of every 8 pairs the last 3 take the software exp2 on the FMA
+// pipe and the others ex2.approx, which balances the two pipes (the same split as
+// the forward softmax). s[i] / dp[i] are read at pair i/2 <= i, before pair i is
+// written, so packing in place is safe.
+__device__ __forceinline__ void p_ds_quarter(uint32_t (&s)[32], uint32_t (&dp)[32], const float* nlse,
+                                             const float* ndl, float c) {
+  constexpr int kPolyDen = 8, kPolyNum = 3;
+  const uint64_t c2 = f2_pack(c, c);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {  // 8 columns: two 16-byte loads of each of nlse, ndl
+    const float4 la = lds4(nlse + 8 * q), lb = lds4(nlse + 8 * q + 4);
+    const float4 da = lds4(ndl + 8 * q), db = lds4(ndl + 8 * q + 4);
+    const uint64_t nl[4] = {f2_pack(la.x, la.y), f2_pack(la.z, la.w), f2_pack(lb.x, lb.y), f2_pack(lb.z, lb.w)};
+    const uint64_t nd[4] = {f2_pack(da.x, da.y), f2_pack(da.z, da.w), f2_pack(db.x, db.y), f2_pack(db.z, db.w)};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = 4 * q + k;
+      const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nl[k]);
+      uint64_t e;
+      if ((i % kPolyDen) >= kPolyDen - kPolyNum) {
+        e = exp2_poly2(x);
+      } else {
+        float x0, x1;
+        f2_unpack(x, x0, x1);
+        e = f2_pack(ex2_approx(x0), ex2_approx(x1));
+      }
+      const uint64_t d =
+          f2_mul(e, f2_add(f2_pack(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1])), nd[k]));
+      float e0, e1, d0, d1;
+      f2_unpack(e, e0, e1);
+      f2_unpack(d, d0, d1);
+      s[i] = pack_bf16x2(e0, e1);
+      dp[i] = pack_bf16x2(d0, d1);
+    }
+  }
+}
+
 // ============================================================================ D
 // D[r] = sum_d O[r, d] dO[r, d] in fp32; 8 threads per 64-value row (coalesced
 // 16-byte loads), reduced with shuffles.
@@ -560,8 +608,8 @@ struct DkvSmem {
   uint32_t tmem_base;
   int abort_flag;
   int mask[kStagesKv];  // per chunk: bit s set = the q block selected key segment s
-  float lse[kStagesKv][128];
-  float dl[kStagesKv][128];
+  alignas(16) float nlse[kStagesKv][128];  // -lse of the chunk's 128 query rows
+  alignas(16) float ndl[kStagesKv][128];   // -D of the chunk's 128 query rows
 };
 
 constexpr size_t kDkvSmemBytes = 1024 + 4 * kBox /*K, V*/ + kStagesKv * kChunkBytes + sizeof(DkvSmem);
@@ -648,8 +696,8 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            sm.lse[st][lane + 32 * j] = lv[j];
-            sm.dl[st][lane + 32 * j] = dv[j];
+            sm.nlse[st][lane + 32 * j] = -lv[j];
+            sm.ndl[st][lane + 32 * j] = -dv[j];
           }
           if (lane == 0) sm.mask[st] = mk;
           __syncwarp();
@@ -756,21 +804,17 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
         // columns 16j..16j+15 of the half, which quarter 0 has already read.
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          const float* lse = sm.lse[st] + 64 * hf + 32 * j;
-          const float* dl = sm.dl[st] + 64 * hf + 32 * j;
           uint32_t s[32], dp[32];
           tmem_ld32(tT + 64 * hf + 32 * j, s);
           tmem_ld32(tT + 128 + 64 * hf + 32 * j, dp);
           tmem_ld_wait();
           reg_fence<32>(s);
           reg_fence<32>(dp);
+          if (on) {
+            p_ds_quarter(s, dp, sm.nlse[st] + 64 * hf + 32 * j, sm.ndl[st] + 64 * hf + 32 * j, p.scale_log2);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = on ? ex2_approx(__uint_as_float(s[2 * i]) * p.scale_log2 - lse[2 * i]) : 0.f;
-            const float p1 = on ? ex2_approx(__uint_as_float(s[2 * i + 1]) * p.scale_log2 - lse[2 * i + 1]) : 0.f;
-            s[i] = pack_bf16x2(p0, p1);
-            dp[i] = pack_bf16x2(p0 * (__uint_as_float(dp[2 * i]) - dl[2 * i]),
-                                p1 * (__uint_as_float(dp[2 * i + 1]) - dl[2 * i + 1]));
+            for (int i = 0; i < 16; ++i) s[i] = dp[i] = 0u;
           }
           tmem_st16(tT + 64 * hf + 16 * j, s);
           tmem_st16(tT + 128 + 64 * hf + 16 * j, dp);
