@@ -603,7 +603,7 @@ struct DkvParams {
 struct DkvSmem {
   uint64_t kv_full, kv_empty;
   uint64_t ch_full[kStagesKv], ch_empty[kStagesKv];
-  uint64_t sp_full, ps_full, acc_full, acc_empty;
+  uint64_t sp_full[2], ps_full[2], acc_full, acc_empty;
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -637,8 +637,10 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
       mbar_init(&sm.ch_full[s], 1);
       mbar_init(&sm.ch_empty[s], 1);
     }
-    mbar_init(&sm.sp_full, 1);
-    mbar_init(&sm.ps_full, 256);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&sm.sp_full[h], 1);
+      mbar_init(&sm.ps_full[h], 128);
+    }
     mbar_init(&sm.acc_full, 1);
     mbar_init(&sm.acc_empty, 256);
     mbar_init(&sm.drain, 1);
@@ -721,59 +723,79 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    const uint32_t id_s = make_idesc_bf16(128, 128, false);
+    // Each chunk is two halves h (the 64 query rows of head 2j + h). Once warpgroup h
+    // has turned half h of chunk c into P^T / dS^T, the warp issues its dV / dK MMAs and
+    // then S^T / dP^T of half h of chunk c + 1, so one warpgroup works on chunk c + 1
+    // while the other finishes chunk c.
+    const uint32_t id_s = make_idesc_bf16(128, 64, false);
     const uint32_t id_acc = make_idesc_bf16(128, 64, true);
     const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sCa = smem_u32(sC);
     const uint64_t kd = sw128_desc(sKa, 1024, 16), vd = sw128_desc(sVa, 1024, 16);
+    // S^T_h = K Q_h^T and dP^T_h = V dO_h^T of the chunk in stage st
+    auto issue_ss = [&](int h, int st) {
+      const uint32_t cq = sCa + st * kChunkBytes + h * kBox, cdo = cq + 2 * kBox;
+      const uint64_t qk = sw128_desc(cq, 1024, 16), dok = sw128_desc(cdo, 1024, 16);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ss_elect(tmem + 64u * h, kd + static_cast<uint64_t>(2 * ks), qk + static_cast<uint64_t>(2 * ks), id_s,
+                     ks > 0 ? 1u : 0u);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ss_elect(tmem + 128u + 64u * h, vd + static_cast<uint64_t>(2 * ks), dok + static_cast<uint64_t>(2 * ks),
+                     id_s, ks > 0 ? 1u : 0u);
+      tc_commit_elect(&sm.sp_full[h]);
+    };
+    // dV += P^T_h dO_h and dK += dS^T_h Q_h (P^T_h / dS^T_h as bf16 pairs in TMEM)
+    auto issue_ts = [&](int h, int st, bool first) {
+      const uint32_t cq = sCa + st * kChunkBytes + h * kBox, cdo = cq + 2 * kBox;
+      const uint64_t qmn = sw128_desc(cq, 1024, 16384), domn = sw128_desc(cdo, 1024, 16384);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ts_elect(tmem + 256, tmem + 64u * h + 8u * ks, domn + static_cast<uint64_t>(ks * 128), id_acc,
+                     (first && ks == 0) ? 0u : 1u);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ts_elect(tmem + 320, tmem + 128u + 64u * h + 8u * ks, qmn + static_cast<uint64_t>(ks * 128), id_acc,
+                     (first && ks == 0) ? 0u : 1u);
+    };
     int gc = 0, live = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const int nch = p.ucount[u] * per_qb;
       if (nch == 0) continue;
-      ok = warp_wait(&sm.kv_full, live & 1, abort_flag, p.status);
+      ok = warp_wait(&sm.kv_full, live & 1, abort_flag, p.status) &&
+           warp_wait(&sm.ch_full[gc % kStagesKv], (gc / kStagesKv) & 1, abort_flag, p.status);
       tc_fence_after();
-      for (int c = 0; ok && c < nch; ++c, ++gc) {
-        const int st = gc % kStagesKv;
-        if (!warp_wait(&sm.ch_full[st], (gc / kStagesKv) & 1, abort_flag, p.status)) {
-          ok = false;
-          break;
+      if (!ok) break;
+      issue_ss(0, gc % kStagesKv);
+      issue_ss(1, gc % kStagesKv);
+      for (int c = 0; ok && c < nch; ++c) {
+        const int g = gc + c, st = g % kStagesKv;
+        for (int h = 0; ok && h < 2; ++h) {
+          ok = warp_wait(&sm.ps_full[h], g & 1, abort_flag, p.status);
+          // The epilogue of the previous live unit must have read dK / dV first.
+          if (ok && c == 0 && h == 0 && live > 0) ok = warp_wait(&sm.acc_empty, (live - 1) & 1, abort_flag, p.status);
+          tc_fence_after();
+          if (!ok) break;
+          issue_ts(h, st, c == 0 && h == 0);
+          if (c + 1 < nch) {
+            // S^T_h / dP^T_h of the next chunk overwrite the P^T_h / dS^T_h that the
+            // MMAs above read; tcgen05.mma executes in issue order.
+            if (h == 0) {
+              ok = warp_wait(&sm.ch_full[(g + 1) % kStagesKv], ((g + 1) / kStagesKv) & 1, abort_flag, p.status);
+              tc_fence_after();
+              if (!ok) break;
+            }
+            issue_ss(h, (g + 1) % kStagesKv);
+          }
         }
-        tc_fence_after();
-        const uint32_t cq = sCa + st * kChunkBytes, cdo = cq + 2 * kBox;
-        const uint64_t qk = sw128_desc(cq, 1024, 16), dok = sw128_desc(cdo, 1024, 16);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          mma_ss_elect(tmem, kd + static_cast<uint64_t>(2 * ks), qk + static_cast<uint64_t>(2 * ks), id_s,
-                       ks > 0 ? 1u : 0u);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          mma_ss_elect(tmem + 128, vd + static_cast<uint64_t>(2 * ks), dok + static_cast<uint64_t>(2 * ks), id_s,
-                       ks > 0 ? 1u : 0u);
-        tc_commit_elect(&sm.sp_full);
-        ok = warp_wait(&sm.ps_full, gc & 1, abort_flag, p.status);
-        // The epilogue of the previous live unit must have read dK / dV first.
-        if (ok && c == 0 && live > 0) ok = warp_wait(&sm.acc_empty, (live - 1) & 1, abort_flag, p.status);
-        tc_fence_after();
-        if (!ok) break;
-        const uint64_t qmn = sw128_desc(cq, 1024, 16384), domn = sw128_desc(cdo, 1024, 16384);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t col = 64u * (ks >> 2) + 8u * (ks & 3);
-          mma_ts_elect(tmem + 256, tmem + col, domn + static_cast<uint64_t>(ks * 128), id_acc,
-                       (c > 0 || ks > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t col = 128u + 64u * (ks >> 2) + 8u * (ks & 3);
-          mma_ts_elect(tmem + 320, tmem + col, qmn + static_cast<uint64_t>(ks * 128), id_acc,
-                       (c > 0 || ks > 0) ? 1u : 0u);
-        }
-        tc_commit_elect(&sm.ch_empty[st]);
+        if (ok) tc_commit_elect(&sm.ch_empty[st]);  // every read of this chunk's stage is issued
       }
       if (!ok) break;
       tc_commit_elect(&sm.acc_full);
       tc_commit_elect(&sm.kv_empty);
       ++live;
+      gc += nch;
     }
     tc_commit_elect(&sm.drain);
     if (lane == 0) wait_noabort_b(&sm.drain, 0, p.status);
@@ -794,7 +816,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
         const int st = gc % kStagesKv;
         // ch_full orders the producer's lse / D / mask writes before these reads
         if (!bounded_wait(&sm.ch_full[st], (gc / kStagesKv) & 1, abort_flag, p.status) ||
-            !bounded_wait(&sm.sp_full, gc & 1, abort_flag, p.status)) {
+            !bounded_wait(&sm.sp_full[hf], gc & 1, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -821,7 +843,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&sm.ps_full);
+        mbar_arrive(&sm.ps_full[hf]);
       }
       if (!ok) break;
       uint32_t o[64];
