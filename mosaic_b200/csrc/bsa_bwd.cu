@@ -307,12 +307,14 @@ __global__ void idx_union_kernel(const int* offs, const int* sorted, int* ucount
 
 // ============================================================================ dQ
 constexpr int kThreadsBwd = 384;  // warp 0 TMA, warp 1 MMA, warps 2-3 idle, warps 4-11 rows
-constexpr int kStagesDq = 4;
+constexpr int kStagesDq = 8;
 constexpr int kMaxSelB = 1024;
 
 struct DqParams {
-  CUtensorMap tm_q, tm_do, tm_k, tm_v;
+  CUtensorMap tm_k, tm_v;
   const int64_t* block_idx;
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* dout;
   const float* lse;
   const float* delta;
   __nv_bfloat16* dq;
@@ -323,25 +325,25 @@ struct DqParams {
 };
 
 struct DqSmem {
-  uint64_t q_full, q_empty;
   uint64_t kv_full[kStagesDq], kv_empty[kStagesDq];
-  uint64_t sp_full[2], ds_full[2], dq_done[2], dq_empty[2];
+  uint64_t qt_full[2], sp_full[2], ds_full[2], dq_done[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
   int sel[kMaxSelB];
 };
 
-constexpr size_t kDqSmemBytes = 1024 + 8 * kBox /*Q, dO*/ + 2 * kStagesDq * kBox /*K, V*/ + sizeof(DqSmem);
+constexpr size_t kDqSmemBytes = 1024 + 2 * kStagesDq * kBox /*K, V*/ + sizeof(DqSmem);
 
-// TMEM of M-tile m (query heads 2m, 2m+1 of the group): S at 192m (dS overwrites
-// its first 32 columns as bf16 pairs), dP at 192m + 64, dQ at 192m + 128.
+// TMEM of M-tile m (query heads 2m, 2m+1 of the group) at 256m: S (64 columns; dS
+// overwrites its first 32 as bf16 pairs), dP at +64, dQ at +128, and the unit's Q and
+// dO rows as bf16 pairs at +192 and +224: the A operands of S = Q K^T and dP = dO V^T,
+// written once per unit by the row threads, so those MMAs read only K / V from shared
+// memory.
 __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constant__ DqParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = tiles;                   // M-tile m: boxes 2m, 2m+1 (heads 2m, 2m+1)
-  uint8_t* sDO = tiles + 4 * kBox;       // same layout
-  uint8_t* sK = tiles + 8 * kBox;        // stages
+  uint8_t* sK = tiles;                   // stages
   uint8_t* sV = sK + kStagesDq * kBox;   // stages
   DqSmem& sm = *reinterpret_cast<DqSmem*>(sV + kStagesDq * kBox);
   volatile int* abort_flag = &sm.abort_flag;
@@ -351,17 +353,15 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
   const int T = p.K * spb;  // 64-key tiles per unit
 
   if (threadIdx.x == 0) {
-    mbar_init(&sm.q_full, 1);
-    mbar_init(&sm.q_empty, 1);
     for (int s = 0; s < kStagesDq; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
     }
     for (int m = 0; m < 2; ++m) {
+      mbar_init(&sm.qt_full[m], 128);
       mbar_init(&sm.sp_full[m], 1);
       mbar_init(&sm.ds_full[m], 128);
       mbar_init(&sm.dq_done[m], 1);
-      mbar_init(&sm.dq_empty[m], 128);
     }
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
@@ -377,13 +377,13 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
-    int g = 0, nq = 0;  // K/V tiles and Q/dO tiles issued
+    // ---------------------------------------------------------------- TMA producer (K / V tiles)
+    int g = 0;  // K/V tiles issued
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const int qt = u % p.qtiles, rest = u / p.qtiles;
       const int h = rest % p.Hk, b = rest / p.Hk;
-      const int n0 = qt * 64, qb = n0 / p.bs;
+      const int qb = qt * 64 / p.bs;
       const int64_t* src = p.block_idx + ((static_cast<int64_t>(b) * p.nqb + qb) * p.Hk + h) * p.K;
       __syncwarp();
       for (int s = lane; s < p.K; s += 32) {
@@ -395,17 +395,6 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
         sm.sel[s] = static_cast<int>(v);
       }
       __syncwarp();
-      if (nq > 0 && !warp_wait(&sm.q_empty, (nq - 1) & 1, abort_flag, p.status)) {
-        ok = false;
-        break;
-      }
-      mbar_arrive_expect_tx_elect(&sm.q_full, 8 * kBox);
-      for (int j = 0; j < 4; ++j) {
-        const int col = (h * G + j) * 64, row = b * p.N + n0;
-        tma_load_2d_elect(sQ + j * kBox, &p.tm_q, &sm.q_full, col, row);
-        tma_load_2d_elect(sDO + j * kBox, &p.tm_do, &sm.q_full, col, row);
-      }
-      ++nq;
       for (int t = 0; t < T; ++t, ++g) {
         const int st = g % kStagesDq, r = g / kStagesDq;
         if (r > 0 && !warp_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) {
@@ -420,7 +409,6 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
     }
     // Drain: every TMA write into shared memory lands before the CTA exits.
     if (lane == 0) {
-      if (nq > 0) wait_noabort_b(&sm.q_full, (nq - 1) & 1, p.status);
       for (int s = 0; s < kStagesDq && s < g; ++s) {
         const int g_last = s + kStagesDq * ((g - 1 - s) / kStagesDq);
         wait_noabort_b(&sm.kv_full[s], (g_last / kStagesDq) & 1, p.status);
@@ -432,51 +420,48 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
     // Software-pipelined: once the rows of M-tile m have turned tile t into dS, the
     // warp issues dQ_m(t) and then S_m / dP_m of tile t + 1, so one warpgroup works on
     // tile t + 1 while the other finishes tile t.
-    const uint32_t id_s = make_idesc_bf16(128, 64, false);
-    const uint32_t id_dq = make_idesc_bf16(128, 64, true);
-    const uint32_t sQa = smem_u32(sQ), sDOa = smem_u32(sDO), sKa = smem_u32(sK), sVa = smem_u32(sV);
-    // S_m = Q_m K^T and dP_m = dO_m V^T of the tile in stage st
+    const uint32_t id_s = make_idesc_bf16(128, 64, false);   // B = K / V tile, K-major
+    const uint32_t id_dq = make_idesc_bf16(128, 64, true);   // B = K tile as [keys x d], MN-major
+    const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV);
+    // S_m = Q_m K^T and dP_m = dO_m V^T of the tile in stage st (Q_m, dO_m from TMEM)
     auto issue_sdp = [&](int m, int st) {
       const uint64_t kd = sw128_desc(sKa + st * kBox, 1024, 16);
       const uint64_t vd = sw128_desc(sVa + st * kBox, 1024, 16);
-      const uint64_t qd = sw128_desc(sQa + 2 * m * kBox, 1024, 16);
-      const uint64_t dod = sw128_desc(sDOa + 2 * m * kBox, 1024, 16);
-      const uint32_t tS = tmem + 192u * m;
+      const uint32_t tM = tmem + 256u * m;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_ss_elect(tS, qd + static_cast<uint64_t>(2 * ks), kd + static_cast<uint64_t>(2 * ks), id_s,
-                     ks > 0 ? 1u : 0u);
+        mma_ts_elect(tM, tM + 192u + 8u * ks, kd + static_cast<uint64_t>(2 * ks), id_s, ks > 0 ? 1u : 0u);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_ss_elect(tS + 64, dod + static_cast<uint64_t>(2 * ks), vd + static_cast<uint64_t>(2 * ks), id_s,
-                     ks > 0 ? 1u : 0u);
+        mma_ts_elect(tM + 64u, tM + 224u + 8u * ks, vd + static_cast<uint64_t>(2 * ks), id_s, ks > 0 ? 1u : 0u);
       tc_commit_elect(&sm.sp_full[m]);
     };
     int g = 0, it = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
-      ok = warp_wait(&sm.q_full, it & 1, abort_flag, p.status) &&
+      // qt_full: the rows have written this unit's Q / dO into TMEM, after reading the
+      // previous unit's dQ (so dQ may be overwritten too).
+      ok = warp_wait(&sm.qt_full[0], it & 1, abort_flag, p.status) &&
+           warp_wait(&sm.qt_full[1], it & 1, abort_flag, p.status) &&
            warp_wait(&sm.kv_full[g % kStagesDq], (g / kStagesDq) & 1, abort_flag, p.status);
       tc_fence_after();
       if (!ok) break;
       issue_sdp(0, g % kStagesDq);
       issue_sdp(1, g % kStagesDq);
-      if (T == 1) tc_commit_elect(&sm.q_empty);
       for (int t = 0; ok && t < T; ++t) {
         const int gt = g + t, st = gt % kStagesDq;
-        const uint64_t kmn = sw128_desc(sKa + st * kBox, 1024, 16384);  // K as the [keys x d] B operand
+        const uint64_t kmn = sw128_desc(sKa + st * kBox, 1024, 16384);
         for (int m = 0; ok && m < 2; ++m) {
           ok = warp_wait(&sm.ds_full[m], gt & 1, abort_flag, p.status);
-          if (ok && t == 0 && it > 0) ok = warp_wait(&sm.dq_empty[m], (it - 1) & 1, abort_flag, p.status);
           tc_fence_after();
           if (!ok) break;
-          const uint32_t tS = tmem + 192u * m;
+          const uint32_t tM = tmem + 256u * m;
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            mma_ts_elect(tS + 128, tS + ks * 8, kmn + static_cast<uint64_t>(ks * 128), id_dq,
+            mma_ts_elect(tM + 128u, tM + 8u * ks, kmn + static_cast<uint64_t>(ks * 128), id_dq,
                          (t > 0 || ks > 0) ? 1u : 0u);
           if (t == T - 1) {
-            tc_commit_elect(&sm.dq_done[m]);
+            tc_commit_elect(&sm.dq_done[m]);  // also: every MMA of the unit reading Q_m / dO_m is issued
           } else {
             if (m == 0) {
               ok = warp_wait(&sm.kv_full[(gt + 1) % kStagesDq], ((gt + 1) / kStagesDq) & 1, abort_flag, p.status);
@@ -486,7 +471,6 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
             // S_m / dP_m of the next tile overwrite the dS that the dQ_m MMAs above read;
             // tcgen05.mma executes in issue order, so those reads come first.
             issue_sdp(m, (gt + 1) % kStagesDq);
-            if (m == 1 && t + 1 == T - 1) tc_commit_elect(&sm.q_empty);
           }
         }
         if (ok) tc_commit_elect(&sm.kv_empty[st]);
@@ -501,7 +485,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
     // ---------------------------------------------------------------- dS and the dQ epilogue, one query row per thread
     const int wg = (warp - 4) >> 2, qd = warp & 3;
     const int row = qd * 32 + lane;
-    const uint32_t tS = tmem + (static_cast<uint32_t>(qd * 32) << 16) + 192u * wg;
+    const uint32_t tM = tmem + (static_cast<uint32_t>(qd * 32) << 16) + 256u * wg;
     int g = 0, it = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
@@ -511,6 +495,24 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
       const int n = qt * 64 + (row & 63);
       const size_t ri = (static_cast<size_t>(b) * p.N + n) * p.Hq + head;
       const float lse_r = p.lse[ri], d_r = p.delta[ri];
+      {
+        // This row of Q and of dO into TMEM. Every MMA of the previous unit has completed:
+        // the epilogue below waited for dq_done, committed after the last of them.
+        const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + ri * 64);
+        const uint4* osrc = reinterpret_cast<const uint4*>(p.dout + ri * 64);
+        uint32_t qa[32], oa[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 x = __ldg(qsrc + i), y = __ldg(osrc + i);
+          qa[4 * i] = x.x; qa[4 * i + 1] = x.y; qa[4 * i + 2] = x.z; qa[4 * i + 3] = x.w;
+          oa[4 * i] = y.x; oa[4 * i + 1] = y.y; oa[4 * i + 2] = y.z; oa[4 * i + 3] = y.w;
+        }
+        tmem_st32(tM + 192, qa);
+        tmem_st32(tM + 224, oa);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.qt_full[wg]);
+      }
       for (int t = 0; t < T; ++t) {
         if (!bounded_wait(&sm.sp_full[wg], (g + t) & 1, abort_flag, p.status)) {
           ok = false;
@@ -518,10 +520,10 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
         }
         tc_fence_after();
         uint32_t s[64], dp[64];
-        tmem_ld32(tS, s);
-        tmem_ld32(tS + 32, s + 32);
-        tmem_ld32(tS + 64, dp);
-        tmem_ld32(tS + 96, dp + 32);
+        tmem_ld32(tM, s);
+        tmem_ld32(tM + 32, s + 32);
+        tmem_ld32(tM + 64, dp);
+        tmem_ld32(tM + 96, dp + 32);
         tmem_ld_wait();
         reg_fence<64>(s);
         reg_fence<64>(dp);
@@ -532,7 +534,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
           const float p1 = ex2_approx(__uint_as_float(s[2 * i + 1]) * p.scale_log2 - lse_r);
           s[i] = pack_bf16x2(p0 * (__uint_as_float(dp[2 * i]) - d_r), p1 * (__uint_as_float(dp[2 * i + 1]) - d_r));
         }
-        tmem_st32(tS, s);
+        tmem_st32(tM, s);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&sm.ds_full[wg]);
@@ -550,7 +552,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
       for (int half = 0; half < 2; ++half) {
         uint32_t o[32];
         if (T > 0) {
-          tmem_ld32(tS + 128 + 32 * half, o);
+          tmem_ld32(tM + 128 + 32 * half, o);
           tmem_ld_wait();
           reg_fence<32>(o);
         } else {
@@ -567,8 +569,6 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
           dst[4 * half + i] = w;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.dq_empty[wg]);
       g += T;
     }
   }
@@ -582,11 +582,13 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
 }
 
 // ============================================================================ dK, dV
-constexpr int kStagesKv = 3;
+constexpr int kStagesKv = 4;
 constexpr int kChunkBytes = 4 * kBox;  // Q chunk (2 boxes) + dO chunk (2 boxes)
 
 struct DkvParams {
-  CUtensorMap tm_q, tm_do, tm_k, tm_v;
+  CUtensorMap tm_q, tm_do;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
   const int* offs;
   const int* list;
   const int* ucount;  // q blocks per 128-key tile
@@ -601,9 +603,8 @@ struct DkvParams {
 };
 
 struct DkvSmem {
-  uint64_t kv_full, kv_empty;
   uint64_t ch_full[kStagesKv], ch_empty[kStagesKv];
-  uint64_t sp_full[2], ps_full[2], acc_full, acc_empty;
+  uint64_t kvt_full, sp_full[2], ps_full[2], acc_full;
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -612,18 +613,19 @@ struct DkvSmem {
   alignas(16) float ndl[kStagesKv][128];   // -D of the chunk's 128 query rows
 };
 
-constexpr size_t kDkvSmemBytes = 1024 + 4 * kBox /*K, V*/ + kStagesKv * kChunkBytes + sizeof(DkvSmem);
+constexpr size_t kDkvSmemBytes = 1024 + kStagesKv * kChunkBytes + sizeof(DkvSmem);
 
 // TMEM (lanes = the 128 keys of the tile): S^T at 0 and dP^T at 128, 128 columns each
 // (one per query row of the chunk: 64 queries of head 2j, then 64 of head 2j+1).
 // Column half hf of S^T is overwritten by P^T as bf16 pairs at 64 hf + [0, 32), of
-// dP^T by dS^T at 128 + 64 hf + [0, 32). dV accumulates at 256, dK at 320.
+// dP^T by dS^T at 128 + 64 hf + [0, 32). dV accumulates at 256, dK at 320. The tile's
+// K and V rows sit at 384 and 416 as bf16 pairs, written once per unit by the row
+// threads: the A operands of S^T = K Q^T and dP^T = V dO^T, which therefore read only
+// Q / dO from shared memory.
 __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_constant__ DkvParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = tiles;              // 128 keys (2 boxes)
-  uint8_t* sV = tiles + 2 * kBox;   // 128 keys (2 boxes)
-  uint8_t* sC = tiles + 4 * kBox;   // stages: Q chunk (2 boxes) then dO chunk (2 boxes)
+  uint8_t* sC = tiles;  // stages: Q chunk (2 boxes) then dO chunk (2 boxes)
   DkvSmem& sm = *reinterpret_cast<DkvSmem*>(sC + kStagesKv * kChunkBytes);
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -631,8 +633,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
   const int per_qb = (p.bs / 64) * (G / 2);  // chunks per q block: 64-query sub-tiles x head pairs
 
   if (threadIdx.x == 0) {
-    mbar_init(&sm.kv_full, 1);
-    mbar_init(&sm.kv_empty, 1);
+    mbar_init(&sm.kvt_full, 256);
     for (int s = 0; s < kStagesKv; ++s) {
       mbar_init(&sm.ch_full[s], 1);
       mbar_init(&sm.ch_empty[s], 1);
@@ -642,7 +643,6 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
       mbar_init(&sm.ps_full[h], 128);
     }
     mbar_init(&sm.acc_full, 1);
-    mbar_init(&sm.acc_empty, 256);
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
     fence_mbar_init();
@@ -661,22 +661,12 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
   // units with chunks ("live" units).
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
-    int gc = 0, live = 0;
+    int gc = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       if (p.ucount[u] == 0) continue;
       const KeyTile kt = decode_key_tile(u, p.ktiles, p.Hk, p.N, p.bs);
       UnionWalk walk = make_walk(p.offs, p.list, kt, p.Hk, p.nkb, p.K);
-      if (live > 0 && !warp_wait(&sm.kv_empty, (live - 1) & 1, abort_flag, p.status)) {
-        ok = false;
-        break;
-      }
-      mbar_arrive_expect_tx_elect(&sm.kv_full, 4 * kBox);
-      for (int s = 0; s < 2; ++s) {
-        tma_load_2d_elect(sK + s * kBox, &p.tm_k, &sm.kv_full, kt.h * 64, kt.b * p.N + kt.key0 + 64 * s);
-        tma_load_2d_elect(sV + s * kBox, &p.tm_v, &sm.kv_full, kt.h * 64, kt.b * p.N + kt.key0 + 64 * s);
-      }
-      ++live;
       int qb, mk;
       while (ok && walk.next(qb, mk)) {
         for (int cq = 0; cq < per_qb; ++cq, ++gc) {
@@ -714,7 +704,6 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
       }
     }
     if (lane == 0) {
-      if (live > 0) wait_noabort_b(&sm.kv_full, (live - 1) & 1, p.status);
       for (int s = 0; s < kStagesKv && s < gc; ++s) {
         const int g_last = s + kStagesKv * ((gc - 1 - s) / kStagesKv);
         wait_noabort_b(&sm.ch_full[s], (g_last / kStagesKv) & 1, p.status);
@@ -729,20 +718,19 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
     // while the other finishes chunk c.
     const uint32_t id_s = make_idesc_bf16(128, 64, false);
     const uint32_t id_acc = make_idesc_bf16(128, 64, true);
-    const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sCa = smem_u32(sC);
-    const uint64_t kd = sw128_desc(sKa, 1024, 16), vd = sw128_desc(sVa, 1024, 16);
-    // S^T_h = K Q_h^T and dP^T_h = V dO_h^T of the chunk in stage st
+    const uint32_t sCa = smem_u32(sC);
+    // S^T_h = K Q_h^T and dP^T_h = V dO_h^T of the chunk in stage st (K, V from TMEM)
     auto issue_ss = [&](int h, int st) {
       const uint32_t cq = sCa + st * kChunkBytes + h * kBox, cdo = cq + 2 * kBox;
       const uint64_t qk = sw128_desc(cq, 1024, 16), dok = sw128_desc(cdo, 1024, 16);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_ss_elect(tmem + 64u * h, kd + static_cast<uint64_t>(2 * ks), qk + static_cast<uint64_t>(2 * ks), id_s,
+        mma_ts_elect(tmem + 64u * h, tmem + 384u + 8u * ks, qk + static_cast<uint64_t>(2 * ks), id_s,
                      ks > 0 ? 1u : 0u);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_ss_elect(tmem + 128u + 64u * h, vd + static_cast<uint64_t>(2 * ks), dok + static_cast<uint64_t>(2 * ks),
-                     id_s, ks > 0 ? 1u : 0u);
+        mma_ts_elect(tmem + 128u + 64u * h, tmem + 416u + 8u * ks, dok + static_cast<uint64_t>(2 * ks), id_s,
+                     ks > 0 ? 1u : 0u);
       tc_commit_elect(&sm.sp_full[h]);
     };
     // dV += P^T_h dO_h and dK += dS^T_h Q_h (P^T_h / dS^T_h as bf16 pairs in TMEM)
@@ -763,7 +751,9 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const int nch = p.ucount[u] * per_qb;
       if (nch == 0) continue;
-      ok = warp_wait(&sm.kv_full, live & 1, abort_flag, p.status) &&
+      // kvt_full: the rows have written this tile's K / V into TMEM, after reading the
+      // previous live unit's dK / dV (so those may be overwritten too).
+      ok = warp_wait(&sm.kvt_full, live & 1, abort_flag, p.status) &&
            warp_wait(&sm.ch_full[gc % kStagesKv], (gc / kStagesKv) & 1, abort_flag, p.status);
       tc_fence_after();
       if (!ok) break;
@@ -773,8 +763,6 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
         const int g = gc + c, st = g % kStagesKv;
         for (int h = 0; ok && h < 2; ++h) {
           ok = warp_wait(&sm.ps_full[h], g & 1, abort_flag, p.status);
-          // The epilogue of the previous live unit must have read dK / dV first.
-          if (ok && c == 0 && h == 0 && live > 0) ok = warp_wait(&sm.acc_empty, (live - 1) & 1, abort_flag, p.status);
           tc_fence_after();
           if (!ok) break;
           issue_ts(h, st, c == 0 && h == 0);
@@ -792,8 +780,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
         if (ok) tc_commit_elect(&sm.ch_empty[st]);  // every read of this chunk's stage is issued
       }
       if (!ok) break;
-      tc_commit_elect(&sm.acc_full);
-      tc_commit_elect(&sm.kv_empty);
+      tc_commit_elect(&sm.acc_full);  // every MMA of the unit, K / V reads included
       ++live;
       gc += nch;
     }
@@ -812,6 +799,28 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const KeyTile kt = decode_key_tile(u, p.ktiles, p.Hk, p.N, p.bs);
       const int nch = p.ucount[u] * per_qb;
+      const int key = kt.key0 + kr;
+      if (nch > 0) {
+        // This key's K row (warpgroup 0) or V row (warpgroup 1) into TMEM. Every MMA of
+        // the previous live unit has completed: its epilogue below waited for acc_full.
+        uint32_t kv[32];
+        if (key < p.N) {
+          const uint4* src = reinterpret_cast<const uint4*>(
+              (hf == 0 ? p.k : p.v) + ((static_cast<size_t>(kt.b) * p.N + key) * p.Hk + kt.h) * 64);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 x = __ldg(src + i);
+            kv[4 * i] = x.x; kv[4 * i + 1] = x.y; kv[4 * i + 2] = x.z; kv[4 * i + 3] = x.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) kv[i] = 0u;
+        }
+        tmem_st32(tT + 384 + 32 * hf, kv);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.kvt_full);
+      }
       for (int c = 0; c < nch; ++c, ++gc) {
         const int st = gc % kStagesKv;
         // ch_full orders the producer's lse / D / mask writes before these reads
@@ -857,14 +866,11 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
         tmem_ld32(tT + 256 + 64 * hf + 32, o + 32);
         tmem_ld_wait();
         reg_fence<64>(o);
-        tc_fence_before();
-        mbar_arrive(&sm.acc_empty);
         ++live;
       } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i) o[i] = 0u;
       }
-      const int key = kt.key0 + kr;
       if (key < p.N) {
         const float f = hf == 0 ? 1.0f : p.scale;
         __nv_bfloat16* out = hf == 0 ? p.dv : p.dk;
@@ -978,11 +984,16 @@ int launch_sparse_bwd(const SparseBwdLaunch& a, cudaStream_t stream) {
       make_tmap_bf16_2d(&tm_k, a.k, static_cast<uint64_t>(B) * N, static_cast<uint64_t>(Hk) * 64) ||
       make_tmap_bf16_2d(&tm_v, a.v, static_cast<uint64_t>(B) * N, static_cast<uint64_t>(Hk) * 64))
     return MOSAIC_ERR_CUDA;
+  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(a.q);
+  const __nv_bfloat16* kb = static_cast<const __nv_bfloat16*>(a.k);
+  const __nv_bfloat16* vb = static_cast<const __nv_bfloat16*>(a.v);
+  const __nv_bfloat16* gob = static_cast<const __nv_bfloat16*>(a.grad_out);
   // dQ
   {
     DqParams p;
     memset(&p, 0, sizeof(p));
-    p.tm_q = tm_q; p.tm_do = tm_do; p.tm_k = tm_k; p.tm_v = tm_v;
+    p.tm_k = tm_k; p.tm_v = tm_v;
+    p.q = qb; p.dout = gob;
     p.block_idx = a.block_idx;
     p.lse = a.lse;
     p.delta = delta;
@@ -1004,7 +1015,8 @@ int launch_sparse_bwd(const SparseBwdLaunch& a, cudaStream_t stream) {
   {
     DkvParams p;
     memset(&p, 0, sizeof(p));
-    p.tm_q = tm_q; p.tm_do = tm_do; p.tm_k = tm_k; p.tm_v = tm_v;
+    p.tm_q = tm_q; p.tm_do = tm_do;
+    p.k = kb; p.v = vb;
     p.offs = offs;
     p.list = sorted;
     p.ucount = ucount;
