@@ -23,6 +23,10 @@ them; `roofline` uses the fused kernel (c) from that loop.
 deeper U-Net stages, the Nside 128 / 256 stress cases) instead; X128 / X256 also
 time cuDNN dense SDPA on the same inputs (`dense_sdpa`).
 
+The line also carries `backward`: the device time of mosaic_sparse_attn's backward
+(the training path of the selected branch, ops.mosaic_attn_bwd) on the same workload
+and its FLOP rate against the measured bf16 peak (--no-backward skips it).
+
 `--impl reference` times the reference algorithm on the host cores instead: the
 reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
 the oracle port (oracle/bsa_oracle.py), run on a bounded sample of the same
@@ -82,6 +86,7 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="S1")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-backward", action="store_true")
     return p.parse_args()
 
 
@@ -96,6 +101,47 @@ def peaks():
 def flops_attend(c):
     """FLOP of kernel (c): QK^T and PV over K*bs selected + bas local keys, 2 FLOP/MAC."""
     return 4 * c["B"] * c["N"] * c["Hq"] * c["D"] * (c["K"] * c["bs"] + c["bas"])
+
+
+def flops_backward(c):
+    """FLOP of the selected-block attention backward: per (query row, head, selected key)
+    S, dP and dQ (3 x 128) in the dQ kernel and S^T, dP^T, dV, dK (4 x 128) in the dK/dV
+    kernel, 2 FLOP/MAC over head_dim 64."""
+    return 896 * c["B"] * c["N"] * c["Hq"] * c["K"] * c["bs"]
+
+
+def backward_leg(c, sets, stream, steps, warmup):
+    """Device time of mosaic_sparse_attn's backward (ops.mosaic_attn_bwd) on the
+    workload's selected branch, with the selection top-k made on each input set."""
+    import mosaic_b200 as M
+    from mosaic_b200 import ops as mops
+
+    scale = c["D"] ** -0.5
+    legs = []
+    for x in sets[:4]:
+        qc, kc, _ = M.block_pool(x["q"], x["k"], x["v"], c["bs"])
+        idx = M.attn_topk(qc, kc, c["K"])
+        out, lse = mops.mosaic_attn_fwd(x["q"], x["k"], x["v"], idx, c["bs"], scale)
+        go = torch.randn_like(x["q"], dtype=torch.float32).bfloat16()
+        legs.append((x, idx, out, lse, go))
+    status = mops.status_buffer(sets[0]["q"].device)
+
+    def step(i):
+        x, idx, out, lse, go = legs[i % len(legs)]
+        mops.mosaic_attn_bwd(x["q"], x["k"], x["v"], out, lse, go, scale, idx, c["bs"], status=status)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        step(i)
+    b.record(stream)
+    torch.cuda.synchronize()
+    if int(status.item()):
+        raise RuntimeError(f"device status {int(status.item())} after the backward leg")
+    return a.elapsed_time(b) / steps
 
 
 def bytes_pool(c):
@@ -434,6 +480,15 @@ def b200_arm(args):
                          f"after 1 warm-up, {secs:.1f} s"}
 
     hbm, tf, src = peaks()
+    bwd = None
+    if not args.no_backward:
+        n_bwd = max(3, min(args.steps, 50))
+        bwd_ms = backward_leg(c, sets, stream, n_bwd, max(3, args.warmup))
+        bwd = {"what": "mosaic_sparse_attn backward (ops.mosaic_attn_bwd: D, inverted block index, dQ and dK/dV "
+                       "tcgen05 kernels) on this workload's selected branch, top-k selection of each input set",
+               "ms": bwd_ms, "steps": n_bwd, "flop_per_step": flops_backward(c),
+               "achieved_tflops": flops_backward(c) / (bwd_ms / 1000) / 1e12, "peak_tflops": tf,
+               "frac": flops_backward(c) / (bwd_ms / 1000) / 1e12 / tf}
     t_att = stage_ms[3] / 1000.0
     achieved = flops_attend(c) / t_att / 1e12
     line = {
@@ -461,6 +516,8 @@ def b200_arm(args):
     }
     if sdpa is not None:
         line["dense_sdpa"] = sdpa
+    if bwd is not None:
+        line["backward"] = bwd
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -311,10 +311,8 @@ constexpr int kStagesDq = 8;
 constexpr int kMaxSelB = 1024;
 
 struct DqParams {
-  CUtensorMap tm_k, tm_v;
+  CUtensorMap tm_q, tm_do, tm_k, tm_v;
   const int64_t* block_idx;
-  const __nv_bfloat16* q;
-  const __nv_bfloat16* dout;
   const float* lse;
   const float* delta;
   __nv_bfloat16* dq;
@@ -326,6 +324,7 @@ struct DqParams {
 
 struct DqSmem {
   uint64_t kv_full[kStagesDq], kv_empty[kStagesDq];
+  uint64_t qs_full, qs_empty;  // the shared-memory staging buffer of the next unit's Q / dO
   uint64_t qt_full[2], sp_full[2], ds_full[2], dq_done[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -333,17 +332,20 @@ struct DqSmem {
   int sel[kMaxSelB];
 };
 
-constexpr size_t kDqSmemBytes = 1024 + 2 * kStagesDq * kBox /*K, V*/ + sizeof(DqSmem);
+constexpr size_t kDqSmemBytes = 1024 + 8 * kBox /*Q, dO staging*/ + 2 * kStagesDq * kBox /*K, V*/ + sizeof(DqSmem);
 
 // TMEM of M-tile m (query heads 2m, 2m+1 of the group) at 256m: S (64 columns; dS
 // overwrites its first 32 as bf16 pairs), dP at +64, dQ at +128, and the unit's Q and
 // dO rows as bf16 pairs at +192 and +224: the A operands of S = Q K^T and dP = dO V^T,
-// written once per unit by the row threads, so those MMAs read only K / V from shared
-// memory.
+// written once per unit by the row threads from a shared-memory staging buffer that
+// the producer fills for the next unit while the current one runs, so those MMAs read
+// only K / V from shared memory.
 __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constant__ DqParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = tiles;                   // stages
+  uint8_t* sQ = tiles;                   // staging: boxes j = 0..3 (head j of the group)
+  uint8_t* sDO = tiles + 4 * kBox;       // same layout
+  uint8_t* sK = tiles + 8 * kBox;        // stages
   uint8_t* sV = sK + kStagesDq * kBox;   // stages
   DqSmem& sm = *reinterpret_cast<DqSmem*>(sV + kStagesDq * kBox);
   volatile int* abort_flag = &sm.abort_flag;
@@ -357,6 +359,8 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
     }
+    mbar_init(&sm.qs_full, 1);
+    mbar_init(&sm.qs_empty, 256);
     for (int m = 0; m < 2; ++m) {
       mbar_init(&sm.qt_full[m], 128);
       mbar_init(&sm.sp_full[m], 1);
@@ -377,8 +381,10 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer (K / V tiles)
-    int g = 0;  // K/V tiles issued
+    // ---------------------------------------------------------------- TMA producer
+    // Per unit: its Q / dO boxes into the staging buffer (free once the rows copied the
+    // previous unit's into TMEM, at that unit's start), then its K / V tiles.
+    int g = 0, nq = 0;  // K/V tiles and Q/dO stagings issued
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const int qt = u % p.qtiles, rest = u / p.qtiles;
@@ -395,6 +401,17 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
         sm.sel[s] = static_cast<int>(v);
       }
       __syncwarp();
+      if (nq > 0 && !warp_wait(&sm.qs_empty, (nq - 1) & 1, abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx_elect(&sm.qs_full, 8 * kBox);
+      for (int j = 0; j < 4; ++j) {
+        const int col = (h * G + j) * 64, row = b * p.N + qt * 64;
+        tma_load_2d_elect(sQ + j * kBox, &p.tm_q, &sm.qs_full, col, row);
+        tma_load_2d_elect(sDO + j * kBox, &p.tm_do, &sm.qs_full, col, row);
+      }
+      ++nq;
       for (int t = 0; t < T; ++t, ++g) {
         const int st = g % kStagesDq, r = g / kStagesDq;
         if (r > 0 && !warp_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) {
@@ -409,6 +426,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
     }
     // Drain: every TMA write into shared memory lands before the CTA exits.
     if (lane == 0) {
+      if (nq > 0) wait_noabort_b(&sm.qs_full, (nq - 1) & 1, p.status);
       for (int s = 0; s < kStagesDq && s < g; ++s) {
         const int g_last = s + kStagesDq * ((g - 1 - s) / kStagesDq);
         wait_noabort_b(&sm.kv_full[s], (g_last / kStagesDq) & 1, p.status);
@@ -496,17 +514,26 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
       const size_t ri = (static_cast<size_t>(b) * p.N + n) * p.Hq + head;
       const float lse_r = p.lse[ri], d_r = p.delta[ri];
       {
-        // This row of Q and of dO into TMEM. Every MMA of the previous unit has completed:
-        // the epilogue below waited for dq_done, committed after the last of them.
-        const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + ri * 64);
-        const uint4* osrc = reinterpret_cast<const uint4*>(p.dout + ri * 64);
+        // This row of Q and of dO, from the staging buffer (a 128-byte-swizzled TMA box:
+        // 16-byte chunk c of box row r sits at chunk c ^ (r & 7)), into TMEM. Every MMA
+        // of the previous unit has completed: its epilogue below waited for dq_done,
+        // committed after the last of them.
+        if (!bounded_wait(&sm.qs_full, it & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        const int r = row & 63;
+        const uint8_t* qrow = sQ + (2 * wg + (row >> 6)) * kBox + r * 128;
+        const uint8_t* orow = sDO + (2 * wg + (row >> 6)) * kBox + r * 128;
         uint32_t qa[32], oa[32];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint4 x = __ldg(qsrc + i), y = __ldg(osrc + i);
-          qa[4 * i] = x.x; qa[4 * i + 1] = x.y; qa[4 * i + 2] = x.z; qa[4 * i + 3] = x.w;
-          oa[4 * i] = y.x; oa[4 * i + 1] = y.y; oa[4 * i + 2] = y.z; oa[4 * i + 3] = y.w;
+        for (int c = 0; c < 8; ++c) {
+          const uint4 x = *reinterpret_cast<const uint4*>(qrow + ((c ^ (r & 7)) << 4));
+          const uint4 y = *reinterpret_cast<const uint4*>(orow + ((c ^ (r & 7)) << 4));
+          qa[4 * c] = x.x; qa[4 * c + 1] = x.y; qa[4 * c + 2] = x.z; qa[4 * c + 3] = x.w;
+          oa[4 * c] = y.x; oa[4 * c + 1] = y.y; oa[4 * c + 2] = y.z; oa[4 * c + 3] = y.w;
         }
+        mbar_arrive(&sm.qs_empty);
         tmem_st32(tM + 192, qa);
         tmem_st32(tM + 224, oa);
         tmem_st_wait();
@@ -984,16 +1011,13 @@ int launch_sparse_bwd(const SparseBwdLaunch& a, cudaStream_t stream) {
       make_tmap_bf16_2d(&tm_k, a.k, static_cast<uint64_t>(B) * N, static_cast<uint64_t>(Hk) * 64) ||
       make_tmap_bf16_2d(&tm_v, a.v, static_cast<uint64_t>(B) * N, static_cast<uint64_t>(Hk) * 64))
     return MOSAIC_ERR_CUDA;
-  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(a.q);
   const __nv_bfloat16* kb = static_cast<const __nv_bfloat16*>(a.k);
   const __nv_bfloat16* vb = static_cast<const __nv_bfloat16*>(a.v);
-  const __nv_bfloat16* gob = static_cast<const __nv_bfloat16*>(a.grad_out);
   // dQ
   {
     DqParams p;
     memset(&p, 0, sizeof(p));
-    p.tm_k = tm_k; p.tm_v = tm_v;
-    p.q = qb; p.dout = gob;
+    p.tm_q = tm_q; p.tm_do = tm_do; p.tm_k = tm_k; p.tm_v = tm_v;
     p.block_idx = a.block_idx;
     p.lse = a.lse;
     p.delta = delta;
