@@ -177,6 +177,25 @@ MOSAIC_API int mosaic_sparse_attn_bwd(const void* q, const void* k, const void* 
                                       int num_kv_heads, int head_dim, int block_size, int block_count,
                                       float softmax_scale, void* stream);
 
+/* Input projections of primitives.MosaicAttention.forward (primitives.py:182-194):
+ * [q | k | v | gate logits] = x W^T with W = cat(to_q.weight, to_k.weight, to_v.weight,
+ * to_strategy_combine_mlp.weight) ([(Hq + 2 Hk) 64 + 3 Hq, dim] bf16; without the gate
+ * rows when gates is NULL), x [S, B, dim] bf16 (sequence-first). Writes, in the layouts
+ * mosaic_bsa_fwd takes: q [B, S, Hq, 64] and k, v [B, S, Hk, 64] bf16, with Mosaic's 2D
+ * RoPE (RoPE.forward, primitives.py:132-135) applied to q and k when rope_cos/rope_sin
+ * ([S, 32] fp32) are given; gates [3, B, S, Hq] bf16 = softmax over the three strategies
+ * of the bf16 gate logits (generate_strategy_weights, primitives.py:172-178).
+ * head_dim 64, dim a multiple of 64, Hq <= 21 with gates. */
+MOSAIC_API int mosaic_attn_qkv_proj(const void* x, const void* w_qkvg, const float* rope_cos, const float* rope_sin,
+                                    void* q, void* k, void* v, void* gates, int* status, int seq_len, int batch,
+                                    int dim, int num_q_heads, int num_kv_heads, int head_dim, void* stream);
+
+/* Output projection of primitives.MosaicAttention.forward (primitives.py:207-208):
+ * out [S, B, dim] = rearrange(attn, 'b s h d -> s b (h d)') to_o.weight^T, attn
+ * [B, S, Hq, 64] bf16 (mosaic_bsa_fwd's output), w_o [dim, Hq*64] bf16. */
+MOSAIC_API int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* status, int seq_len,
+                                    int batch, int dim, int num_q_heads, int head_dim, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

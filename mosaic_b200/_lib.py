@@ -52,6 +52,8 @@ SIGNATURES = {
     "mosaic_attn_topk": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp], _i),
     "mosaic_sparse_attn_bwd_workspace_bytes": ([_i] * 7, _sz),
     "mosaic_sparse_attn_bwd": ([_vp] * 10 + [_vp, _sz, _vp] + [_i] * 7 + [_f, _vp], _i),
+    "mosaic_attn_qkv_proj": ([_vp] * 9 + [_i] * 6 + [_vp], _i),
+    "mosaic_attn_out_proj": ([_vp] * 4 + [_i] * 5 + [_vp], _i),
 }
 
 EXPECTED_ABI_VERSION = 1

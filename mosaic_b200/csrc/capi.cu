@@ -411,4 +411,40 @@ int mosaic_sparse_attn_bwd(const void* q, const void* k, const void* v, const vo
   return launch_sparse_bwd(a, static_cast<cudaStream_t>(stream));
 }
 
+int mosaic_attn_qkv_proj(const void* x, const void* w_qkvg, const float* rope_cos, const float* rope_sin, void* q,
+                         void* k, void* v, void* gates, int* status, int seq_len, int batch, int dim,
+                         int num_q_heads, int num_kv_heads, int head_dim, void* stream) {
+  if (seq_len < 0 || batch < 0 || dim <= 0 || num_q_heads <= 0 || num_kv_heads <= 0)
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
+  if (dim % 64 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (gates != nullptr && num_q_heads > 21) return MOSAIC_ERR_UNSUPPORTED;  // 3 Hq gate columns fit one 64-column group
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (seq_len == 0 || batch == 0) return MOSAIC_OK;
+  if (!x || !w_qkvg || !q || !k || !v) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(w_qkvg) || !aligned16(q) || !aligned16(k) || !aligned16(v))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  QkvProjLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.x = x; a.w = w_qkvg; a.rope_cos = rope_cos; a.rope_sin = rope_sin;
+  a.q = q; a.k = k; a.v = v; a.gates = gates; a.status = status;
+  a.S = seq_len; a.B = batch; a.dim = dim; a.Hq = num_q_heads; a.Hk = num_kv_heads;
+  return launch_qkv_proj(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* status, int seq_len, int batch, int dim,
+                         int num_q_heads, int head_dim, void* stream) {
+  if (seq_len < 0 || batch < 0 || dim <= 0 || num_q_heads <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
+  if (dim % 8 != 0) return MOSAIC_ERR_UNSUPPORTED;  // 16-byte rows for the weight's tensor map and the stores
+  if (seq_len == 0 || batch == 0) return MOSAIC_OK;
+  if (!attn || !w_o || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(attn) || !aligned16(w_o) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  OutProjLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.attn = attn; a.w = w_o; a.out = out; a.status = status;
+  a.S = seq_len; a.B = batch; a.dim = dim; a.Hq = num_q_heads;
+  return launch_out_proj(a, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

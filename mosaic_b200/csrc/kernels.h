@@ -97,6 +97,29 @@ SparseBwdWorkspace sparse_bwd_workspace(int B, int N, int Hq, int Hk, int bs, in
 int sparse_bwd_max_selected();
 int launch_sparse_bwd(const SparseBwdLaunch& a, cudaStream_t stream);
 
+// Projections around the attention op (proj.cu).
+struct QkvProjLaunch {
+  const void* x;          // [S, B, dim] bf16
+  const void* w;          // [(Hq + 2 Hk) 64 (+ 3 Hq), dim] bf16 = cat(to_q, to_k, to_v[, gate]) weights
+  const float* rope_cos;  // [S, 32] fp32 or null
+  const float* rope_sin;
+  void* q;                // [B, S, Hq, 64] bf16
+  void* k;                // [B, S, Hk, 64] bf16
+  void* v;                // [B, S, Hk, 64] bf16
+  void* gates;            // [3, B, S, Hq] bf16 or null (then w has no gate rows)
+  int* status;
+  int S, B, dim, Hq, Hk;
+};
+struct OutProjLaunch {
+  const void* attn;  // [B, S, Hq*64] bf16
+  const void* w;     // [dim, Hq*64] bf16 (to_o.weight)
+  void* out;         // [S, B, dim] bf16
+  int* status;
+  int S, B, dim, Hq;
+};
+int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream);
+int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream);
+
 int launch_engine(const EngineLaunch& a, cudaStream_t stream);
 int launch_pool(const PoolLaunch& a, cudaStream_t stream);
 int launch_topk(const TopkLaunch& a, cudaStream_t stream);

@@ -1,0 +1,371 @@
+// The linear projections around the attention op (primitives.MosaicAttention,
+// primitives.py:139-209) as one persistent tcgen05 GEMM with two epilogues.
+//
+//   mode kQkv:   [q | k | v | gate logits] = x W^T for W = cat(to_q, to_k, to_v,
+//                to_strategy_combine_mlp) weights, x [S, B, dim] (sequence-first, as
+//                MosaicAttention.forward receives it). The epilogue rounds each output
+//                to bf16 (the Linear's output dtype), applies Mosaic's 2D RoPE to q
+//                and k (RoPE.forward, primitives.py:132-135, same fp32 operation order
+//                as pool.cu), softmaxes the gate logits over the three strategies in
+//                fp32 (generate_strategy_weights, primitives.py:172-178) and writes
+//                q [B, S, Hq, 64], k, v [B, S, Hk, 64] and gates [3, B, S, Hq] bf16:
+//                the layouts mosaic_attn_func takes (the rearranges of
+//                primitives.py:187-189,175 become epilogue addressing).
+//   mode kPlain: out = a W^T for the output projection to_o, with a the attention
+//                output [B, S, Hq*64] and out [S, B, dim] (the rearrange of
+//                primitives.py:207 is epilogue addressing).
+//
+// Tiles of 128 rows x 256 columns, K in 64-wide stages (TMA, 128-byte swizzle, 4-stage
+// ring), fp32 accumulators double-buffered in TMEM so the epilogue of one tile runs
+// under the MMAs of the next. Warp 0 loads, warp 1 issues the MMAs (one elected lane of
+// a converged warp), warps 4-7 run the epilogue, one output row per thread. Every wait
+// is bounded; no TMA multicast.
+#include <cstring>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace mosaic {
+namespace {
+
+constexpr int kPBM = 128, kPBN = 256, kPBK = 64, kPStages = 4;
+constexpr int kPThreads = 256;              // warp 0 TMA, warp 1 MMA, warps 2-3 idle, warps 4-7 epilogue
+constexpr int kPBox = 64 * 128;             // one 64-row x 64-column bf16 box
+constexpr int kPABytes = kPBM * kPBK * 2;   // 16 KB
+constexpr int kPBBytes = kPBN * kPBK * 2;   // 32 KB
+constexpr int kPStageBytes = kPABytes + kPBBytes;
+
+enum ProjMode : int { kQkv = 0, kPlain = 1 };
+
+struct ProjParams {
+  CUtensorMap tm_a, tm_w;
+  __nv_bfloat16* q;
+  __nv_bfloat16* k;
+  __nv_bfloat16* v;
+  __nv_bfloat16* g;        // gates [3, B, S, Hq] or null
+  const float* rope_cos;   // [S, 32] or null
+  const float* rope_sin;
+  __nv_bfloat16* out;      // kPlain
+  int* status;
+  int mode;
+  int M, K, N;             // GEMM: M rows of A, K, N output columns
+  int S, B, Hq, Hk;
+  int m_tiles, n_tiles, tiles, k_blocks;
+};
+
+struct ProjSmem {
+  uint64_t full[kPStages], empty[kPStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr size_t kProjSmemBytes = 1024 + kPStages * kPStageBytes + sizeof(ProjSmem);
+
+__device__ __forceinline__ bool wait_noabort_p(uint64_t* bar, uint32_t parity, int* status) {
+  int dummy = 0;
+  return bounded_wait(bar, parity, &dummy, status);
+}
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// 32 consecutive output columns of one row (fp32 accumulators) -> bf16, with RoPE when
+// cos / sin are given (pair i of the chunk uses frequency p0 + i). The reference rounds
+// the Linear output to bf16 first, then rotates in fp32: out[2i] = x[2i] cos - x[2i+1]
+// sin and out[2i+1] = x[2i+1] cos + x[2i] sin, each product and the sum rounded.
+__device__ __forceinline__ void store_chunk(uint4* dst, const uint32_t (&acc)[32], const float* cos_row,
+                                            const float* sin_row, int p0) {
+  uint32_t packed[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
+    if (cos_row != nullptr) {
+      const float c = __ldg(cos_row + p0 + i), s = __ldg(sin_row + p0 + i);
+      const float o0 = __fadd_rn(__fmul_rn(x0, c), __fmul_rn(-x1, s));
+      const float o1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+      x0 = o0;
+      x1 = o1;
+    }
+    packed[i] = pack_bf16x2(x0, x1);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+}
+
+__global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constant__ ProjParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  ProjSmem& sm = *reinterpret_cast<ProjSmem*>(tiles + kPStages * kPStageBytes);
+  volatile int* abort_flag = &sm.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], 128);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    int g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+      const int mt = t / p.n_tiles, nt = t % p.n_tiles;
+      for (int kb = 0; kb < p.k_blocks; ++kb, ++g) {
+        const int st = g % kPStages, r = g / kPStages;
+        if (r > 0 && !warp_wait(&sm.empty[st], (r - 1) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = tiles + st * kPStageBytes;
+        uint8_t* sb = sa + kPABytes;
+        mbar_arrive_expect_tx_elect(&sm.full[st], kPStageBytes);
+        for (int i = 0; i < 2; ++i) tma_load_2d_elect(sa + i * kPBox, &p.tm_a, &sm.full[st], kb * kPBK, mt * kPBM + 64 * i);
+        for (int i = 0; i < 4; ++i) tma_load_2d_elect(sb + i * kPBox, &p.tm_w, &sm.full[st], kb * kPBK, nt * kPBN + 64 * i);
+      }
+    }
+    if (lane == 0) {
+      for (int s = 0; s < kPStages && s < g; ++s) {
+        const int g_last = s + kPStages * ((g - 1 - s) / kPStages);
+        wait_noabort_p(&sm.full[s], (g_last / kPStages) & 1, p.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    const uint32_t idesc = make_idesc_bf16(kPBM, kPBN, false);
+    const uint32_t sbase = smem_u32(tiles);
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++it) {
+      const int a = it & 1;
+      // The epilogue must have read this accumulator's previous tile.
+      if (it >= 2) ok = warp_wait(&sm.acc_empty[a], ((it >> 1) - 1) & 1, abort_flag, p.status);
+      tc_fence_after();
+      for (int kb = 0; ok && kb < p.k_blocks; ++kb, ++g) {
+        const int st = g % kPStages;
+        if (!warp_wait(&sm.full[st], (g / kPStages) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(sbase + st * kPStageBytes, 1024, 16);
+        const uint64_t bd = sw128_desc(sbase + st * kPStageBytes + kPABytes, 1024, 16);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_ss_elect(tmem + 256u * a, ad + static_cast<uint64_t>(2 * ks), bd + static_cast<uint64_t>(2 * ks), idesc,
+                       (kb > 0 || ks > 0) ? 1u : 0u);
+        tc_commit_elect(&sm.empty[st]);
+      }
+      if (!ok) break;
+      tc_commit_elect(&sm.acc_full[a]);
+    }
+    tc_commit_elect(&sm.drain);
+    if (lane == 0) wait_noabort_p(&sm.drain, 0, p.status);
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- epilogue, one output row per thread
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int qcols = p.Hq * 64, kcols = p.Hk * 64;
+    const int gbase = qcols + 2 * kcols;  // first gate-logit column (kQkv)
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++it) {
+      const int a = it & 1;
+      const int mt = t / p.n_tiles, nt = t % p.n_tiles;
+      if (!bounded_wait(&sm.acc_full[a], (it >> 1) & 1, abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int m = mt * kPBM + row;
+      const bool live = m < p.M;
+      const uint32_t tacc = tmem + lane_off + 256u * a;
+#pragma unroll 1
+      for (int ci = 0; ci < kPBN / 32; ++ci) {
+        const int c0 = nt * kPBN + 32 * ci;  // warp-uniform
+        if (c0 >= p.N) break;
+        uint32_t acc[32];
+        if (p.mode == kPlain) {
+          tmem_ld32(tacc + 32 * ci, acc);
+          tmem_ld_wait();
+          reg_fence<32>(acc);
+          if (live) {
+            // A rows are (b, s) (attention output), out rows (s, b)
+            const int b = m / p.S, s = m % p.S;
+            store_chunk(reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(s) * p.B + b) * p.N + c0), acc,
+                        nullptr, nullptr, 0);
+          }
+          continue;
+        }
+        const int s = m / p.B, b = m % p.B;  // x rows are (s, b)
+        if (c0 < gbase) {
+          tmem_ld32(tacc + 32 * ci, acc);
+          tmem_ld_wait();
+          reg_fence<32>(acc);
+          if (!live) continue;
+          __nv_bfloat16* dst;
+          const float* cr = nullptr;
+          const float* sr = nullptr;
+          int d0;
+          if (c0 < qcols) {
+            d0 = c0 % 64;
+            dst = p.q + ((static_cast<size_t>(b) * p.S + s) * p.Hq + c0 / 64) * 64 + d0;
+            if (p.rope_cos) {
+              cr = p.rope_cos + static_cast<size_t>(s) * 32;
+              sr = p.rope_sin + static_cast<size_t>(s) * 32;
+            }
+          } else if (c0 < qcols + kcols) {
+            d0 = (c0 - qcols) % 64;
+            dst = p.k + ((static_cast<size_t>(b) * p.S + s) * p.Hk + (c0 - qcols) / 64) * 64 + d0;
+            if (p.rope_cos) {
+              cr = p.rope_cos + static_cast<size_t>(s) * 32;
+              sr = p.rope_sin + static_cast<size_t>(s) * 32;
+            }
+          } else {
+            d0 = (c0 - qcols - kcols) % 64;
+            dst = p.v + ((static_cast<size_t>(b) * p.S + s) * p.Hk + (c0 - qcols - kcols) / 64) * 64 + d0;
+          }
+          store_chunk(reinterpret_cast<uint4*>(dst), acc, cr, sr, d0 / 2);
+        } else if (c0 == gbase) {
+          // The 3 Hq gate logits (at most 64 columns, starting 64-aligned, so inside this
+          // tile): logits are bf16 Linear outputs laid out (head, strategy); softmax over
+          // the three strategies in fp32, rounded to bf16.
+          uint32_t hi[32];
+          tmem_ld32(tacc + 32 * ci, acc);
+          tmem_ld32(tacc + 32 * ci + 32, hi);
+          tmem_ld_wait();
+          reg_fence<32>(acc);
+          reg_fence<32>(hi);
+          if (live && p.g != nullptr) {
+#pragma unroll
+            for (int h = 0; h < 21; ++h) {
+              if (h >= p.Hq) break;
+              float l[3];
+#pragma unroll
+              for (int j = 0; j < 3; ++j) {
+                const int e = 3 * h + j;
+                l[j] = bf16_round(__uint_as_float(e < 32 ? acc[e & 31] : hi[(e - 32) & 31]));
+              }
+              const float mx = fmaxf(fmaxf(l[0], l[1]), l[2]);
+              const float e0 = expf(l[0] - mx), e1 = expf(l[1] - mx), e2 = expf(l[2] - mx);
+              const float sum = e0 + e1 + e2;
+              const size_t plane = static_cast<size_t>(p.B) * p.S * p.Hq;
+              const size_t o = (static_cast<size_t>(b) * p.S + s) * p.Hq + h;
+              p.g[o] = __float2bfloat16_rn(e0 / sum);
+              p.g[plane + o] = __float2bfloat16_rn(e1 / sum);
+              p.g[2 * plane + o] = __float2bfloat16_rn(e2 / sum);
+            }
+          }
+          ++ci;  // the second chunk was consumed with the first
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.acc_empty[a]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int sm_count_p() {
+  static int count[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (count[dev] == 0 && cudaDeviceGetAttribute(&count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 0;
+  return count[dev];
+}
+
+int launch_proj(ProjParams& p, cudaStream_t stream) {
+  static bool done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOSAIC_ERR_CUDA;
+  if (!done[dev]) {
+    if (cudaFuncSetAttribute(proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kProjSmemBytes)) != cudaSuccess)
+      return MOSAIC_ERR_CUDA;
+    done[dev] = true;
+  }
+  const int sms = sm_count_p();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  p.m_tiles = (p.M + kPBM - 1) / kPBM;
+  p.n_tiles = (p.N + kPBN - 1) / kPBN;
+  p.tiles = p.m_tiles * p.n_tiles;
+  p.k_blocks = p.K / kPBK;
+  const int grid = p.tiles < sms ? p.tiles : sms;
+  if (grid > 0) proj_kernel<<<grid, kPThreads, kProjSmemBytes, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+}  // namespace
+
+int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream) {
+  ProjParams p;
+  memset(&p, 0, sizeof(p));
+  const int n = (a.Hq + 2 * a.Hk) * 64 + (a.gates ? 3 * a.Hq : 0);
+  if (make_tmap_bf16_2d(&p.tm_a, a.x, static_cast<uint64_t>(a.S) * a.B, static_cast<uint64_t>(a.dim)) ||
+      make_tmap_bf16_2d(&p.tm_w, a.w, static_cast<uint64_t>(n), static_cast<uint64_t>(a.dim)))
+    return MOSAIC_ERR_CUDA;
+  p.q = static_cast<__nv_bfloat16*>(a.q);
+  p.k = static_cast<__nv_bfloat16*>(a.k);
+  p.v = static_cast<__nv_bfloat16*>(a.v);
+  p.g = static_cast<__nv_bfloat16*>(a.gates);
+  p.rope_cos = a.rope_cos;
+  p.rope_sin = a.rope_sin;
+  p.status = a.status;
+  p.mode = kQkv;
+  p.M = a.S * a.B;
+  p.K = a.dim;
+  p.N = n;
+  p.S = a.S;
+  p.B = a.B;
+  p.Hq = a.Hq;
+  p.Hk = a.Hk;
+  return launch_proj(p, stream);
+}
+
+int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream) {
+  ProjParams p;
+  memset(&p, 0, sizeof(p));
+  const int kdim = a.Hq * 64;
+  if (make_tmap_bf16_2d(&p.tm_a, a.attn, static_cast<uint64_t>(a.S) * a.B, static_cast<uint64_t>(kdim)) ||
+      make_tmap_bf16_2d(&p.tm_w, a.w, static_cast<uint64_t>(a.dim), static_cast<uint64_t>(kdim)))
+    return MOSAIC_ERR_CUDA;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.status = a.status;
+  p.mode = kPlain;
+  p.M = a.S * a.B;
+  p.K = kdim;
+  p.N = a.dim;
+  p.S = a.S;
+  p.B = a.B;
+  p.Hq = a.Hq;
+  return launch_proj(p, stream);
+}
+
+}  // namespace mosaic

@@ -277,6 +277,42 @@ def mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_s
     return o_ba * w[0] + o_cmp * w[1] + o_slc * w[2]
 
 
+def attention_projections(x, w_q, w_k, w_v, w_g, num_q_heads, num_kv_heads, rope_cos=None, rope_sin=None):
+    """The projections of MosaicAttention.forward (primitives.py:182-194), fp32:
+    x [S, B, dim] -> q [B, S, Hq, 64], k, v [B, S, Hk, 64] (q, k rotated by RoPE.forward,
+    primitives.py:132-135, when the tables are given) and the strategy weights
+    [3, B, S, Hq] = softmax over the three strategies of x w_g^T laid out (head,
+    strategy) (generate_strategy_weights, primitives.py:172-178), or None without w_g."""
+    xf = x.float()
+    S, B, _ = xf.shape
+    q = (xf @ w_q.float().t()).reshape(S, B, num_q_heads, -1).permute(1, 0, 2, 3)
+    k = (xf @ w_k.float().t()).reshape(S, B, num_kv_heads, -1).permute(1, 0, 2, 3)
+    v = (xf @ w_v.float().t()).reshape(S, B, num_kv_heads, -1).permute(1, 0, 2, 3)
+    if rope_cos is not None:
+        q, k = rope_apply(q, rope_cos, rope_sin), rope_apply(k, rope_cos, rope_sin)
+    g = None
+    if w_g is not None:
+        logits = (xf @ w_g.float().t()).reshape(S, B, num_q_heads, 3)      # 't b (h s)'
+        g = torch.softmax(logits, dim=-1).permute(3, 1, 0, 2)               # -> 's b t h'
+    return q.contiguous(), k.contiguous(), v.contiguous(), None if g is None else g.contiguous()
+
+
+def mosaic_attention(x, w_q, w_k, w_v, w_g, w_o, num_q_heads, num_kv_heads, rope_cos, rope_sin, block_attn_size,
+                     sparse_block_size, sparse_block_count, block_attn_only, no_compression=False,
+                     block_indices=None, parts=None):
+    """MosaicAttention.forward (primitives.py:182-209), fp32: projections, the
+    attention of mosaic_attn_func, and to_o applied to rearrange(o, 'b s h d -> s b (h d)').
+    `block_indices` / `parts` as in mosaic_attn_func; `parts` also receives q, k, v, g."""
+    q, k, v, g = attention_projections(x, w_q, w_k, w_v, None if block_attn_only else w_g, num_q_heads,
+                                       num_kv_heads, rope_cos, rope_sin)
+    if parts is not None:
+        parts.update(q=q, k=k, v=v, g=g)
+    o = mosaic_attn_func(q, k, v, None if g is None else g.unsqueeze(-1), block_attn_size, sparse_block_size,
+                         sparse_block_count, block_attn_only, no_compression, block_indices=block_indices, parts=parts)
+    B, S, H, D = o.shape
+    return o.permute(1, 0, 2, 3).reshape(S, B, H * D) @ w_o.float().t()
+
+
 def mosaic_attn_func_sample(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,
                             windows):
     """mosaic_attn_func restricted to the queries of the given local windows: the

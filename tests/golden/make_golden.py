@@ -34,6 +34,11 @@ forward kernel's own output and lse, with the block mask from ops.mosaic_block_m
 ops.py:461 does. They keep 64 sampled rows of dq, dk, dv (fp16) and fp64 per-head
 sums. One config repeats a block inside some selections, which pins the
 reference's counting of repeated blocks (twice for dq, once for dk / dv).
+
+The attention-block fixtures (block_*.npz) run primitives.MosaicAttention.forward
+(projections, RoPE, strategy gates, mosaic_attn_func as above, to_o) in fp32 on
+seeded bf16-valued weights and input, and keep the selected block indices, 64
+sampled token rows of the output and fp64 per-batch sums.
 """
 import os
 import sys
@@ -146,6 +151,60 @@ def main_bwd(ops):
         print(name, "written")
 
 
+BLOCK_CONFIGS = {
+    # name: S, B, dim, Hq, Hk, bas, bs, K, seed, block_attn_only, no_compression
+    "block_n768_d256_h4x1": (768, 1, 256, 4, 1, 256, 64, 4, 20, False, False),
+    "block_n768_b2_d512_h8x2_nocmp": (768, 2, 512, 8, 2, 256, 128, 2, 21, False, True),
+}
+
+
+def main_block(P):
+    """primitives.MosaicAttention.forward itself (fp32 on the CPU, bf16-valued weights and
+    input, its Triton sparse kernel in the interpreter, flash-attn as SDPA)."""
+    import types as _types
+    sys.path.insert(0, ROOT)
+    from oracle import bsa_oracle as O
+    from tests.golden_util import draw_block_inputs
+    real_topk = P.attn_topk
+    for name, (S, B, dim, Hq, Hk, bas, bs, K, seed, bao, noc) in BLOCK_CONFIGS.items():
+        x, w_q, w_k, w_v, w_g, w_o = draw_block_inputs(S, B, dim, Hq, Hk, seed)
+        cfg = _types.SimpleNamespace(num_heads=Hq, gqa_ratio=Hq // Hk, dim=dim, qkv_compress_ratio=dim // Hq // 64,
+                                     rope=True, rope_theta=10000, block_attn_size=bas, sparse_block_size=bs,
+                                     sparse_block_count=K)
+        mod = P.MosaicAttention(cfg, bao, noc)
+        with torch.no_grad():
+            mod.to_q.weight.copy_(w_q.float())
+            mod.to_k.weight.copy_(w_k.float())
+            mod.to_v.weight.copy_(w_v.float())
+            mod.to_o.weight.copy_(w_o.float())
+            if mod.to_strategy_combine_mlp is not None:
+                mod.to_strategy_combine_mlp.weight.copy_(w_g.float())
+        grid = O.healpix_grid(int(round((S / 12) ** 0.5)))
+        mod.q_rope.initialize_rope(grid)
+        mod.k_rope.initialize_rope(grid)
+        seen = {}
+
+        def topk_rec(qc, kc, kk, _seen=seen):
+            idx = real_topk(qc, kc, kk)
+            _seen["idx"] = idx
+            return idx
+        P.attn_topk = topk_rec
+        with torch.no_grad():
+            out = mod(x.float())
+        P.attn_topk = real_topk
+        rows = torch.sort(torch.randperm(S, generator=torch.Generator().manual_seed(300 + seed))[:64]).values
+        idx = seen.get("idx")
+        np.savez_compressed(
+            os.path.join(HERE, f"{name}.npz"),
+            meta=np.array([S, B, dim, Hq, Hk, bas, bs, K, seed, int(bao), int(noc)], dtype=np.int64),
+            rows=rows.numpy().astype(np.int32),
+            block_indices=(idx.numpy().astype(np.int16) if idx is not None else np.zeros(0, np.int16)),
+            out_rows=out[rows].to(torch.float16).numpy(),
+            out_sums=out.double().sum(dim=(0, 2)).numpy(),
+        )
+        print(name, "written")
+
+
 def main(ref_dir):
     sys.path.insert(0, ROOT)
     from oracle import bsa_oracle as O
@@ -201,6 +260,7 @@ def main(ref_dir):
         )
         print(name, "written")
     main_bwd(ops)
+    main_block(P)
 
 
 if __name__ == "__main__":

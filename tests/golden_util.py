@@ -13,7 +13,7 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 def fixture_names():
     """The forward fixtures."""
-    return sorted(n for n in _all_names() if not n.startswith("bwd_"))
+    return sorted(n for n in _all_names() if not n.startswith(("bwd_", "block_")))
 
 
 def bwd_fixture_names():
@@ -68,3 +68,31 @@ def inputs(d):
 
 def t(a):
     return torch.from_numpy(np.asarray(a)).float()
+
+
+def block_fixture_names():
+    """The attention-block fixtures (block_*.npz)."""
+    return sorted(n for n in _all_names() if n.startswith("block_"))
+
+
+def load_block(name):
+    z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
+    d = {k: z[k] for k in z.files}
+    S, B, dim, Hq, Hk, bas, bs, K, seed, bao, noc = (int(x) for x in d["meta"])
+    d.update(S=S, B=B, dim=dim, Hq=Hq, Hk=Hk, bas=bas, bs=bs, K=K, seed=seed, block_attn_only=bool(bao),
+             no_compression=bool(noc))
+    return d
+
+
+def draw_block_inputs(S, B, dim, Hq, Hk, seed):
+    """Seeded bf16 input and weights of an attention-block fixture: x [S, B, dim] ~ N(0, 1),
+    weights ~ N(0, 1/dim) (to_q, to_k, to_v, gate, to_o); make_golden.py uses this too."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(S, B, dim, generator=g).bfloat16()
+    sd = dim ** -0.5
+    w_q = (torch.randn(Hq * 64, dim, generator=g) * sd).bfloat16()
+    w_k = (torch.randn(Hk * 64, dim, generator=g) * sd).bfloat16()
+    w_v = (torch.randn(Hk * 64, dim, generator=g) * sd).bfloat16()
+    w_g = (torch.randn(3 * Hq, dim, generator=g) * sd).bfloat16()
+    w_o = (torch.randn(dim, Hq * 64, generator=g) * (Hq * 64) ** -0.5).bfloat16()
+    return x, w_q, w_k, w_v, w_g, w_o

@@ -172,3 +172,44 @@ def test_sparse_bwd_rejects_bad_arguments(kw, code):
 def test_sparse_bwd_empty_inputs_are_a_no_op():
     assert _sparse_bwd(B=0) == _lib.MOSAIC_OK
     assert _sparse_bwd(N=0) == _lib.MOSAIC_OK
+
+
+def _qkv(**kw):
+    a = dict(x=FAKE, w=FAKE, cos=None, sin=None, q=FAKE, k=FAKE, v=FAKE, g=FAKE, status=None, S=3072, B=1, dim=768,
+             Hq=12, Hk=3, D=64)
+    a.update(kw)
+    return _lib.load().mosaic_attn_qkv_proj(a["x"], a["w"], a["cos"], a["sin"], a["q"], a["k"], a["v"], a["g"],
+                                            a["status"], a["S"], a["B"], a["dim"], a["Hq"], a["Hk"], a["D"], None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(x=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(v=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(q=ctypes.c_void_p(0x10008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(cos=FAKE), _lib.MOSAIC_ERR_INVALID_ARGUMENT),          # cos without sin
+    (dict(D=128), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(dim=760), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(Hq=24, Hk=6), _lib.MOSAIC_ERR_UNSUPPORTED),           # 3 Hq gate columns > 64
+    (dict(S=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+])
+def test_qkv_proj_rejects_bad_arguments(kw, code):
+    assert _qkv(**kw) == code
+
+
+def test_qkv_proj_without_gates_allows_more_heads_and_empty_is_noop():
+    assert _qkv(S=0) == _lib.MOSAIC_OK and _qkv(B=0) == _lib.MOSAIC_OK
+    assert _qkv(Hq=24, Hk=6, g=None, S=0) == _lib.MOSAIC_OK
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(attn=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(out=ctypes.c_void_p(0x10008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(D=32), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(dim=770), _lib.MOSAIC_ERR_UNSUPPORTED),
+])
+def test_out_proj_rejects_bad_arguments(kw, code):
+    a = dict(attn=FAKE, w=FAKE, out=FAKE, S=3072, B=1, dim=768, Hq=12, D=64)
+    a.update(kw)
+    rc = _lib.load().mosaic_attn_out_proj(a["attn"], a["w"], a["out"], None, a["S"], a["B"], a["dim"], a["Hq"],
+                                          a["D"], None)
+    assert rc == code

@@ -141,3 +141,28 @@ def test_backward_oracle_is_the_gradient_of_the_forward_oracle():
             torch.testing.assert_close(dv, va.grad, atol=1e-5, rtol=1e-5)
         else:
             assert (dk - ka.grad).abs().max() > 1e-2
+
+
+# ----------------------------------------------------------------------------- attention block
+BLOCK_NAMES = GU.block_fixture_names()
+
+
+def test_block_fixtures_present():
+    assert len(BLOCK_NAMES) >= 2
+
+
+@pytest.mark.parametrize("name", BLOCK_NAMES)
+def test_attention_block_matches_reference(name):
+    """oracle.mosaic_attention against primitives.MosaicAttention.forward run on the same
+    seeded weights (projections, RoPE, strategy gates, attention, to_o; B = 2 in one
+    fixture, so the sequence-first rearranges are pinned too)."""
+    d = GU.load_block(name)
+    x, w_q, w_k, w_v, w_g, w_o = GU.draw_block_inputs(d["S"], d["B"], d["dim"], d["Hq"], d["Hk"], d["seed"])
+    cos, sin = O.rope_tables(O.healpix_grid(int(round((d["S"] / 12) ** 0.5))))
+    idx = torch.from_numpy(d["block_indices"]).long()
+    out = O.mosaic_attention(x, w_q, w_k, w_v, w_g, w_o, d["Hq"], d["Hk"], cos, sin, d["bas"], d["bs"], d["K"],
+                             d["block_attn_only"], d["no_compression"], block_indices=idx)
+    rows = torch.from_numpy(d["rows"]).long()
+    diff = (out[rows] - GU.t(d["out_rows"])).abs()
+    assert diff.max() < 1e-2 and diff.mean() < 1e-3, (diff.max(), diff.mean())
+    torch.testing.assert_close(out.double().sum(dim=(0, 2)), torch.from_numpy(d["out_sums"]), atol=1.0, rtol=1e-2)
