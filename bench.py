@@ -25,7 +25,11 @@ time cuDNN dense SDPA on the same inputs (`dense_sdpa`).
 
 The line also carries `backward`: the device time of mosaic_sparse_attn's backward
 (the training path of the selected branch, ops.mosaic_attn_bwd) on the same workload
-and its FLOP rate against the measured bf16 peak (--no-backward skips it).
+and its FLOP rate against the measured bf16 peak (--no-backward skips it); and
+`attention_block`: the whole MosaicAttention forward at the stage's dims (fused
+projections + attention + output projection, stage times, the projection GEMMs' FLOP
+rates) next to the reference module's eager sequence on the same GPU (--no-block
+skips it).
 
 `--impl reference` times the reference algorithm on the host cores instead: the
 reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
@@ -87,6 +91,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-backward", action="store_true")
+    p.add_argument("--no-block", action="store_true")
     return p.parse_args()
 
 
@@ -142,6 +147,89 @@ def backward_leg(c, sets, stream, steps, warmup):
     if int(status.item()):
         raise RuntimeError(f"device status {int(status.item())} after the backward leg")
     return a.elapsed_time(b) / steps
+
+
+def block_leg(c, sets, stream, steps, warmup):
+    """The whole attention block of a Mosaic layer (primitives.MosaicAttention.forward) at
+    the workload's stage dims (dim = 64 Hq): the fused path (mosaic_attn_qkv_proj ->
+    mosaic_attn_func -> mosaic_attn_out_proj) timed stage by stage, and the reference
+    module's eager sequence on the same GPU (cuBLAS Linear layers, torch RoPE and
+    softmax, layout copies, the same attention op in the middle) for comparison."""
+    import torch.nn.functional as F
+
+    import mosaic_b200 as M
+    from mosaic_b200 import attention as A
+    from mosaic_b200.healpix import healpix_rope_tables
+
+    B, N, Hq, Hk = c["B"], c["N"], c["Hq"], c["Hk"]
+    dim = 64 * Hq
+    dev = sets[0]["q"].device
+    g = torch.Generator(device=dev).manual_seed(99)
+    sd = dim ** -0.5
+    w_q, w_k, w_v = ((torch.randn(h * 64, dim, generator=g, device=dev) * sd).bfloat16() for h in (Hq, Hk, Hk))
+    w_g = (torch.randn(3 * Hq, dim, generator=g, device=dev) * sd).bfloat16()
+    w_o = (torch.randn(dim, Hq * 64, generator=g, device=dev) * (Hq * 64) ** -0.5).bfloat16()
+    w_cat = torch.cat([w_q, w_k, w_v, w_g])
+    cos, sin = (t.to(dev) for t in healpix_rope_tables(c["nside"]))
+    xs = [torch.randn(N, B, dim, generator=g, device=dev).bfloat16() for _ in range(4)]
+
+    def fused(x, ev=None):
+        if ev: ev[0].record(stream)
+        q, k, v, gw = A.qkv_projection(x, w_cat, Hq, Hk, cos, sin)
+        if ev: ev[1].record(stream)
+        o = M.mosaic_attn_func(q, k, v, gw, c["bas"], c["bs"], c["K"], False)
+        if ev: ev[2].record(stream)
+        out = A.out_projection(o, w_o)
+        if ev: ev[3].record(stream)
+        return out
+
+    cos2 = cos.unsqueeze(0).unsqueeze(2).repeat_interleave(2, dim=-1)
+    sin2 = sin.unsqueeze(0).unsqueeze(2).repeat_interleave(2, dim=-1)
+
+    def rope(x):
+        xf = x.float()
+        rot = torch.stack((-xf[..., 1::2], xf[..., 0::2]), dim=-1).flatten(-2)
+        return (xf * cos2 + rot * sin2).to(x.dtype)
+
+    def eager(x):
+        q = F.linear(x, w_q).reshape(N, B, Hq, 64).permute(1, 0, 2, 3)
+        k = F.linear(x, w_k).reshape(N, B, Hk, 64).permute(1, 0, 2, 3)
+        v = F.linear(x, w_v).reshape(N, B, Hk, 64).permute(1, 0, 2, 3).contiguous()
+        logits = F.linear(x, w_g).reshape(N, B, Hq, 3).permute(3, 1, 0, 2)
+        gw = torch.softmax(logits.float(), dim=0).to(x.dtype)
+        q, k = rope(q).contiguous(), rope(k).contiguous()
+        o = M.mosaic_attn_func(q, k, v, gw.unsqueeze(-1), c["bas"], c["bs"], c["K"], False)
+        return F.linear(o.permute(1, 0, 2, 3).reshape(N, B, Hq * 64), w_o)
+
+    ref_out, out = eager(xs[0]), fused(xs[0])
+    torch.cuda.synchronize()
+    agree = float((ref_out.float() - out.float()).abs().max())
+    for i in range(warmup):
+        fused(xs[i % 4])
+        eager(xs[i % 4])
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for i in range(steps):
+        fused(xs[i % 4], evs[i])
+    torch.cuda.synchronize()
+    st = [sum(e[j].elapsed_time(e[j + 1]) for e in evs) / steps for j in range(3)]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        eager(xs[i % 4])
+    b.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = a.elapsed_time(b) / steps
+    M_ = B * N
+    flop_in = 2 * M_ * dim * (w_cat.shape[0])
+    flop_out = 2 * M_ * (Hq * 64) * dim
+    return {"what": f"primitives.MosaicAttention.forward at dim {dim}: fused projection (RoPE, gates) -> "
+                    "mosaic_attn_func -> output projection", "steps": steps,
+            "ms": sum(st), "tokens_per_s": M_ / (sum(st) / 1000),
+            "stages_us": {"qkv_proj": 1000 * st[0], "attention": 1000 * st[1], "out_proj": 1000 * st[2]},
+            "qkv_proj_tflops": flop_in / (st[0] / 1000) / 1e12, "out_proj_tflops": flop_out / (st[2] / 1000) / 1e12,
+            "eager_reference_sequence_ms": eager_ms, "fused_speedup_vs_eager": eager_ms / sum(st),
+            "max_abs_vs_eager": agree}
 
 
 def bytes_pool(c):
@@ -489,6 +577,11 @@ def b200_arm(args):
                "ms": bwd_ms, "steps": n_bwd, "flop_per_step": flops_backward(c),
                "achieved_tflops": flops_backward(c) / (bwd_ms / 1000) / 1e12, "peak_tflops": tf,
                "frac": flops_backward(c) / (bwd_ms / 1000) / 1e12 / tf}
+    blk = None
+    if not args.no_block and world == 1:
+        blk = block_leg(c, sets, stream, max(3, min(args.steps, 50)), max(3, args.warmup))
+        blk["qkv_proj_frac"] = blk["qkv_proj_tflops"] / tf
+        blk["out_proj_frac"] = blk["out_proj_tflops"] / tf
     t_att = stage_ms[3] / 1000.0
     achieved = flops_attend(c) / t_att / 1e12
     line = {
@@ -518,6 +611,8 @@ def b200_arm(args):
         line["dense_sdpa"] = sdpa
     if bwd is not None:
         line["backward"] = bwd
+    if blk is not None:
+        line["attention_block"] = blk
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -18,8 +18,9 @@
 // Tiles of 128 rows x 256 columns, K in 64-wide stages (TMA, 128-byte swizzle, 4-stage
 // ring), fp32 accumulators double-buffered in TMEM so the epilogue of one tile runs
 // under the MMAs of the next. Warp 0 loads, warp 1 issues the MMAs (one elected lane of
-// a converged warp), warps 4-7 run the epilogue, one output row per thread. Every wait
-// is bounded; no TMA multicast.
+// a converged warp), warps 4-11 run the epilogue as two warpgroups, each owning 128 of
+// the tile's 256 columns, one output row per thread. Every wait is bounded; no TMA
+// multicast.
 #include <cstring>
 
 #include "kernels.h"
@@ -29,7 +30,7 @@ namespace mosaic {
 namespace {
 
 constexpr int kPBM = 128, kPBN = 256, kPBK = 64, kPStages = 4;
-constexpr int kPThreads = 256;              // warp 0 TMA, warp 1 MMA, warps 2-3 idle, warps 4-7 epilogue
+constexpr int kPThreads = 384;              // warp 0 TMA, warp 1 MMA, warps 2-3 idle, warps 4-11 epilogue
 constexpr int kPBox = 64 * 128;             // one 64-row x 64-column bf16 box
 constexpr int kPABytes = kPBM * kPBK * 2;   // 16 KB
 constexpr int kPBBytes = kPBN * kPBK * 2;   // 32 KB
@@ -77,13 +78,22 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 __device__ __forceinline__ void store_chunk(uint4* dst, const uint32_t (&acc)[32], const float* cos_row,
                                             const float* sin_row, int p0) {
   uint32_t packed[16];
+  float cs[16], sn[16];
+  if (cos_row != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // 16 frequencies: four 16-byte loads of each table row
+      const float4 c = __ldg(reinterpret_cast<const float4*>(cos_row + p0) + i);
+      const float4 s = __ldg(reinterpret_cast<const float4*>(sin_row + p0) + i);
+      cs[4 * i] = c.x; cs[4 * i + 1] = c.y; cs[4 * i + 2] = c.z; cs[4 * i + 3] = c.w;
+      sn[4 * i] = s.x; sn[4 * i + 1] = s.y; sn[4 * i + 2] = s.z; sn[4 * i + 3] = s.w;
+    }
+  }
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
     if (cos_row != nullptr) {
-      const float c = __ldg(cos_row + p0 + i), s = __ldg(sin_row + p0 + i);
-      const float o0 = __fadd_rn(__fmul_rn(x0, c), __fmul_rn(-x1, s));
-      const float o1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+      const float o0 = __fadd_rn(__fmul_rn(x0, cs[i]), __fmul_rn(-x1, sn[i]));
+      const float o1 = __fadd_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x0, sn[i]));
       x0 = o0;
       x1 = o1;
     }
@@ -108,7 +118,7 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sm.acc_full[a], 1);
-      mbar_init(&sm.acc_empty[a], 128);
+      mbar_init(&sm.acc_empty[a], 256);
     }
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
@@ -183,6 +193,7 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
     __syncwarp();
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- epilogue, one output row per thread
+    const int half = (warp - 4) >> 2;  // warpgroup: columns [128 half, 128 half + 128) of each tile
     const int row = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int qcols = p.Hq * 64, kcols = p.Hk * 64;
@@ -201,7 +212,7 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
       const bool live = m < p.M;
       const uint32_t tacc = tmem + lane_off + 256u * a;
 #pragma unroll 1
-      for (int ci = 0; ci < kPBN / 32; ++ci) {
+      for (int ci = 4 * half; ci < 4 * half + 4; ++ci) {
         const int c0 = nt * kPBN + 32 * ci;  // warp-uniform
         if (c0 >= p.N) break;
         uint32_t acc[32];
