@@ -196,6 +196,30 @@ MOSAIC_API int mosaic_attn_qkv_proj(const void* x, const void* w_qkvg, const flo
 MOSAIC_API int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* status, int seq_len,
                                     int batch, int dim, int num_q_heads, int head_dim, void* stream);
 
+/* out [rows, out_features] = row_scale[r] * (a [rows, in_features] w^T) in bf16 (fp32
+ * accumulation), row_scale optional (NULL = 1): a Linear layer without bias on the
+ * tensor core. Serves CrossAttentionInterpolate's to_kv (primitives.py:275, with the
+ * row factor of its RMSNorm, primitives.py:273, as row_scale) and to_o (:283).
+ * in_features a multiple of 64, out_features a multiple of 8. */
+MOSAIC_API int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
+                             int in_features, int out_features, void* stream);
+
+/* rinv[r] = 1 / sqrt(mean_d x[r, d]^2 + eps) for x [rows, dim] bf16: the row factor of
+ * torch.nn.RMSNorm without an affine weight (the kv_norm of CrossAttentionInterpolate,
+ * primitives.py:247,273; rmsnorm_elementwise_affine=False in every preset). */
+MOSAIC_API int mosaic_row_rms(const void* x, float* rinv, int rows, int dim, float eps, void* stream);
+
+/* The gather-attention of CrossAttentionInterpolate.forward (primitives.py:268-281):
+ * for target point s, batch b, head h: q_j = w_q[h rows] . rel_pos[s, j] (w_q = to_q.weight
+ * [dim, 3] fp32, rel_pos [points_to, k, 3] fp32), scores scale * q_j . k[neighbors[s, j], b, h],
+ * softmax over the k neighbours (fp32), out[s, b, h] = sum_j a_j v[neighbors[s, j], b, h].
+ * kv [points_from, B, 2 dim] bf16 is to_kv's output ('s b (n h d)'), neighbors int32
+ * [points_to, k], out [points_to, B, dim] bf16 (before to_o). head_dim 64, dim a multiple
+ * of 256. Out-of-range neighbour indices set MOSAIC_STATUS_BAD_INDEX and read point 0. */
+MOSAIC_API int mosaic_interp_attend(const void* kv, const int* neighbors, const float* rel_pos, const float* w_q,
+                                    void* out, int* status, int points_to, int points_from, int batch, int dim,
+                                    int num_heads, int num_neighbors, float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,17 +8,20 @@ Public API (same signatures as the reference's ops.py / primitives.py):
     attn_topk(q, k, block_count), block_attention(q, k, v, block_size)
     MosaicAttention(config, block_attn_only, no_compression=False)   # primitives.py:139-209
         (the whole attention block: fused projections + RoPE + gates, attention, to_o)
+    CrossAttentionInterpolate(config)                                 # primitives.py:228-284
 plus get_healpix_grid / rope_tables for the RoPE tables, `ensemble` for
 member-sharded multi-GPU runs and `streaming.StreamedAttention` for host-resident
 batches with their PCIe copies overlapped with the attention.
 """
 from . import attention
 from .attention import MosaicAttention
+from . import interp
+from .interp import CrossAttentionInterpolate
 from .healpix import get_healpix_grid, healpix_rope_tables, pix2ang_nest, rope_tables
 from .ops import mosaic_attn_bwd, mosaic_attn_fwd, mosaic_sparse_attn, mosaic_sparse_attn_with_lse
 from .primitives import attn_topk, block_attention, block_pool, cmp_attention, mosaic_attn_func
 
 __all__ = [
     "mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "mosaic_attn_fwd", "mosaic_attn_bwd", "mosaic_attn_func", "attn_topk", "block_attention",
-    "block_pool", "cmp_attention", "MosaicAttention", "get_healpix_grid", "healpix_rope_tables", "pix2ang_nest", "rope_tables",
+    "block_pool", "cmp_attention", "MosaicAttention", "CrossAttentionInterpolate", "get_healpix_grid", "healpix_rope_tables", "pix2ang_nest", "rope_tables",
 ]

@@ -54,6 +54,9 @@ SIGNATURES = {
     "mosaic_sparse_attn_bwd": ([_vp] * 10 + [_vp, _sz, _vp] + [_i] * 7 + [_f, _vp], _i),
     "mosaic_attn_qkv_proj": ([_vp] * 9 + [_i] * 6 + [_vp], _i),
     "mosaic_attn_out_proj": ([_vp] * 4 + [_i] * 5 + [_vp], _i),
+    "mosaic_linear": ([_vp] * 5 + [_i] * 3 + [_vp], _i),
+    "mosaic_row_rms": ([_vp, _vp, _i, _i, _f, _vp], _i),
+    "mosaic_interp_attend": ([_vp] * 6 + [_i] * 6 + [_f, _vp], _i),
 }
 
 EXPECTED_ABI_VERSION = 1

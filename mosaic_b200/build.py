@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmosaic_b200.so")
-SOURCES = ["bsa_engine.cu", "bsa_bwd.cu", "proj.cu", "pool.cu", "topk.cu", "topk_tc.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["bsa_engine.cu", "bsa_bwd.cu", "proj.cu", "interp.cu", "pool.cu", "topk.cu", "topk_tc.cu", "capi.cu", "noalloc.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-std=c++17", "-lineinfo",

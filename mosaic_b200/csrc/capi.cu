@@ -447,4 +447,44 @@ int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* stat
   return launch_out_proj(a, static_cast<cudaStream_t>(stream));
 }
 
+int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
+                  int in_features, int out_features, void* stream) {
+  if (rows < 0 || in_features <= 0 || out_features <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (in_features % 64 != 0 || out_features % 8 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (rows == 0) return MOSAIC_OK;
+  if (!a || !w || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  LinearLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.a = a; l.w = w; l.out = out; l.rscale = row_scale; l.status = status;
+  l.M = rows; l.K = in_features; l.N = out_features;
+  return launch_linear(l, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_row_rms(const void* x, float* rinv, int rows, int dim, float eps, void* stream) {
+  if (rows < 0 || dim <= 0 || !(eps >= 0.f)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dim % 8 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (rows == 0) return MOSAIC_OK;
+  if (!x || !rinv || !aligned16(x)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  return launch_row_rms(x, rinv, rows, dim, eps, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_interp_attend(const void* kv, const int* neighbors, const float* rel_pos, const float* w_q, void* out,
+                         int* status, int points_to, int points_from, int batch, int dim, int num_heads,
+                         int num_neighbors, float scale, void* stream) {
+  if (points_to < 0 || points_from <= 0 || batch < 0 || dim <= 0 || num_heads <= 0 || num_neighbors <= 0)
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dim % num_heads != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dim / num_heads != kHeadDim || dim % 256 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (points_to == 0 || batch == 0) return MOSAIC_OK;
+  if (!kv || !neighbors || !rel_pos || !w_q || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(kv) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  InterpLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.kv = kv; l.neighbors = neighbors; l.rel_pos = rel_pos; l.w_q = w_q; l.out = out; l.status = status;
+  l.S_to = points_to; l.S_from = points_from; l.B = batch; l.dim = dim; l.k = num_neighbors;
+  l.scale = scale > 0.f ? scale : 0.125f;
+  return launch_interp_attend(l, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

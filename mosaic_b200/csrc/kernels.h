@@ -117,7 +117,29 @@ struct OutProjLaunch {
   int* status;
   int S, B, dim, Hq;
 };
+struct LinearLaunch {
+  const void* a;        // [M, K] bf16
+  const void* w;        // [N, K] bf16
+  void* out;            // [M, N] bf16
+  const float* rscale;  // [M] fp32 row factors or null
+  int* status;
+  int M, K, N;
+};
+// Cross-attention interpolation (interp.cu).
+struct InterpLaunch {
+  const void* kv;        // [S_from, B, 2 dim] bf16 (to_kv output, 's b (n h d)')
+  const int* neighbors;  // [S_to, k] int32 indices into the S_from points
+  const float* rel_pos;  // [S_to, k, 3] fp32 unit vectors
+  const float* w_q;      // [dim, 3] fp32 (to_q.weight)
+  void* out;             // [S_to, B, dim] bf16
+  int* status;
+  int S_to, S_from, B, dim, k;
+  float scale;
+};
 int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream);
+int launch_linear(const LinearLaunch& a, cudaStream_t stream);
+int launch_interp_attend(const InterpLaunch& a, cudaStream_t stream);
+int launch_row_rms(const void* x, float* rinv, long long rows, int dim, float eps, cudaStream_t stream);
 int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream);
 
 int launch_engine(const EngineLaunch& a, cudaStream_t stream);

@@ -14,6 +14,9 @@
 //   mode kPlain: out = a W^T for the output projection to_o, with a the attention
 //                output [B, S, Hq*64] and out [S, B, dim] (the rearrange of
 //                primitives.py:207 is epilogue addressing).
+//   mode kLinear: out[m] = rscale[m] * (a[m] W^T), rows kept in place, rscale optional:
+//                the Linear layers of CrossAttentionInterpolate (to_kv with the row
+//                factor of its RMSNorm folded in, to_o).
 //
 // Tiles of 128 rows x 256 columns, K in 64-wide stages (TMA, 128-byte swizzle, 4-stage
 // ring), fp32 accumulators double-buffered in TMEM so the epilogue of one tile runs
@@ -36,7 +39,7 @@ constexpr int kPABytes = kPBM * kPBK * 2;   // 16 KB
 constexpr int kPBBytes = kPBN * kPBK * 2;   // 32 KB
 constexpr int kPStageBytes = kPABytes + kPBBytes;
 
-enum ProjMode : int { kQkv = 0, kPlain = 1 };
+enum ProjMode : int { kQkv = 0, kPlain = 1, kLinear = 2 };
 
 struct ProjParams {
   CUtensorMap tm_a, tm_w;
@@ -46,7 +49,8 @@ struct ProjParams {
   __nv_bfloat16* g;        // gates [3, B, S, Hq] or null
   const float* rope_cos;   // [S, 32] or null
   const float* rope_sin;
-  __nv_bfloat16* out;      // kPlain
+  __nv_bfloat16* out;      // kPlain, kLinear
+  const float* rscale;     // kLinear: per-row factor or null
   int* status;
   int mode;
   int M, K, N;             // GEMM: M rows of A, K, N output columns
@@ -75,8 +79,9 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 // cos / sin are given (pair i of the chunk uses frequency p0 + i). The reference rounds
 // the Linear output to bf16 first, then rotates in fp32: out[2i] = x[2i] cos - x[2i+1]
 // sin and out[2i+1] = x[2i+1] cos + x[2i] sin, each product and the sum rounded.
+// `rs` scales every accumulator first (kLinear's row factor; 1 otherwise).
 __device__ __forceinline__ void store_chunk(uint4* dst, const uint32_t (&acc)[32], const float* cos_row,
-                                            const float* sin_row, int p0) {
+                                            const float* sin_row, int p0, float rs = 1.0f) {
   uint32_t packed[16];
   float cs[16], sn[16];
   if (cos_row != nullptr) {
@@ -90,7 +95,7 @@ __device__ __forceinline__ void store_chunk(uint4* dst, const uint32_t (&acc)[32
   }
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
+    float x0 = bf16_round(__uint_as_float(acc[2 * i]) * rs), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]) * rs);
     if (cos_row != nullptr) {
       const float o0 = __fadd_rn(__fmul_rn(x0, cs[i]), __fmul_rn(-x1, sn[i]));
       const float o1 = __fadd_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x0, sn[i]));
@@ -228,6 +233,15 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           }
           continue;
         }
+        if (p.mode == kLinear) {
+          tmem_ld32(tacc + 32 * ci, acc);
+          tmem_ld_wait();
+          reg_fence<32>(acc);
+          if (live)
+            store_chunk(reinterpret_cast<uint4*>(p.out + static_cast<size_t>(m) * p.N + c0), acc, nullptr, nullptr,
+                        0, p.rscale != nullptr ? __ldg(p.rscale + m) : 1.0f);
+          continue;
+        }
         const int s = m / p.B, b = m % p.B;  // x rows are (s, b)
         if (c0 < gbase) {
           tmem_ld32(tacc + 32 * ci, acc);
@@ -357,6 +371,22 @@ int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream) {
   p.B = a.B;
   p.Hq = a.Hq;
   p.Hk = a.Hk;
+  return launch_proj(p, stream);
+}
+
+int launch_linear(const LinearLaunch& a, cudaStream_t stream) {
+  ProjParams p;
+  memset(&p, 0, sizeof(p));
+  if (make_tmap_bf16_2d(&p.tm_a, a.a, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K)) ||
+      make_tmap_bf16_2d(&p.tm_w, a.w, static_cast<uint64_t>(a.N), static_cast<uint64_t>(a.K)))
+    return MOSAIC_ERR_CUDA;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.rscale = a.rscale;
+  p.status = a.status;
+  p.mode = kLinear;
+  p.M = a.M;
+  p.K = a.K;
+  p.N = a.N;
   return launch_proj(p, stream);
 }
 

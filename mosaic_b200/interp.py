@@ -1,0 +1,151 @@
+"""Drop-in for primitives.CrossAttentionInterpolate (primitives.py:228-284), the k-nearest
+neighbour cross-attention that moves fields between the lat-lon and HEALPix grids.
+
+    x_from [S_from, B, dim] --mosaic_row_rms + mosaic_linear--> kv = to_kv(RMSNorm(x_from))
+                            --mosaic_interp_attend-----------> per target: softmax over its k
+                                                               neighbours, q from rel_pos
+                            --mosaic_linear------------------> to_o -> [S_to, B, dim]
+
+The module keeps the reference's constructor (`config.k_neighbors`, `dim`, `num_heads`,
+`rmsnorm_elementwise_affine`), submodules (`kv_norm`, `to_q`, `to_kv`, `to_o`) and
+buffers (`neighbors`, `rel_pos`), so a reference state dict loads. The neighbour search
+of `initialize_interpolation_scheme` (sklearn's BallTree with the haversine metric in
+the reference, utils.py:33-40) is an exact k-nearest search on the device: haversine
+distance is monotonic in the dot product of the points' unit vectors, computed in
+fp64. Inference only, like MosaicAttention here.
+"""
+import torch
+import torch.nn as nn
+
+from . import _lib
+from .ops import _ptr, _require_cuda, _stream_ptr
+
+__all__ = ["CrossAttentionInterpolate", "rad_to_xyz", "knn_neighbors", "linear", "row_rms", "interp_attend"]
+
+
+def rad_to_xyz(lonlat):
+    """utils.rad_to_xyz (utils.py:7-16): (lon, lat) radians -> unit xyz."""
+    lon, lat = lonlat[..., 0], lonlat[..., 1]
+    return torch.stack([torch.cos(lat) * torch.cos(lon), torch.cos(lat) * torch.sin(lon), torch.sin(lat)], dim=-1)
+
+
+def knn_neighbors(pos_from_rad, pos_to_rad, k, chunk=2048):
+    """int64 [S_to, k]: the k points of pos_from nearest to each point of pos_to on the
+    sphere (both (lon, lat) radians), nearest first. Same sets as the reference's
+    BallTree haversine query up to ties in distance."""
+    a = rad_to_xyz(pos_to_rad.double())
+    b = rad_to_xyz(pos_from_rad.double())
+    out = []
+    for i in range(0, a.shape[0], chunk):
+        out.append(torch.topk(a[i:i + chunk] @ b.t(), k, dim=1).indices)
+    return torch.cat(out).contiguous()
+
+
+def _bf16c(t):
+    t = t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
+    return t.contiguous()
+
+
+def linear(a, w, row_scale=None, status=None):
+    """a [..., in] @ w^T -> [..., out] bf16 through mosaic_linear (optionally times row_scale
+    per row of the flattened a)."""
+    _require_cuda(a, w)
+    lead, k_in = a.shape[:-1], a.shape[-1]
+    ab, wb = _bf16c(a).reshape(-1, k_in), _bf16c(w)
+    rows, n_out = ab.shape[0], wb.shape[0]
+    out = torch.empty(rows, n_out, dtype=torch.bfloat16, device=a.device)
+    rs = None if row_scale is None else row_scale.float().contiguous()
+    with torch.cuda.device(a.device):
+        rc = _lib.load().mosaic_linear(_ptr(ab), _ptr(wb), _ptr(out), _ptr(rs), _ptr(status), rows, k_in, n_out,
+                                       _stream_ptr(a.device))
+    _lib.check("mosaic_linear", rc)
+    return out.reshape(*lead, n_out)
+
+
+def row_rms(x, eps):
+    """fp32 1 / sqrt(mean(x^2, -1) + eps) per row of x (flattened to [rows, dim])."""
+    _require_cuda(x)
+    xb = _bf16c(x).reshape(-1, x.shape[-1])
+    rinv = torch.empty(xb.shape[0], dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().mosaic_row_rms(_ptr(xb), _ptr(rinv), xb.shape[0], xb.shape[1], float(eps),
+                                        _stream_ptr(x.device))
+    _lib.check("mosaic_row_rms", rc)
+    return rinv
+
+
+def interp_attend(kv, neighbors, rel_pos, w_q, num_heads, points_from, status=None):
+    """The gather-attention of CrossAttentionInterpolate.forward through mosaic_interp_attend:
+    kv [S_from, B, 2 dim] bf16, neighbors [S_to, k], rel_pos [S_to, k, 3], w_q [dim, 3] ->
+    [S_to, B, dim] bf16 (before to_o)."""
+    _require_cuda(kv, neighbors, rel_pos, w_q)
+    S_from, B, two_dim = kv.shape
+    dim = two_dim // 2
+    S_to, kn = neighbors.shape
+    out = torch.empty(S_to, B, dim, dtype=torch.bfloat16, device=kv.device)
+    nb = neighbors.to(torch.int32).contiguous()
+    rp = rel_pos.float().contiguous()
+    wq = w_q.float().contiguous()
+    kvb = _bf16c(kv)
+    with torch.cuda.device(kv.device):
+        rc = _lib.load().mosaic_interp_attend(_ptr(kvb), _ptr(nb), _ptr(rp), _ptr(wq), _ptr(out), _ptr(status), S_to,
+                                              int(points_from), B, dim, int(num_heads), kn, (dim // num_heads) ** -0.5,
+                                              _stream_ptr(kv.device))
+    _lib.check("mosaic_interp_attend", rc)
+    return out
+
+
+class CrossAttentionInterpolate(nn.Module):
+    """primitives.CrossAttentionInterpolate (primitives.py:228-284) on libmosaic_b200.so."""
+
+    space_dim = 3
+
+    def __init__(self, config):
+        super().__init__()
+        self.k_neighbors = config.k_neighbors
+        dim = config.dim
+        num_heads = config.num_heads
+        head_dim = dim // num_heads
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.scale = head_dim ** -0.5
+        self.kv_norm = nn.RMSNorm(dim, elementwise_affine=config.rmsnorm_elementwise_affine)
+        self.to_q = nn.Linear(self.space_dim, dim, bias=False)
+        self.to_kv = nn.Linear(dim, 2 * dim, bias=False)
+        self.to_o = nn.Linear(dim, dim, bias=False)
+        self.register_buffer("neighbors", None, persistent=True)
+        self.register_buffer("rel_pos", None, persistent=True)
+        self.points_from = None
+
+    @torch.no_grad()
+    def initialize_interpolation_scheme(self, pos_from_rad, pos_to_rad):
+        """neighbors [S_to, k] and the unit relative positions [S_to, k, 3] of
+        primitives.py:253-261, computed on pos_to_rad's device."""
+        dev = pos_to_rad.device
+        neighbors = knn_neighbors(pos_from_rad.to(dev), pos_to_rad, self.k_neighbors)
+        self._set_scheme(neighbors, pos_from_rad.to(dev), pos_to_rad)
+
+    def _set_scheme(self, neighbors, pos_from_rad, pos_to_rad):
+        pos_to_xyz = rad_to_xyz(pos_to_rad)
+        pos_from_xyz = rad_to_xyz(pos_from_rad)
+        rel = (pos_to_xyz.unsqueeze(1) - pos_from_xyz[neighbors]).contiguous()
+        self.register_buffer("neighbors", neighbors.long().contiguous(), persistent=True)
+        self.register_buffer("rel_pos", torch.nn.functional.normalize(rel, dim=-1).contiguous(), persistent=True)
+        self.points_from = pos_from_rad.shape[0]
+
+    def forward(self, x_from):
+        if self.neighbors is None or self.rel_pos is None:
+            raise ValueError("Interpolation scheme not initialized.")
+        if torch.is_grad_enabled() and (x_from.requires_grad or any(p.requires_grad for p in self.parameters())):
+            raise NotImplementedError(
+                "mosaic_b200.CrossAttentionInterpolate serves inference; run it under torch.no_grad() or "
+                "torch.inference_mode()")
+        S_from = x_from.shape[0] if self.points_from is None else self.points_from
+        eps = self.kv_norm.eps if self.kv_norm.eps is not None else torch.finfo(x_from.dtype).eps
+        w_kv = self.to_kv.weight
+        if self.kv_norm.weight is not None:  # affine RMSNorm: fold the weight into to_kv's input columns
+            w_kv = w_kv * self.kv_norm.weight.unsqueeze(0)
+        rinv = row_rms(x_from, eps)
+        kv = linear(x_from, w_kv, rinv)
+        o = interp_attend(kv, self.neighbors, self.rel_pos, self.to_q.weight, self.num_heads, S_from)
+        return linear(o, self.to_o.weight).to(x_from.dtype)

@@ -1,4 +1,5 @@
-"""CPU restatement of the reference's block-sparse attention forward.
+"""CPU restatement of the reference's block-sparse attention forward, its backward
+and the layers around it (the attention block, the cross-attention interpolation).
 
 TEST INFRASTRUCTURE: the checker for the CUDA path and the timed CPU baseline.
 Only tests/, __graft_entry__.smoke() and bench.py's CPU legs use it; the product
@@ -311,6 +312,26 @@ def mosaic_attention(x, w_q, w_k, w_v, w_g, w_o, num_q_heads, num_kv_heads, rope
                          sparse_block_count, block_attn_only, no_compression, block_indices=block_indices, parts=parts)
     B, S, H, D = o.shape
     return o.permute(1, 0, 2, 3).reshape(S, B, H * D) @ w_o.float().t()
+
+
+def cross_attention_interpolate(x_from, neighbors, rel_pos, w_q, w_kv, w_o, num_heads, eps, norm_weight=None):
+    """CrossAttentionInterpolate.forward (primitives.py:264-284), fp32: x_from [S_from, B, dim],
+    neighbors [S_to, k], rel_pos [S_to, k, 3] -> [S_to, B, dim]. kv_norm is torch.nn.RMSNorm
+    (x / sqrt(mean(x^2) + eps), times norm_weight when affine)."""
+    xf = x_from.float()
+    S_from, B, dim = xf.shape
+    H = num_heads
+    D = dim // H
+    q = (rel_pos.float() @ w_q.float().t()).reshape(*rel_pos.shape[:2], 1, H, D)          # s k 1 h d
+    x = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    if norm_weight is not None:
+        x = x * norm_weight.float()
+    kv = (x @ w_kv.float().t()).reshape(S_from, B, 2, H, D).permute(2, 0, 1, 3, 4)         # n s b h d
+    k, v = kv[:, neighbors.long()]                                                          # s k b h d
+    scores = (q * k).sum(-1, keepdim=True) * D ** -0.5
+    a = torch.softmax(scores, dim=1)
+    out = (a * v).sum(dim=1).reshape(neighbors.shape[0], B, dim)
+    return out @ w_o.float().t()
 
 
 def mosaic_attn_func_sample(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,

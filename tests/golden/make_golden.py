@@ -12,8 +12,9 @@ It imports the reference's `ops` and `primitives` modules and runs, on the CPU:
   * primitives.flash_attn_func rebound to torch SDPA with GQA (flash-attn is a
     CUDA-only third-party op; its published semantics are non-causal softmax
     attention, scale head_dim**-0.5, query head j -> kv head j // G).
-healpy is not installed: the nested pixel centres for the RoPE angles come from
-the restatement in oracle/bsa_oracle.py (pinned separately by known answers).
+healpy is not installed: the nested pixel centres for the RoPE angles (and the
+interpolation grids) come from the restatement in oracle/bsa_oracle.py (pinned
+separately by known answers); sklearn (the reference's BallTree) is installed.
 
 Harness patches (test-side only, to the Triton interpreter): bf16 operands of
 tl.dot are up-converted to fp32 before numpy's matmul (the stock interpreter
@@ -39,6 +40,11 @@ The attention-block fixtures (block_*.npz) run primitives.MosaicAttention.forwar
 (projections, RoPE, strategy gates, mosaic_attn_func as above, to_o) in fp32 on
 seeded bf16-valued weights and input, and keep the selected block indices, 64
 sampled token rows of the output and fp64 per-batch sums.
+
+The interpolation fixtures (interp_*.npz) run primitives.CrossAttentionInterpolate
+(its BallTree neighbour search, relative positions and forward) in fp32 on seeded
+bf16-valued weights and input between a small lat-lon grid and HEALPix nside 4, in
+both directions, and keep the neighbour table, 64 sampled target rows and fp64 sums.
 """
 import os
 import sys
@@ -205,6 +211,46 @@ def main_block(P):
         print(name, "written")
 
 
+INTERP_CONFIGS = {
+    # name: n_lon, n_lat, nside, to_hp, B, dim, heads, k, seed
+    "interp_ll24x13_to_hp4_d256_h4_k8": (24, 13, 4, True, 2, 256, 4, 8, 30),
+    "interp_hp4_to_ll24x13_d512_h8_k6": (24, 13, 4, False, 1, 512, 8, 6, 31),
+}
+
+
+def main_interp(P):
+    """primitives.CrossAttentionInterpolate itself (fp32 on the CPU): the reference's
+    neighbour search (utils.get_neighbors, sklearn BallTree, haversine), relative
+    positions and forward on seeded bf16-valued weights and input. The HEALPix pixel
+    centres come from the oracle's restatement (healpy is not installed)."""
+    import types as _types
+    sys.path.insert(0, ROOT)
+    from tests.golden_util import draw_interp_inputs, interp_grids
+    for name, (n_lon, n_lat, nside, to_hp, B, dim, H, kn, seed) in INTERP_CONFIGS.items():
+        ll, hp = interp_grids(n_lon, n_lat, nside)
+        pos_from, pos_to = (ll, hp) if to_hp else (hp, ll)
+        x, w_q, w_kv, w_o = draw_interp_inputs(pos_from.shape[0], B, dim, seed)
+        cfg = _types.SimpleNamespace(k_neighbors=kn, dim=dim, num_heads=H, rmsnorm_elementwise_affine=False)
+        mod = P.CrossAttentionInterpolate(cfg)
+        with torch.no_grad():
+            mod.to_q.weight.copy_(w_q.float())
+            mod.to_kv.weight.copy_(w_kv.float())
+            mod.to_o.weight.copy_(w_o.float())
+        mod.initialize_interpolation_scheme(pos_from, pos_to)
+        with torch.no_grad():
+            out = mod(x.float())
+        rows = torch.sort(torch.randperm(pos_to.shape[0], generator=torch.Generator().manual_seed(400 + seed))[:64]).values
+        np.savez_compressed(
+            os.path.join(HERE, f"{name}.npz"),
+            meta=np.array([n_lon, n_lat, nside, int(to_hp), B, dim, H, kn, seed], dtype=np.int64),
+            neighbors=mod.neighbors.numpy().astype(np.int32),
+            rows=rows.numpy().astype(np.int32),
+            out_rows=out[rows].to(torch.float16).numpy(),
+            out_sums=out.double().sum(dim=(0, 2)).numpy(),
+        )
+        print(name, "written")
+
+
 def main(ref_dir):
     sys.path.insert(0, ROOT)
     from oracle import bsa_oracle as O
@@ -261,6 +307,7 @@ def main(ref_dir):
         print(name, "written")
     main_bwd(ops)
     main_block(P)
+    main_interp(P)
 
 
 if __name__ == "__main__":

@@ -13,7 +13,7 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 def fixture_names():
     """The forward fixtures."""
-    return sorted(n for n in _all_names() if not n.startswith(("bwd_", "block_")))
+    return sorted(n for n in _all_names() if not n.startswith(("bwd_", "block_", "interp_")))
 
 
 def bwd_fixture_names():
@@ -96,3 +96,39 @@ def draw_block_inputs(S, B, dim, Hq, Hk, seed):
     w_g = (torch.randn(3 * Hq, dim, generator=g) * sd).bfloat16()
     w_o = (torch.randn(dim, Hq * 64, generator=g) * (Hq * 64) ** -0.5).bfloat16()
     return x, w_q, w_k, w_v, w_g, w_o
+
+
+def interp_fixture_names():
+    """The cross-attention interpolation fixtures (interp_*.npz)."""
+    return sorted(n for n in _all_names() if n.startswith("interp_"))
+
+
+def load_interp(name):
+    z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
+    d = {k: z[k] for k in z.files}
+    n_lon, n_lat, nside, to_hp, B, dim, H, kn, seed = (int(x) for x in d["meta"])
+    d.update(n_lon=n_lon, n_lat=n_lat, nside=nside, to_hp=bool(to_hp), B=B, dim=dim, H=H, k=kn, seed=seed)
+    return d
+
+
+def interp_grids(n_lon, n_lat, nside):
+    """(lat-lon grid, HEALPix grid), each [npoints, 2] (lon, lat) radians, built as
+    Transformer.initialize_interpolation builds them (mosaic.py:272-276): the lat-lon
+    grid is meshgrid(lon, lat, 'ij') flattened, lon 0..360 and lat -90..90 evenly."""
+    lon = torch.linspace(0, 360, n_lon + 1)[:-1]
+    lat = torch.linspace(-90, 90, n_lat)
+    ll = torch.deg2rad(torch.stack(torch.meshgrid(lon, lat, indexing="ij"), -1).reshape(-1, 2))
+    hp = torch.deg2rad(O.healpix_grid(nside))
+    return ll, hp
+
+
+def draw_interp_inputs(S_from, B, dim, seed):
+    """Seeded bf16 input and weights of an interpolation fixture: x_from [S_from, B, dim]
+    ~ N(0, 1), to_q.weight [dim, 3] ~ N(0, 1), to_kv.weight [2 dim, dim] and to_o.weight
+    [dim, dim] ~ N(0, 1/dim); make_golden.py uses this too."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(S_from, B, dim, generator=g).bfloat16()
+    w_q = torch.randn(dim, 3, generator=g).bfloat16()
+    w_kv = (torch.randn(2 * dim, dim, generator=g) * dim ** -0.5).bfloat16()
+    w_o = (torch.randn(dim, dim, generator=g) * dim ** -0.5).bfloat16()
+    return x, w_q, w_kv, w_o

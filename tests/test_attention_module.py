@@ -44,3 +44,17 @@ def test_forward_requiring_gradients_raises():
     m = M.MosaicAttention(cfg(dim=256, heads=4), block_attn_only=False)
     with pytest.raises(NotImplementedError):
         m(torch.randn(768, 1, 256))
+
+
+def test_interpolate_module_names_and_scheme():
+    from tests import golden_util as GU
+    cfg_i = types.SimpleNamespace(k_neighbors=6, dim=256, num_heads=4, rmsnorm_elementwise_affine=False)
+    m = M.CrossAttentionInterpolate(cfg_i)
+    ll, hp = GU.interp_grids(24, 13, 4)
+    m.initialize_interpolation_scheme(ll, hp)
+    assert set(m.state_dict()) == {"to_q.weight", "to_kv.weight", "to_o.weight", "neighbors", "rel_pos"}
+    assert tuple(m.neighbors.shape) == (192, 6) and tuple(m.rel_pos.shape) == (192, 6, 3)
+    n = m.rel_pos.norm(dim=-1)  # unit vectors, or 0 where a target coincides with a source point
+    assert (((n - 1).abs() < 1e-5) | (n == 0)).all() and (n == 0).float().mean() < 0.05
+    with pytest.raises(NotImplementedError):
+        m(torch.randn(312, 1, 256))

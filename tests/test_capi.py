@@ -213,3 +213,29 @@ def test_out_proj_rejects_bad_arguments(kw, code):
     rc = _lib.load().mosaic_attn_out_proj(a["attn"], a["w"], a["out"], None, a["S"], a["B"], a["dim"], a["Hq"],
                                           a["D"], None)
     assert rc == code
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(kv=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(nbr=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(out=ctypes.c_void_p(0x10008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(H=8), _lib.MOSAIC_ERR_UNSUPPORTED),          # head_dim 96
+    (dict(dim=640, H=10), _lib.MOSAIC_ERR_UNSUPPORTED),  # dim not a multiple of 256
+    (dict(k=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(S_from=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+])
+def test_interp_attend_rejects_bad_arguments(kw, code):
+    a = dict(kv=FAKE, nbr=FAKE, rel=FAKE, wq=FAKE, out=FAKE, S_to=49152, S_from=29040, B=1, dim=768, H=12, k=24)
+    a.update(kw)
+    rc = _lib.load().mosaic_interp_attend(a["kv"], a["nbr"], a["rel"], a["wq"], a["out"], None, a["S_to"],
+                                          a["S_from"], a["B"], a["dim"], a["H"], a["k"], 0.0, None)
+    assert rc == code
+
+
+def test_linear_and_rms_reject_bad_arguments():
+    lib = _lib.load()
+    assert lib.mosaic_linear(FAKE, FAKE, FAKE, None, None, 100, 100, 64, None) == _lib.MOSAIC_ERR_UNSUPPORTED
+    assert lib.mosaic_linear(None, FAKE, FAKE, None, None, 100, 128, 64, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+    assert lib.mosaic_linear(FAKE, FAKE, FAKE, None, None, 0, 128, 64, None) == _lib.MOSAIC_OK
+    assert lib.mosaic_row_rms(FAKE, FAKE, 10, 100, 1e-6, None) == _lib.MOSAIC_ERR_UNSUPPORTED
+    assert lib.mosaic_row_rms(FAKE, None, 10, 128, 1e-6, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT

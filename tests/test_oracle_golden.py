@@ -166,3 +166,49 @@ def test_attention_block_matches_reference(name):
     diff = (out[rows] - GU.t(d["out_rows"])).abs()
     assert diff.max() < 1e-2 and diff.mean() < 1e-3, (diff.max(), diff.mean())
     torch.testing.assert_close(out.double().sum(dim=(0, 2)), torch.from_numpy(d["out_sums"]), atol=1.0, rtol=1e-2)
+
+
+# ----------------------------------------------------------------------------- interpolation
+INTERP_NAMES = GU.interp_fixture_names()
+
+
+def test_interp_fixtures_present():
+    assert len(INTERP_NAMES) >= 2
+
+
+def _interp_case(d):
+    from mosaic_b200 import interp as I
+    ll, hp = GU.interp_grids(d["n_lon"], d["n_lat"], d["nside"])
+    pf, pt = (ll, hp) if d["to_hp"] else (hp, ll)
+    nb = torch.from_numpy(d["neighbors"]).long()
+    rel = torch.nn.functional.normalize(I.rad_to_xyz(pt).unsqueeze(1) - I.rad_to_xyz(pf)[nb], dim=-1)
+    return pf, pt, nb, rel
+
+
+@pytest.mark.parametrize("name", INTERP_NAMES)
+def test_cross_attention_interpolate_matches_reference(name):
+    """oracle.cross_attention_interpolate against primitives.CrossAttentionInterpolate
+    run with its own BallTree neighbours (both grid directions, batch 2 in one)."""
+    d = GU.load_interp(name)
+    pf, pt, nb, rel = _interp_case(d)
+    x, w_q, w_kv, w_o = GU.draw_interp_inputs(pf.shape[0], d["B"], d["dim"], d["seed"])
+    out = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, d["H"], torch.finfo(torch.float32).eps)
+    rows = torch.from_numpy(d["rows"]).long()
+    diff = (out[rows] - GU.t(d["out_rows"])).abs()
+    assert diff.max() < 3e-3 and diff.mean() < 3e-4, (diff.max(), diff.mean())
+    torch.testing.assert_close(out.double().sum(dim=(0, 2)), torch.from_numpy(d["out_sums"]), atol=1e-2, rtol=1e-4)
+
+
+@pytest.mark.parametrize("name", INTERP_NAMES)
+def test_neighbour_search_matches_balltree_up_to_ties(name):
+    """mosaic_b200.interp.knn_neighbors (exact search by unit-vector dot product) against
+    the reference's BallTree haversine query: per target the same multiset of distances
+    (the grids are symmetric, so equidistant points may be swapped at the k-th place)."""
+    from mosaic_b200 import interp as I
+    d = GU.load_interp(name)
+    pf, pt, nb, _ = _interp_case(d)
+    mine = I.knn_neighbors(pf, pt, d["k"])
+    a, b = I.rad_to_xyz(pt.double()), I.rad_to_xyz(pf.double())
+    dist = lambda idx: torch.sort((a.unsqueeze(1) * b[idx]).sum(-1), 1).values
+    assert (dist(mine) - dist(nb)).abs().max() < 1e-12
+    assert (torch.sort(mine, 1).values == torch.sort(nb, 1).values).all(1).float().mean() > 0.9
