@@ -29,7 +29,8 @@ and its FLOP rate against the measured bf16 peak (--no-backward skips it); and
 `attention_block`: the whole MosaicAttention forward at the stage's dims (fused
 projections + attention + output projection, stage times, the projection GEMMs' FLOP
 rates) next to the reference module's eager sequence on the same GPU (--no-block
-skips it).
+skips it); and, for S1, `interpolation`: CrossAttentionInterpolate in both grid
+directions at the model's sizes, likewise beside its eager sequence (--no-interp).
 
 `--impl reference` times the reference algorithm on the host cores instead: the
 reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
@@ -92,6 +93,7 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-backward", action="store_true")
     p.add_argument("--no-block", action="store_true")
+    p.add_argument("--no-interp", action="store_true")
     return p.parse_args()
 
 
@@ -230,6 +232,84 @@ def block_leg(c, sets, stream, steps, warmup):
             "qkv_proj_tflops": flop_in / (st[0] / 1000) / 1e12, "out_proj_tflops": flop_out / (st[2] / 1000) / 1e12,
             "eager_reference_sequence_ms": eager_ms, "fused_speedup_vs_eager": eager_ms / sum(st),
             "max_abs_vs_eager": agree}
+
+
+def interp_leg(stream, steps, warmup, dim=768, heads=12, k=24):
+    """primitives.CrossAttentionInterpolate.forward at the model's sizes (dim 768, 12 heads,
+    24 neighbours, one ensemble member) in both directions between the 240 x 121 lat-lon
+    grid and HEALPix nside 64: mosaic_row_rms + mosaic_linear (to_kv) -> mosaic_interp_attend
+    -> mosaic_linear (to_o), stage by stage, beside the reference module's eager torch
+    sequence on the same GPU (RMSNorm, Linear layers, gather, softmax)."""
+    import torch.nn.functional as F
+
+    from mosaic_b200 import interp as I
+    from mosaic_b200.healpix import get_healpix_grid
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lon = torch.linspace(0, 360, 241)[:-1]
+    lat = torch.linspace(-90, 90, 121)
+    ll = torch.deg2rad(torch.stack(torch.meshgrid(lon, lat, indexing="ij"), -1).reshape(-1, 2)).to(dev)
+    hp = torch.deg2rad(get_healpix_grid(64)).to(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    w_q = torch.randn(dim, 3, generator=g, device=dev)
+    w_kv = (torch.randn(2 * dim, dim, generator=g, device=dev) * dim ** -0.5).bfloat16()
+    w_o = (torch.randn(dim, dim, generator=g, device=dev) * dim ** -0.5).bfloat16()
+    res = {}
+    for name, (pf, pt) in (("ll_to_hp", (ll, hp)), ("hp_to_ll", (hp, ll))):
+        nb = I.knn_neighbors(pf, pt, k)
+        rel = F.normalize(I.rad_to_xyz(pt).unsqueeze(1) - I.rad_to_xyz(pf)[nb], dim=-1).float()
+        nb32 = nb.to(torch.int32)
+        S_from, S_to = pf.shape[0], pt.shape[0]
+        xs = [torch.randn(S_from, 1, dim, generator=g, device=dev).bfloat16() for _ in range(4)]
+        eps = torch.finfo(torch.bfloat16).eps
+
+        def fused(x, ev=None):
+            if ev: ev[0].record(stream)
+            kv = I.linear(x, w_kv, I.row_rms(x, eps))
+            if ev: ev[1].record(stream)
+            o = I.interp_attend(kv, nb32, rel, w_q, heads, S_from)
+            if ev: ev[2].record(stream)
+            out = I.linear(o, w_o)
+            if ev: ev[3].record(stream)
+            return out
+
+        def eager(x):
+            q = F.linear(rel, w_q).reshape(S_to, k, 1, heads, dim // heads)
+            xn = F.rms_norm(x, (dim,), eps=eps)
+            kv = F.linear(xn, w_kv).reshape(S_from, 1, 2, heads, dim // heads).permute(2, 0, 1, 3, 4)
+            kk, vv = kv[:, nb]
+            a = torch.softmax((q * kk).sum(-1, keepdim=True).float() * (dim // heads) ** -0.5, dim=1).to(x.dtype)
+            return F.linear((a * vv).sum(1).reshape(S_to, 1, dim), w_o)
+
+        ref_out, out = eager(xs[0]), fused(xs[0])
+        torch.cuda.synchronize()
+        diff = float((ref_out.float() - out.float()).abs().max())
+        for i in range(warmup):
+            fused(xs[i % 4])
+            eager(xs[i % 4])
+        torch.cuda.synchronize()
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+        for i in range(steps):
+            fused(xs[i % 4], evs[i])
+        torch.cuda.synchronize()
+        st = [sum(e[j].elapsed_time(e[j + 1]) for e in evs) / steps for j in range(3)]
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record(stream)
+        for i in range(steps):
+            eager(xs[i % 4])
+        b_.record(stream)
+        torch.cuda.synchronize()
+        eager_ms = a_.elapsed_time(b_) / steps
+        gather = S_to * k * 2 * dim * 2                              # k / v bytes the targets read
+        hbm = S_from * 2 * dim * 2 + S_to * dim * 2 + S_to * k * 16   # kv once, out, neighbours + rel_pos
+        res[name] = {"points_from": S_from, "points_to": S_to, "ms": sum(st),
+                     "stages_us": {"rms_to_kv": 1000 * st[0], "attend": 1000 * st[1], "to_o": 1000 * st[2]},
+                     "attend_gather_gbs": gather / (st[1] / 1000) / 1e9, "attend_hbm_gbs": hbm / (st[1] / 1000) / 1e9,
+                     "eager_reference_sequence_ms": eager_ms, "fused_speedup_vs_eager": eager_ms / sum(st),
+                     "max_abs_vs_eager": diff}
+    res["what"] = ("primitives.CrossAttentionInterpolate.forward, dim 768, 12 heads, k 24, one member, "
+                   "240 x 121 lat-lon <-> HEALPix nside 64")
+    return res
 
 
 def bytes_pool(c):
@@ -582,6 +662,11 @@ def b200_arm(args):
         blk = block_leg(c, sets, stream, max(3, min(args.steps, 50)), max(3, args.warmup))
         blk["qkv_proj_frac"] = blk["qkv_proj_tflops"] / tf
         blk["out_proj_frac"] = blk["out_proj_tflops"] / tf
+    itp = None
+    if not args.no_interp and world == 1 and name == "S1":
+        itp = interp_leg(stream, max(3, min(args.steps, 50)), max(3, args.warmup))
+        for leg in ("ll_to_hp", "hp_to_ll"):
+            itp[leg]["attend_hbm_frac"] = itp[leg]["attend_hbm_gbs"] / hbm
     t_att = stage_ms[3] / 1000.0
     achieved = flops_attend(c) / t_att / 1e12
     line = {
@@ -613,6 +698,8 @@ def b200_arm(args):
         line["backward"] = bwd
     if blk is not None:
         line["attention_block"] = blk
+    if itp is not None:
+        line["interpolation"] = itp
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
