@@ -487,4 +487,33 @@ int mosaic_interp_attend(const void* kv, const int* neighbors, const float* rel_
   return launch_interp_attend(l, static_cast<cudaStream_t>(stream));
 }
 
+int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, const int* tile_targets,
+                               const int* tile_point_off, const int* tile_points, const uint8_t* local_idx,
+                               const int* order, const float* rel_pos, const float* w_q, void* out, int* status,
+                               int num_tiles, int max_union, int points_from, int batch, int dim, int num_heads,
+                               int num_neighbors, float scale, void* stream) {
+  if (num_tiles < 0 || max_union < 0 || points_from <= 0 || batch < 0 || dim <= 0 || num_heads <= 0 ||
+      num_neighbors <= 0)
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dim % num_heads != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dim / num_heads != kHeadDim || dim % 128 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  // local indices are bytes, unions padded to 16-row mma steps; two lanes per target
+  if (max_union > 256 || max_union % 16 != 0 || num_neighbors > 32) return MOSAIC_ERR_UNSUPPORTED;
+  if (tiled_interp_smem_bytes(max_union, num_heads, num_neighbors) > 227 * 1024) return MOSAIC_ERR_UNSUPPORTED;
+  if (num_tiles == 0 || batch == 0) return MOSAIC_OK;
+  if (!kv || !kw_workspace || !tile_targets || !tile_point_off || !tile_points || !local_idx || !rel_pos || !w_q ||
+      !out)
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(kv) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  InterpTiledLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.kv = kv; l.kw = kw_workspace; l.tile_targets = tile_targets; l.tile_point_off = tile_point_off;
+  l.tile_points = tile_points; l.local_idx = local_idx; l.order = order; l.rel_pos = rel_pos; l.w_q = w_q;
+  l.out = out; l.status = status;
+  l.S_from = points_from; l.B = batch; l.dim = dim; l.k = num_neighbors; l.n_tiles = num_tiles;
+  l.max_union = max_union;
+  l.scale = scale > 0.f ? scale : 0.125f;
+  return launch_interp_tiled(l, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

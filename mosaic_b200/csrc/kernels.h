@@ -136,7 +136,24 @@ struct InterpLaunch {
   int S_to, S_from, B, dim, k;
   float scale;
 };
+struct InterpTiledLaunch {
+  const void* kv;            // [S_from, B, 2 dim] bf16
+  float* kw;                 // [S_from, B, H, 4] fp32 scratch, written here
+  const int* tile_targets;   // [n_tiles + 1] offsets into `order`; <= 32 targets per tile
+  const int* tile_point_off; // [n_tiles + 1] offsets into tile_points; multiples of 16
+  const int* tile_points;    // source points of each tile's neighbour union (padded to 16)
+  const uint8_t* local_idx;  // [S_to, k] position of neighbour j inside its tile's union
+  const int* order;          // [S_to] targets in tile order, or null = identity
+  const float* rel_pos;      // [S_to, k, 3]
+  const float* w_q;          // [dim, 3]
+  void* out;                 // [S_to, B, dim] bf16
+  int* status;
+  int S_from, B, dim, k, n_tiles, max_union;
+  float scale;
+};
 int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream);
+int launch_interp_tiled(const InterpTiledLaunch& a, cudaStream_t stream);
+size_t tiled_interp_smem_bytes(int max_union, int H, int k);
 int launch_linear(const LinearLaunch& a, cudaStream_t stream);
 int launch_interp_attend(const InterpLaunch& a, cudaStream_t stream);
 int launch_row_rms(const void* x, float* rinv, long long rows, int dim, float eps, cudaStream_t stream);

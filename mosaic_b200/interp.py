@@ -2,9 +2,14 @@
 neighbour cross-attention that moves fields between the lat-lon and HEALPix grids.
 
     x_from [S_from, B, dim] --mosaic_row_rms + mosaic_linear--> kv = to_kv(RMSNorm(x_from))
-                            --mosaic_interp_attend-----------> per target: softmax over its k
+                            --mosaic_interp_attend_tiled-----> per target: softmax over its k
                                                                neighbours, q from rel_pos
                             --mosaic_linear------------------> to_o -> [S_to, B, dim]
+
+The neighbour table is static, so the module packs the targets once into tiles of
+spatially adjacent points (`build_tiles`) whose merged neighbour lists fit in shared
+memory; the tiled kernel then reads each source point once per tile instead of once
+per (target, neighbour). Neighbour counts above 32 take mosaic_interp_attend.
 
 The module keeps the reference's constructor (`config.k_neighbors`, `dim`, `num_heads`,
 `rmsnorm_elementwise_affine`), submodules (`kv_norm`, `to_q`, `to_kv`, `to_o`) and
@@ -20,7 +25,12 @@ import torch.nn as nn
 from . import _lib
 from .ops import _ptr, _require_cuda, _stream_ptr
 
-__all__ = ["CrossAttentionInterpolate", "rad_to_xyz", "knn_neighbors", "linear", "row_rms", "interp_attend"]
+__all__ = ["CrossAttentionInterpolate", "rad_to_xyz", "knn_neighbors", "linear", "row_rms", "interp_attend",
+           "build_tiles", "interp_attend_tiled"]
+
+TILE_MAX_UNION = 80  # source points per tile (a multiple of 16: the tensor-core k step)
+TILE_MAX_TARGETS = 32  # 2 blocks of 16 rows
+TILED_MAX_NEIGHBORS = 32
 
 
 def rad_to_xyz(lonlat):
@@ -95,6 +105,109 @@ def interp_attend(kv, neighbors, rel_pos, w_q, num_heads, points_from, status=No
     return out
 
 
+def _morton3(xyz, bits=10):
+    """3D Morton (Z-order) key of unit vectors: targets sorted by it form compact patches."""
+    q = ((xyz + 1) * 0.5 * ((1 << bits) - 1)).round().long().clamp(0, (1 << bits) - 1)
+    key = torch.zeros(xyz.shape[0], dtype=torch.long)
+    for bit in range(bits):
+        for d in range(3):
+            key |= ((q[:, d] >> bit) & 1) << (3 * bit + d)
+    return key
+
+
+def _pack(nb, order, max_union, max_targets):
+    """Greedy packing of targets, in `order`, into tiles whose neighbour union stays within
+    max_union points and max_targets targets; list of target lists."""
+    tiles, cur, cur_set = [], [], set()
+    for t in order:
+        merged = cur_set.union(nb[t])
+        if cur and (len(merged) > max_union or len(cur) >= max_targets):
+            tiles.append(cur)
+            cur, merged = [], set(nb[t])
+        cur.append(t)
+        cur_set = merged
+    if cur:
+        tiles.append(cur)
+    return tiles
+
+
+def build_tiles(neighbors, pos_to_rad, max_union=TILE_MAX_UNION, max_targets=TILE_MAX_TARGETS):
+    """The tile tables of mosaic_interp_attend_tiled for a static neighbour table
+    [S_to, k] and the targets' (lon, lat) radians: the targets in index order and (when
+    pos_to_rad is given) in 3D Morton order are each packed greedily, and the packing that
+    stages fewer source points in total is kept. Each tile's union is padded with repeats of
+    its first point to a multiple of 16. Returns a dict of CPU tensors (tile_targets,
+    tile_point_off, tile_points, local int32/uint8, order int32 or None) and max_union (the
+    largest padded union). Neighbour lists must not repeat a point (a k-nearest search
+    never does): the tiled kernel scatters each weight to its point's position."""
+    nb = neighbors.detach().cpu().long()
+    S_to, kn = nb.shape
+    if max_union % 16 or not 16 <= max_union <= 256 or not 1 <= max_targets <= TILE_MAX_TARGETS:
+        raise ValueError(f"max_union {max_union} (a multiple of 16 up to 256), max_targets {max_targets} (<= 32)")
+    if kn > max_union:
+        raise ValueError(f"{kn} neighbours do not fit a tile of {max_union} points")
+    srt = nb.sort(dim=1).values
+    if kn > 1 and bool((srt[:, 1:] == srt[:, :-1]).any()):
+        raise ValueError("a neighbour list repeats a point")
+    rows = nb.tolist()
+    best = None
+    orders = [None]
+    if pos_to_rad is not None:
+        orders.append(torch.argsort(_morton3(rad_to_xyz(pos_to_rad.detach().cpu().double())), stable=True))
+    for order in orders:
+        seq = range(S_to) if order is None else order.tolist()
+        tiles = _pack(rows, seq, max_union, max_targets)
+        staged = sum(len(set().union(*(rows[t] for t in tl))) for tl in tiles)
+        if best is None or staged < best[0]:
+            best = (staged, order, tiles)
+    _, order, tiles = best
+    tile_targets, point_off, points = [0], [0], []
+    local = torch.empty(S_to, kn, dtype=torch.uint8)
+    for tl in tiles:
+        ts = torch.tensor(tl)
+        uni, inv = torch.unique(nb[ts], sorted=True, return_inverse=True)
+        local[ts] = inv.to(torch.uint8)
+        pad = -uni.numel() % 16
+        points.append(torch.cat([uni, uni[:1].expand(pad)]) if pad else uni)
+        uni = points[-1]
+        tile_targets.append(tile_targets[-1] + len(tl))
+        point_off.append(point_off[-1] + uni.numel())
+    return {
+        "tile_targets": torch.tensor(tile_targets, dtype=torch.int32),
+        "tile_point_off": torch.tensor(point_off, dtype=torch.int32),
+        "tile_points": torch.cat(points).to(torch.int32),
+        "local": local,
+        "order": None if order is None else order.to(torch.int32),
+        "max_union": max(b - a for a, b in zip(point_off[:-1], point_off[1:])),
+    }
+
+
+def interp_attend_tiled(kv, tiles, rel_pos, w_q, num_heads, points_from, status=None):
+    """interp_attend through mosaic_interp_attend_tiled with the tables of build_tiles
+    (tensors on kv's device)."""
+    _require_cuda(kv, rel_pos, w_q)
+    S_from, B, two_dim = kv.shape
+    dim = two_dim // 2
+    S_to, kn = tiles["local"].shape
+    out = torch.empty(S_to, B, dim, dtype=torch.bfloat16, device=kv.device)
+    kw = torch.empty(S_from, B, num_heads, 3, dtype=torch.float32, device=kv.device)
+    rp = rel_pos.float().contiguous()
+    wq = w_q.float().contiguous()
+    kvb = _bf16c(kv)
+    n_tiles = tiles["tile_targets"].numel() - 1
+    with torch.cuda.device(kv.device):
+        rc = _lib.load().mosaic_interp_attend_tiled(
+            _ptr(kvb), _ptr(kw), _ptr(tiles["tile_targets"]), _ptr(tiles["tile_point_off"]),
+            _ptr(tiles["tile_points"]), _ptr(tiles["local"]), _ptr(tiles["order"]), _ptr(rp), _ptr(wq), _ptr(out),
+            _ptr(status), n_tiles, int(tiles["max_union"]), int(points_from), B, dim, int(num_heads), kn,
+            (dim // num_heads) ** -0.5, _stream_ptr(kv.device))
+    _lib.check("mosaic_interp_attend_tiled", rc)
+    return out
+
+
+_TILE_KEYS = ("tile_targets", "tile_point_off", "tile_points", "local", "order")
+
+
 class CrossAttentionInterpolate(nn.Module):
     """primitives.CrossAttentionInterpolate (primitives.py:228-284) on libmosaic_b200.so."""
 
@@ -116,6 +229,9 @@ class CrossAttentionInterpolate(nn.Module):
         self.register_buffer("neighbors", None, persistent=True)
         self.register_buffer("rel_pos", None, persistent=True)
         self.points_from = None
+        for key in _TILE_KEYS:  # tile tables of the tiled kernel, derived from `neighbors`
+            self.register_buffer("_tile_" + key, None, persistent=False)
+        self._tile_max_union = None
 
     @torch.no_grad()
     def initialize_interpolation_scheme(self, pos_from_rad, pos_to_rad):
@@ -132,6 +248,40 @@ class CrossAttentionInterpolate(nn.Module):
         self.register_buffer("neighbors", neighbors.long().contiguous(), persistent=True)
         self.register_buffer("rel_pos", torch.nn.functional.normalize(rel, dim=-1).contiguous(), persistent=True)
         self.points_from = pos_from_rad.shape[0]
+        self._pos_to_rad = pos_to_rad.detach().cpu()
+        self._drop_tiles()
+        self._tiles()
+
+    def _drop_tiles(self):
+        for key in _TILE_KEYS:
+            setattr(self, "_tile_" + key, None)
+        self._tile_max_union = None
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        super()._load_from_state_dict(*args, **kwargs)
+        self._drop_tiles()  # rebuilt from the loaded neighbour table on first use
+
+    def _tiles(self):
+        """The tile tables for the current neighbour table (built on first use), or None
+        when the neighbour count is above what the tiled kernel takes."""
+        if self.neighbors.shape[1] > TILED_MAX_NEIGHBORS:
+            return None
+        if self._tile_max_union == 0:  # neighbour lists with repeats: untiled kernel
+            return None
+        if self._tile_max_union is None:
+            # after a state-dict load the target positions are unknown: index order only
+            try:
+                t = build_tiles(self.neighbors, getattr(self, "_pos_to_rad", None))
+            except ValueError:
+                self._tile_max_union = 0
+                return None
+            dev = self.neighbors.device
+            for key in _TILE_KEYS:
+                setattr(self, "_tile_" + key, None if t[key] is None else t[key].to(dev))
+            self._tile_max_union = t["max_union"]
+        tiles = {key: getattr(self, "_tile_" + key) for key in _TILE_KEYS}
+        tiles["max_union"] = self._tile_max_union
+        return tiles
 
     def forward(self, x_from):
         if self.neighbors is None or self.rel_pos is None:
@@ -147,5 +297,9 @@ class CrossAttentionInterpolate(nn.Module):
             w_kv = w_kv * self.kv_norm.weight.unsqueeze(0)
         rinv = row_rms(x_from, eps)
         kv = linear(x_from, w_kv, rinv)
-        o = interp_attend(kv, self.neighbors, self.rel_pos, self.to_q.weight, self.num_heads, S_from)
+        tiles = self._tiles()
+        if tiles is not None:
+            o = interp_attend_tiled(kv, tiles, self.rel_pos, self.to_q.weight, self.num_heads, S_from)
+        else:
+            o = interp_attend(kv, self.neighbors, self.rel_pos, self.to_q.weight, self.num_heads, S_from)
         return linear(o, self.to_o.weight).to(x_from.dtype)

@@ -58,3 +58,44 @@ def test_interpolate_module_names_and_scheme():
     assert (((n - 1).abs() < 1e-5) | (n == 0)).all() and (n == 0).float().mean() < 0.05
     with pytest.raises(NotImplementedError):
         m(torch.randn(312, 1, 256))
+
+
+@pytest.mark.parametrize("grids,k,umax,tmax", [((24, 13, 4, True), 8, 80, 32), ((48, 25, 8, False), 24, 64, 16),
+                                               ((24, 13, 4, False), 1, 16, 1), ((24, 13, 4, True), 32, 32, 4),
+                                               ((48, 25, 8, True), 24, 256, 32)])
+def test_interp_tiles_reconstruct_the_neighbour_table(grids, k, umax, tmax):
+    """build_tiles: every target in exactly one tile (the order is a permutation), each
+    tile's union within max_union and max_targets, sorted and duplicate-free up to the
+    padding (repeats of its first point to a multiple of 16), and tile_points[local] gives
+    back the neighbour table exactly."""
+    from mosaic_b200 import interp as I
+    from tests import golden_util as GU
+    n_lon, n_lat, nside, to_hp = grids
+    ll, hp = GU.interp_grids(n_lon, n_lat, nside)
+    pf, pt = (ll, hp) if to_hp else (hp, ll)
+    nb = I.knn_neighbors(pf, pt, k)
+    t = I.build_tiles(nb, pt, max_union=umax, max_targets=tmax)
+    order = torch.arange(pt.shape[0]) if t["order"] is None else t["order"].long()
+    assert sorted(order.tolist()) == list(range(pt.shape[0]))
+    tt, po = t["tile_targets"].long(), t["tile_point_off"].long()
+    pts, loc = t["tile_points"].long(), t["local"].long()
+    assert tt[0] == 0 and tt[-1] == pt.shape[0] and po[-1] == pts.numel() and t["local"].dtype == torch.uint8
+    assert t["max_union"] == int((po[1:] - po[:-1]).max()) <= umax
+    for i in range(tt.numel() - 1):
+        ts = order[tt[i]:tt[i + 1]]
+        assert 1 <= ts.numel() <= tmax
+        u = pts[po[i]:po[i + 1]]
+        n_uni = torch.unique(nb[ts]).numel()
+        assert u.numel() % 16 == 0 and u.numel() - n_uni < 16
+        assert (u[1:n_uni] > u[:n_uni - 1]).all() and (u[n_uni:] == u[0]).all()
+        assert torch.equal(u[loc[ts]], nb[ts])
+
+
+def test_interp_tiles_reject_bad_tables():
+    from mosaic_b200 import interp as I
+    with pytest.raises(ValueError):  # more neighbours than a union holds
+        I.build_tiles(torch.arange(40).reshape(2, 20), None, max_union=16)
+    with pytest.raises(ValueError):  # repeated neighbour
+        I.build_tiles(torch.tensor([[0, 1, 2], [3, 4, 3]]), None)
+    with pytest.raises(ValueError):  # union not a multiple of the mma k step
+        I.build_tiles(torch.arange(6).reshape(2, 3), None, max_union=40)

@@ -33,6 +33,23 @@ def test_library_exports_every_declared_symbol():
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def declared_arg_counts():
+    """{function: number of parameters} from the header's MOSAIC_API declarations."""
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"MOSAIC_API[^;(]*?\b(mosaic_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src, flags=re.S):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_the_header_arity():
+    counts = declared_arg_counts()
+    assert set(counts) == set(declared_functions())
+    for name, n in counts.items():
+        assert len(_lib.SIGNATURES[name][0]) == n, (name, n, len(_lib.SIGNATURES[name][0]))
+
+
 def test_abi_version_and_error_strings():
     lib = _lib.load()
     assert lib.mosaic_abi_version() == _lib.EXPECTED_ABI_VERSION

@@ -1,5 +1,5 @@
 """Parity of the cross-attention interpolation (mosaic_row_rms, mosaic_linear,
-mosaic_interp_attend and the CrossAttentionInterpolate module) with the CPU oracle's
+mosaic_interp_attend, mosaic_interp_attend_tiled and the CrossAttentionInterpolate module) with the CPU oracle's
 restatement of primitives.CrossAttentionInterpolate.forward and with the fixtures of
 the reference module. Tolerance: bf16 tensors with fp32 arithmetic inside, compared
 with the fp32 oracle at max-abs 2e-2 and mean-abs 2e-3 of the output's largest
@@ -54,6 +54,91 @@ def test_interp_attend_matches_oracle(cfg):
     kk, vv = kvr[:, nb]
     a = torch.softmax((q * kk).sum(-1, keepdim=True) * D ** -0.5, dim=1)
     close_rel(out, (a * vv).sum(1).reshape(pt.shape[0], B, dim))
+
+
+def oracle_attend(kv, nb, rel, w_q, H):
+    S_from, B, two_dim = kv.shape
+    dim = two_dim // 2
+    D = dim // H
+    q = (rel @ w_q.t()).reshape(*rel.shape[:2], 1, H, D)
+    kvr = kv.float().reshape(S_from, B, 2, H, D).permute(2, 0, 1, 3, 4)
+    kk, vv = kvr[:, nb]
+    a = torch.softmax((q * kk).sum(-1, keepdim=True) * D ** -0.5, dim=1)
+    return (a * vv).sum(1).reshape(nb.shape[0], B, dim)
+
+
+def dev_tiles(t):
+    return {key: (val.to(DEV) if torch.is_tensor(val) else val) for key, val in t.items()}
+
+
+@pytest.mark.parametrize("cfg", [(48, 25, 8, True, 1, 256, 4, 24, 80, 32), (48, 25, 8, False, 3, 768, 12, 20, 96, 32),
+                                 (24, 13, 4, True, 2, 512, 8, 8, 80, 32), (48, 25, 8, True, 1, 256, 4, 32, 48, 3),
+                                 (24, 13, 4, False, 2, 256, 4, 1, 16, 1), (48, 25, 8, False, 1, 512, 8, 17, 256, 32),
+                                 (24, 13, 4, True, 1, 384, 6, 24, 112, 17), (24, 13, 4, False, 2, 128, 2, 12, 32, 20)])
+def test_interp_attend_tiled_matches_oracle(cfg):
+    """Tiles from the default packing, from small unions / few targets (many ragged tiles),
+    one neighbour per target, unions up to 256 points, and dims of 384 and 128 (a last
+    chunk of one head pair, a single chunk)."""
+    n_lon, n_lat, nside, to_hp, B, dim, H, k, umax, tmax = cfg
+    pf, pt, nb, rel = scheme(n_lon, n_lat, nside, to_hp, k)
+    tiles = I.build_tiles(nb, pt, max_union=umax, max_targets=tmax)
+    assert tiles["max_union"] <= umax
+    g = torch.Generator().manual_seed(dim + k + 1)
+    kv = torch.randn(pf.shape[0], B, 2 * dim, generator=g).bfloat16()
+    w_q = torch.randn(dim, 3, generator=g)
+    status = mops.status_buffer(DEV)
+    out = I.interp_attend_tiled(kv.to(DEV), dev_tiles(tiles), rel.to(DEV), w_q.to(DEV), H, pf.shape[0],
+                                status=status)
+    torch.cuda.synchronize()
+    assert mops.check_status(status) == 0
+    close_rel(out, oracle_attend(kv, nb, rel, w_q, H))
+    if dim % 256 == 0:
+        untiled = I.interp_attend(kv.to(DEV), nb.to(DEV), rel.to(DEV), w_q.to(DEV), H, pf.shape[0])
+        close_rel(out, untiled.float().cpu())
+
+
+def test_tiled_bad_local_index_is_reported_not_faulted():
+    pf, pt, nb, rel = scheme(24, 13, 4, True, 8)
+    tiles = I.build_tiles(nb, pt)
+    tiles["local"] = tiles["local"].clone()
+    tiles["local"][5, 3] = 254  # planted on the host: beyond its tile's union
+    kv = torch.randn(pf.shape[0], 1, 512).bfloat16()
+    status = mops.status_buffer(DEV)
+    out = I.interp_attend_tiled(kv.to(DEV), dev_tiles(tiles), rel.to(DEV), torch.randn(256, 3).to(DEV), 4,
+                                pf.shape[0], status=status)
+    torch.cuda.synchronize()
+    assert status.item() & 2
+    assert torch.isfinite(out.float()).all()
+
+
+def test_module_above_32_neighbours_takes_untiled_kernel():
+    pf, pt, nb, rel = scheme(24, 13, 4, True, 40)
+    m, x, (w_q, w_kv, w_o) = module(256, 4, 40, pf, pt, nb, seed=3, B=2)
+    assert m._tiles() is None
+    with torch.no_grad():
+        out = m(x.to(DEV))
+    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 4, torch.finfo(torch.bfloat16).eps)
+    close_rel(out, ref)
+
+
+def test_module_after_state_dict_load_rebuilds_tiles():
+    pf, pt, nb, rel = scheme(48, 25, 8, True, 24)
+    m, x, (w_q, w_kv, w_o) = module(256, 4, 24, pf, pt, nb, seed=5, B=1)
+    cfg = types.SimpleNamespace(k_neighbors=24, dim=256, num_heads=4, rmsnorm_elementwise_affine=False)
+    m2 = M.CrossAttentionInterpolate(cfg)
+    m2.initialize_interpolation_scheme(pf, pt)
+    with torch.no_grad():
+        m2.neighbors.copy_(torch.roll(m2.neighbors, 1, dims=0))  # a stale table, replaced by the load
+    m2._tiles()
+    m2.load_state_dict(m.state_dict())
+    assert m2._tile_max_union is None
+    m2 = m2.to(DEV)
+    for lin in (m2.to_kv, m2.to_o):
+        lin.to(torch.bfloat16)
+    with torch.no_grad():
+        out = m2(x.to(DEV))
+    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 4, torch.finfo(torch.bfloat16).eps)
+    close_rel(out, ref)
 
 
 def test_linear_and_row_rms():
