@@ -227,8 +227,9 @@ MOSAIC_API int mosaic_interp_attend(const void* kv, const int* neighbors, const 
  * of their neighbours, padded with repeats to a multiple of 16, at most max_union <= 256
  * (a multiple of 16). local_idx [points_to, k] (uint8) is each neighbour's position in its
  * tile's list; a target's neighbours are distinct points; num_neighbors <= 32, dim a
- * multiple of 128. kw_workspace holds points_from * batch * num_heads * 4 floats of
- * scratch. Each tile copies its points' v rows once into shared memory and runs the
+ * multiple of 128. kw_workspace holds points_from * batch * num_heads * 4 floats: the
+ * per-point, per-head vectors (to_q.weight_h^T k_h, 0), computed here first unless
+ * kw_ready is nonzero (the caller wrote them; w_q may then be NULL). Each tile copies its points' v rows once into shared memory and runs the
  * attention as P (softmax weights, bf16) x V on the tensor cores, so the outputs equal
  * mosaic_interp_attend's up to the bf16 rounding of the weights (as the reference
  * module's bf16 softmax) and fp32 summation order. Inconsistent tables set
@@ -238,7 +239,7 @@ MOSAIC_API int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, c
                                           const uint8_t* local_idx, const int* order, const float* rel_pos,
                                           const float* w_q, void* out, int* status, int num_tiles, int max_union,
                                           int points_from, int batch, int dim, int num_heads, int num_neighbors,
-                                          float scale, void* stream);
+                                          int kw_ready, float scale, void* stream);
 
 #ifdef __cplusplus
 }

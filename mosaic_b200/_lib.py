@@ -57,7 +57,7 @@ SIGNATURES = {
     "mosaic_linear": ([_vp] * 5 + [_i] * 3 + [_vp], _i),
     "mosaic_row_rms": ([_vp, _vp, _i, _i, _f, _vp], _i),
     "mosaic_interp_attend": ([_vp] * 6 + [_i] * 6 + [_f, _vp], _i),
-    "mosaic_interp_attend_tiled": ([_vp] * 11 + [_i] * 7 + [_f, _vp], _i),
+    "mosaic_interp_attend_tiled": ([_vp] * 11 + [_i] * 8 + [_f, _vp], _i),
 }
 
 EXPECTED_ABI_VERSION = 1

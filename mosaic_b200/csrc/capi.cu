@@ -491,7 +491,7 @@ int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, const int* t
                                const int* tile_point_off, const int* tile_points, const uint8_t* local_idx,
                                const int* order, const float* rel_pos, const float* w_q, void* out, int* status,
                                int num_tiles, int max_union, int points_from, int batch, int dim, int num_heads,
-                               int num_neighbors, float scale, void* stream) {
+                               int num_neighbors, int kw_ready, float scale, void* stream) {
   if (num_tiles < 0 || max_union < 0 || points_from <= 0 || batch < 0 || dim <= 0 || num_heads <= 0 ||
       num_neighbors <= 0)
     return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -501,7 +501,8 @@ int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, const int* t
   if (max_union > 256 || max_union % 16 != 0 || num_neighbors > 32) return MOSAIC_ERR_UNSUPPORTED;
   if (tiled_interp_smem_bytes(max_union, num_heads, num_neighbors) > 227 * 1024) return MOSAIC_ERR_UNSUPPORTED;
   if (num_tiles == 0 || batch == 0) return MOSAIC_OK;
-  if (!kv || !kw_workspace || !tile_targets || !tile_point_off || !tile_points || !local_idx || !rel_pos || !w_q ||
+  if (!kv || !kw_workspace || !tile_targets || !tile_point_off || !tile_points || !local_idx || !rel_pos ||
+      (!w_q && !kw_ready) ||
       !out)
     return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(kv) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -513,6 +514,7 @@ int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, const int* t
   l.S_from = points_from; l.B = batch; l.dim = dim; l.k = num_neighbors; l.n_tiles = num_tiles;
   l.max_union = max_union;
   l.scale = scale > 0.f ? scale : 0.125f;
+  l.kw_ready = kw_ready != 0;
   return launch_interp_tiled(l, static_cast<cudaStream_t>(stream));
 }
 

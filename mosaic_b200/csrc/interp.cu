@@ -107,8 +107,8 @@ __global__ void interp_attend_kernel(const __nv_bfloat16* __restrict__ kv, const
 // (fp32, from the bf16 k; kw[.., 3] = 0): by linearity q_j . k = rel_pos[s, j] .
 // kw[n(s, j), b, h], so one 3-vector per (source point, head) replaces the 64-wide q of
 // every (target, neighbour) pair. Lanes own 8 columns (8 lanes per head); a warp holds
-// the 24 weights of its columns in registers for a 256-column pass and sweeps its rows.
-constexpr int kKwRowsPerWarp = 16;
+// the 24 weights of its columns in registers for a 256-column pass over its 4 rows.
+constexpr int kKwRowsPerWarp = 4;
 
 __global__ void __launch_bounds__(256) interp_kw_kernel(const __nv_bfloat16* __restrict__ kv,
                                                         const float* __restrict__ wq, float4* __restrict__ kw,
@@ -116,11 +116,15 @@ __global__ void __launch_bounds__(256) interp_kw_kernel(const __nv_bfloat16* __r
   const int lane = threadIdx.x & 31, H = dim >> 6;
   const long long row0 = (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kKwRowsPerWarp;
   if (row0 >= rows) return;
-  const long long row_end = min(rows, row0 + kKwRowsPerWarp);
   for (int c0 = 0; c0 < dim; c0 += 256) {
     const int c = c0 + lane * 8;
     // dim % 256 == 128: lanes beyond dim in the last pass contribute zeros
     const bool in = c < dim;
+    uint4 raw[kKwRowsPerWarp];  // the warp's rows first, so that their loads are in flight together
+#pragma unroll
+    for (int r = 0; r < kKwRowsPerWarp; ++r)
+      raw[r] = in && row0 + r < rows ? __ldg(reinterpret_cast<const uint4*>(kv + (row0 + r) * 2 * dim + c))
+                                     : make_uint4(0, 0, 0, 0);
     float w[24];
     const float4* w4 = reinterpret_cast<const float4*>(wq + (in ? c : 0) * 3);  // 24 floats, 96 B
 #pragma unroll
@@ -128,19 +132,19 @@ __global__ void __launch_bounds__(256) interp_kw_kernel(const __nv_bfloat16* __r
       const float4 t = __ldg(w4 + i);
       w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
     }
-    for (long long row = row0; row < row_end; ++row) {
-      const uint4 raw = in ? __ldg(reinterpret_cast<const uint4*>(kv + row * 2 * dim + c)) : make_uint4(0, 0, 0, 0);
-      const uint32_t kwd[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int r = 0; r < kKwRowsPerWarp; ++r) {
+      const uint32_t kwd[4] = {raw[r].x, raw[r].y, raw[r].z, raw[r].w};
       float a0 = 0.f, a1 = 0.f, a2 = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float2 kf = make_float2(__uint_as_float(kwd[i] << 16), __uint_as_float(kwd[i] & 0xffff0000u));
-        a0 = fmaf(kf.x, w[6 * i], a0);
-        a1 = fmaf(kf.x, w[6 * i + 1], a1);
-        a2 = fmaf(kf.x, w[6 * i + 2], a2);
-        a0 = fmaf(kf.y, w[6 * i + 3], a0);
-        a1 = fmaf(kf.y, w[6 * i + 4], a1);
-        a2 = fmaf(kf.y, w[6 * i + 5], a2);
+        const float kx = __uint_as_float(kwd[i] << 16), ky = __uint_as_float(kwd[i] & 0xffff0000u);
+        a0 = fmaf(kx, w[6 * i], a0);
+        a1 = fmaf(kx, w[6 * i + 1], a1);
+        a2 = fmaf(kx, w[6 * i + 2], a2);
+        a0 = fmaf(ky, w[6 * i + 3], a0);
+        a1 = fmaf(ky, w[6 * i + 4], a1);
+        a2 = fmaf(ky, w[6 * i + 5], a2);
       }
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
@@ -148,7 +152,7 @@ __global__ void __launch_bounds__(256) interp_kw_kernel(const __nv_bfloat16* __r
         a1 += __shfl_xor_sync(0xffffffffu, a1, o);
         a2 += __shfl_xor_sync(0xffffffffu, a2, o);
       }
-      if ((lane & 7) == 0 && in) kw[row * H + (c >> 6)] = make_float4(a0, a1, a2, 0.f);
+      if ((lane & 7) == 0 && in && row0 + r < rows) kw[(row0 + r) * H + (c >> 6)] = make_float4(a0, a1, a2, 0.f);
     }
   }
 }
@@ -464,7 +468,8 @@ int launch_interp_tiled(const InterpTiledLaunch& a, cudaStream_t stream) {
   if (a.n_tiles == 0 || a.B == 0) return MOSAIC_OK;
   const long long rows = static_cast<long long>(a.S_from) * a.B;
   const long long kw_rows_per_block = 8LL * kKwRowsPerWarp;
-  interp_kw_kernel<<<static_cast<unsigned>((rows + kw_rows_per_block - 1) / kw_rows_per_block), 256, 0, stream>>>(
+  if (!a.kw_ready)
+    interp_kw_kernel<<<static_cast<unsigned>((rows + kw_rows_per_block - 1) / kw_rows_per_block), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(a.kv), a.w_q, reinterpret_cast<float4*>(a.kw), rows, a.dim);
   const size_t smem = tiled_layout(a.max_union, a.dim / 64).total;
   static size_t set_bytes[64] = {};

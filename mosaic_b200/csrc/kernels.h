@@ -150,6 +150,7 @@ struct InterpTiledLaunch {
   int* status;
   int S_from, B, dim, k, n_tiles, max_union;
   float scale;
+  bool kw_ready;             // kw already holds the vectors (the caller computed them)
 };
 int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream);
 int launch_interp_tiled(const InterpTiledLaunch& a, cudaStream_t stream);

@@ -74,14 +74,6 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, vol
 }
 
 // ---------------------------------------------------------------- TMA
-// Untiled bulk copy global -> this CTA's shared memory (no multicast), completing `bytes`
-// of transaction on `bar`. Both addresses 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(__cvta_generic_to_global(src)), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -182,17 +182,21 @@ def build_tiles(neighbors, pos_to_rad, max_union=TILE_MAX_UNION, max_targets=TIL
     }
 
 
-def interp_attend_tiled(kv, tiles, rel_pos, w_q, num_heads, points_from, status=None):
+def interp_attend_tiled(kv, tiles, rel_pos, w_q, num_heads, points_from, status=None, kw=None):
     """interp_attend through mosaic_interp_attend_tiled with the tables of build_tiles
-    (tensors on kv's device)."""
-    _require_cuda(kv, rel_pos, w_q)
+    (tensors on kv's device). `kw` [S_from, B, H, 4] fp32 = (to_q.weight_h^T k_h, 0) per
+    point and head, when the caller has it, skips the kernel that computes it (w_q may
+    then be None)."""
+    _require_cuda(kv, rel_pos, *(() if w_q is None else (w_q,)))
     S_from, B, two_dim = kv.shape
     dim = two_dim // 2
     S_to, kn = tiles["local"].shape
     out = torch.empty(S_to, B, dim, dtype=torch.bfloat16, device=kv.device)
-    kw = torch.empty(S_from, B, num_heads, 3, dtype=torch.float32, device=kv.device)
+    kw_ready = kw is not None
+    if kw is None:  # the call writes (x, y, z, 0) per point and head
+        kw = torch.empty(S_from, B, num_heads, 4, dtype=torch.float32, device=kv.device)
     rp = rel_pos.float().contiguous()
-    wq = w_q.float().contiguous()
+    wq = None if w_q is None else w_q.float().contiguous()
     kvb = _bf16c(kv)
     n_tiles = tiles["tile_targets"].numel() - 1
     with torch.cuda.device(kv.device):
@@ -200,7 +204,7 @@ def interp_attend_tiled(kv, tiles, rel_pos, w_q, num_heads, points_from, status=
             _ptr(kvb), _ptr(kw), _ptr(tiles["tile_targets"]), _ptr(tiles["tile_point_off"]),
             _ptr(tiles["tile_points"]), _ptr(tiles["local"]), _ptr(tiles["order"]), _ptr(rp), _ptr(wq), _ptr(out),
             _ptr(status), n_tiles, int(tiles["max_union"]), int(points_from), B, dim, int(num_heads), kn,
-            (dim // num_heads) ** -0.5, _stream_ptr(kv.device))
+            int(kw_ready), (dim // num_heads) ** -0.5, _stream_ptr(kv.device))
     _lib.check("mosaic_interp_attend_tiled", rc)
     return out
 

@@ -141,6 +141,22 @@ def test_module_after_state_dict_load_rebuilds_tiles():
     close_rel(out, ref)
 
 
+def test_tiled_attend_takes_callers_key_vectors():
+    """kw_ready: key vectors (to_q.weight_h^T k_h, 0) supplied by the caller give the
+    same output as the ones the call computes itself (two members)."""
+    g = torch.Generator().manual_seed(4)
+    dim, H = 768, 12
+    w_q = torch.randn(dim, 3, generator=g).to(DEV)
+    pf, pt, nb, rel = scheme(24, 13, 4, True, 8)
+    kv = torch.randn(pf.shape[0], 2, 2 * dim, generator=g).bfloat16().to(DEV)
+    tiles = dev_tiles(I.build_tiles(nb, pt))
+    a = I.interp_attend_tiled(kv, tiles, rel.to(DEV), w_q, H, pf.shape[0])
+    kw = torch.einsum("pbhd,hdc->pbhc", kv[..., :dim].float().reshape(pf.shape[0], 2, H, 64), w_q.reshape(H, 64, 3))
+    kw = torch.cat([kw, torch.zeros_like(kw[..., :1])], -1).contiguous()
+    b = I.interp_attend_tiled(kv, tiles, rel.to(DEV), None, H, pf.shape[0], kw=kw)
+    close_rel(a, b.float().cpu(), max_rel=1e-2, mean_rel=1e-4)
+
+
 def test_linear_and_row_rms():
     g = torch.Generator().manual_seed(1)
     a = torch.randn(1000, 768, generator=g).bfloat16()
