@@ -30,7 +30,9 @@ and its FLOP rate against the measured bf16 peak (--no-backward skips it); and
 projections + attention + output projection, stage times, the projection GEMMs' FLOP
 rates) next to the reference module's eager sequence on the same GPU (--no-block
 skips it); and, for S1, `interpolation`: CrossAttentionInterpolate in both grid
-directions at the model's sizes, likewise beside its eager sequence (--no-interp).
+directions at the model's sizes, likewise beside its eager sequence (--no-interp), and
+`updown`: HEALPixDownsample 64 -> 32 and HEALPixUpsample 32 -> 64 at the U-Net's first
+stage dims, beside their eager sequences (--no-updown).
 
 `--impl reference` times the reference algorithm on the host cores instead: the
 reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
@@ -94,6 +96,7 @@ def parse():
     p.add_argument("--no-backward", action="store_true")
     p.add_argument("--no-block", action="store_true")
     p.add_argument("--no-interp", action="store_true")
+    p.add_argument("--no-updown", action="store_true")
     return p.parse_args()
 
 
@@ -321,6 +324,70 @@ def interp_leg(stream, steps, warmup, dim=768, heads=12, k=24):
                      "max_abs_vs_eager": diff}
     res["what"] = ("primitives.CrossAttentionInterpolate.forward, dim 768, 12 heads, k 24, one member, "
                    "240 x 121 lat-lon <-> HEALPix nside 64")
+    return res
+
+
+def updown_leg(stream, steps, warmup, dims=(768, 1024), nsides=(64, 32)):
+    """primitives.HEALPixDownsample (nside 64 -> 32, 768 -> 1024 channels) and
+    HEALPixUpsample (32 -> 64, 1024 -> 768, with the skip connection) at the U-Net's first
+    stage, one member: the fused modules (one tcgen05 GEMM with the bias / shortcut
+    epilogue + the RMSNorm pass) beside the reference modules' eager sequence (rearrange,
+    two cuBLAS Linear layers, adds, torch RMSNorm) on the same GPU, same bf16 weights."""
+    import torch.nn.functional as F_
+    from mosaic_b200 import updown as U
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(11)
+    c_fine, c_coarse = dims
+    nf, nc = nsides
+    Fk = (nf // nc) ** 2
+    n = 12 * nc * nc
+    res = {}
+    for kind in ("down", "up"):
+        c_in, c_out = (c_fine, c_coarse) if kind == "down" else (c_coarse, c_fine)
+        m = (U.HEALPixDownsample(c_in, c_out, nf, nc, False) if kind == "down"
+             else U.HEALPixUpsample(c_in, c_out, nc, nf, False)).to(dev)
+        m.proj_x.to(torch.bfloat16)
+        m.proj_pos.to(torch.bfloat16)
+        rows_in = n * Fk if kind == "down" else n
+        xs = [torch.randn(rows_in, 1, c_in, generator=g, device=dev).bfloat16() for _ in range(4)]
+        scs = [torch.randn(n * Fk, 1, c_out, generator=g, device=dev).bfloat16() for _ in range(4)]
+        eps = torch.finfo(torch.bfloat16).eps
+        rel = m.rel_pos.bfloat16()
+
+        def fused(i):
+            return m(xs[i % 4]) if kind == "down" else m(xs[i % 4], scs[i % 4])
+
+        def eager(i):
+            x = xs[i % 4]
+            if kind == "down":
+                y = F_.linear(x.reshape(n, Fk, 1, c_in).permute(0, 2, 1, 3).reshape(n, 1, Fk * c_in), m.proj_x.weight)
+                y = y + F_.linear(rel, m.proj_pos.weight).unsqueeze(1)
+            else:
+                y = F_.linear(x, m.proj_x.weight) + F_.linear(rel, m.proj_pos.weight).unsqueeze(1)
+                y = y.reshape(n, 1, Fk, c_out).permute(0, 2, 1, 3).reshape(n * Fk, 1, c_out) + scs[i % 4]
+            return F_.rms_norm(y, (c_out,), eps=eps)
+
+        with torch.no_grad():
+            diff = float((fused(0).float() - eager(0).float()).abs().max())
+            ts = {}
+            for label, fn in (("fused", fused), ("eager", eager)):
+                for i in range(warmup):
+                    fn(i)
+                torch.cuda.synchronize()
+                a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a_.record(stream)
+                for i in range(steps):
+                    fn(i)
+                b_.record(stream)
+                torch.cuda.synchronize()
+                ts[label] = a_.elapsed_time(b_) / steps
+        flop = 2 * n * (Fk * c_in if kind == "down" else c_in) * (c_out if kind == "down" else Fk * c_out)
+        res[kind] = {"ms": ts["fused"], "gemm_tflops_incl_norm": flop / (ts["fused"] / 1000) / 1e12,
+                     "eager_reference_sequence_ms": ts["eager"], "fused_speedup_vs_eager": ts["eager"] / ts["fused"],
+                     "max_abs_vs_eager": diff, "flop": flop}
+    res["what"] = (f"HEALPixDownsample nside {nf}->{nc} ({c_fine}->{c_coarse}) and HEALPixUpsample {nc}->{nf} "
+                   f"({c_coarse}->{c_fine}, + shortcut), one member, no affine norm")
     return res
 
 
@@ -679,6 +746,11 @@ def b200_arm(args):
         itp = interp_leg(stream, max(3, min(args.steps, 50)), max(3, args.warmup))
         for leg in ("ll_to_hp", "hp_to_ll"):
             itp[leg]["attend_hbm_frac"] = itp[leg]["attend_hbm_gbs"] / hbm
+    ud = None
+    if not args.no_updown and world == 1 and name == "S1":
+        ud = updown_leg(stream, max(3, min(args.steps, 50)), max(3, args.warmup))
+        for leg in ("down", "up"):
+            ud[leg]["frac_of_peak"] = ud[leg]["gemm_tflops_incl_norm"] / tf
     t_att = stage_ms[3] / 1000.0
     achieved = flops_attend(c) / t_att / 1e12
     line = {
@@ -712,6 +784,8 @@ def b200_arm(args):
         line["attention_block"] = blk
     if itp is not None:
         line["interpolation"] = itp
+    if ud is not None:
+        line["updown"] = ud
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -17,11 +17,13 @@ from . import attention
 from .attention import MosaicAttention
 from . import interp
 from .interp import CrossAttentionInterpolate
+from . import updown
+from .updown import HEALPixDownsample, HEALPixUpsample
 from .healpix import get_healpix_grid, healpix_rope_tables, pix2ang_nest, rope_tables
 from .ops import mosaic_attn_bwd, mosaic_attn_fwd, mosaic_sparse_attn, mosaic_sparse_attn_with_lse
 from .primitives import attn_topk, block_attention, block_pool, cmp_attention, mosaic_attn_func
 
 __all__ = [
     "mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "mosaic_attn_fwd", "mosaic_attn_bwd", "mosaic_attn_func", "attn_topk", "block_attention",
-    "block_pool", "cmp_attention", "MosaicAttention", "CrossAttentionInterpolate", "get_healpix_grid", "healpix_rope_tables", "pix2ang_nest", "rope_tables",
+    "block_pool", "cmp_attention", "MosaicAttention", "CrossAttentionInterpolate", "HEALPixDownsample", "HEALPixUpsample", "get_healpix_grid", "healpix_rope_tables", "pix2ang_nest", "rope_tables",
 ]

@@ -33,6 +33,27 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
   return r == CUDA_SUCCESS ? 0 : 1;
 }
 
+int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                      uint64_t stride1_bytes, uint64_t stride2_bytes) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return 1;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {64, 1, 64};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 1;
+}
+
 namespace {
 
 // Self-test of the bounded-wait machinery every pipeline kernel uses: one warp
@@ -516,6 +537,47 @@ int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, const int* t
   l.scale = scale > 0.f ? scale : 0.125f;
   l.kw_ready = kw_ready != 0;
   return launch_interp_tiled(l, static_cast<cudaStream_t>(stream));
+}
+
+static int check_updown(const void* x, const void* w_x, const void* pos_bias, const float* norm_weight, void* out,
+                        float* ss_workspace, int n_coarse, int factor, int batch, int in_dim, int out_dim, float eps) {
+  if (n_coarse < 0 || factor < 1 || batch < 0 || in_dim <= 0 || out_dim <= 0 || !(eps >= 0.f))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (in_dim % 64 != 0 || out_dim % 128 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (n_coarse == 0 || batch == 0) return MOSAIC_OK;
+  if (!x || !w_x || !pos_bias || !out || !ss_workspace) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(w_x) || !aligned16(pos_bias) || !aligned16(out) ||
+      (norm_weight != nullptr && !aligned16(norm_weight)))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  return -1;  // go on
+}
+
+int mosaic_healpix_downsample(const void* x, const void* w_x, const void* pos_bias, const float* norm_weight,
+                              void* out, float* ss_workspace, int* status, int n_coarse, int factor, int batch,
+                              int in_dim, int out_dim, float eps, void* stream) {
+  const int rc = check_updown(x, w_x, pos_bias, norm_weight, out, ss_workspace, n_coarse, factor, batch, in_dim,
+                              out_dim, eps);
+  if (rc >= 0) return rc;
+  UpDownLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.x = x; l.w = w_x; l.pos = pos_bias; l.norm_w = norm_weight; l.out = out; l.ss = ss_workspace;
+  l.status = status; l.n = n_coarse; l.F = factor; l.B = batch; l.c_in = in_dim; l.c_out = out_dim; l.eps = eps;
+  return launch_healpix_down(l, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_healpix_upsample(const void* x, const void* shortcut, const void* w_x, const void* pos_bias,
+                            const float* norm_weight, void* out, float* ss_workspace, int* status, int n_coarse,
+                            int factor, int batch, int in_dim, int out_dim, float eps, void* stream) {
+  const int rc = check_updown(x, w_x, pos_bias, norm_weight, out, ss_workspace, n_coarse, factor, batch, in_dim,
+                              out_dim, eps);
+  if (rc >= 0) return rc;
+  if (shortcut != nullptr && !aligned16(shortcut)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  UpDownLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.x = x; l.shortcut = shortcut; l.w = w_x; l.pos = pos_bias; l.norm_w = norm_weight; l.out = out;
+  l.ss = ss_workspace; l.status = status; l.n = n_coarse; l.F = factor; l.B = batch; l.c_in = in_dim;
+  l.c_out = out_dim; l.eps = eps;
+  return launch_healpix_up(l, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -152,6 +152,21 @@ struct InterpTiledLaunch {
   float scale;
   bool kw_ready;             // kw already holds the vectors (the caller computed them)
 };
+// HEALPix down/upsampling (proj.cu): GEMM + position bias (+ shortcut) + RMSNorm.
+struct UpDownLaunch {
+  const void* x;         // down: [(n f), B, c_in]; up: [n, B, c_in] bf16
+  const void* shortcut;  // up: [(n f), B, c_out] bf16 or null
+  const void* w;         // down: [c_out, F c_in]; up: [F c_out, c_in] bf16 (proj_x.weight)
+  const void* pos;       // down: [n, c_out]; up: [n, F c_out] bf16 (proj_pos(rel_pos))
+  const float* norm_w;   // [c_out] fp32 or null
+  void* out;             // down: [n, B, c_out]; up: [(n f), B, c_out] bf16
+  float* ss;             // [output rows] fp32 scratch
+  int* status;
+  int n, F, B, c_in, c_out;
+  float eps;
+};
+int launch_healpix_down(const UpDownLaunch& a, cudaStream_t stream);
+int launch_healpix_up(const UpDownLaunch& a, cudaStream_t stream);
 int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream);
 int launch_interp_tiled(const InterpTiledLaunch& a, cudaStream_t stream);
 size_t tiled_interp_smem_bytes(int max_union, int H, int k);
@@ -170,5 +185,9 @@ int launch_topk_tc(const TopkLaunch& a, cudaStream_t stream);
 // Encodes a 2D bf16 tensor map over `rows` x `cols` elements (row pitch = cols),
 // 64x64 boxes, 128-byte swizzle. Returns 0 on success.
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
+// 3D bf16 tensor map (d0 innermost, contiguous), strides of dims 1 and 2 in bytes,
+// 64 x 1 x 64 boxes, 128-byte swizzle: a box lands in shared memory like a 64 x 64 2D box.
+int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                      uint64_t stride1_bytes, uint64_t stride2_bytes);
 
 }  // namespace mosaic

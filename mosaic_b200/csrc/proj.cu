@@ -17,6 +17,18 @@
 //   mode kLinear: out[m] = rscale[m] * (a[m] W^T), rows kept in place, rscale optional:
 //                the Linear layers of CrossAttentionInterpolate (to_kv with the row
 //                factor of its RMSNorm folded in, to_o).
+//   mode kDown:  HEALPixDownsample (primitives.py:325-329) for one ensemble member b:
+//                A rows are coarse pixels n, A columns (f, c) the F children's channels,
+//                read straight from x [(n f), B, c] through a 3D tensor map (the
+//                rearrange '(n f) b c -> n b (f c)' is addressing); the epilogue rounds
+//                proj_x's output to bf16, adds the bf16 proj_pos(rel_pos) row of n,
+//                rounds, stores row (n, b) and adds its sum of squares to ss[n B + b].
+//   mode kUp:    HEALPixUpsample (primitives.py:352-357): A = x [n, B, c_in] rows (n, b),
+//                output column j = (f, d); the epilogue adds the bias row, then the
+//                shortcut, rounding after each add as the reference's bf16 ops do, and
+//                stores row ((n f), b) (the rearrange 'n b (f d) -> (n f) b d').
+//                RMSNorm then runs as rms_apply_kernel over the stored rows with the
+//                accumulated sums of squares (the norm spans several column tiles).
 //
 // Tiles of 128 rows x 256 columns, K in 64-wide stages (TMA, 128-byte swizzle, 4-stage
 // ring), fp32 accumulators double-buffered in TMEM so the epilogue of one tile runs
@@ -39,7 +51,7 @@ constexpr int kPABytes = kPBM * kPBK * 2;   // 16 KB
 constexpr int kPBBytes = kPBN * kPBK * 2;   // 32 KB
 constexpr int kPStageBytes = kPABytes + kPBBytes;
 
-enum ProjMode : int { kQkv = 0, kPlain = 1, kLinear = 2 };
+enum ProjMode : int { kQkv = 0, kPlain = 1, kLinear = 2, kDown = 3, kUp = 4 };
 
 struct ProjParams {
   CUtensorMap tm_a, tm_w;
@@ -51,6 +63,11 @@ struct ProjParams {
   const float* rope_sin;
   __nv_bfloat16* out;      // kPlain, kLinear
   const float* rscale;     // kLinear: per-row factor or null
+  const __nv_bfloat16* pos;       // kDown / kUp: [n, N] bias rows
+  const __nv_bfloat16* shortcut;  // kUp: [(n f), B, out_dim] or null
+  float* ss;                      // kDown / kUp: sum of squares per stored row
+  int F, out_dim, member, c_blocks;
+  int a3d;                        // A is the 3D map (c, f, n) of kDown
   int* status;
   int mode;
   int M, K, N;             // GEMM: M rows of A, K, N output columns
@@ -109,6 +126,68 @@ __device__ __forceinline__ void store_chunk(uint4* dst, const uint32_t (&acc)[32
     dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
 }
 
+// 32 output columns of one row for kDown / kUp: y = bf16(bf16(acc) + pos) (+ shortcut,
+// rounded again), stored as bf16; returns the sum of y^2 (fp32) for the row's RMSNorm.
+__device__ __forceinline__ float store_chunk_res(uint4* dst, const uint32_t (&acc)[32], const __nv_bfloat16* pos,
+                                                 const __nv_bfloat16* sc) {
+  uint32_t pw[16], sw[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 t = __ldg(reinterpret_cast<const uint4*>(pos) + i);
+    pw[4 * i] = t.x; pw[4 * i + 1] = t.y; pw[4 * i + 2] = t.z; pw[4 * i + 3] = t.w;
+    const uint4 u = sc != nullptr ? __ldg(reinterpret_cast<const uint4*>(sc) + i) : make_uint4(0, 0, 0, 0);
+    sw[4 * i] = u.x; sw[4 * i + 1] = u.y; sw[4 * i + 2] = u.z; sw[4 * i + 3] = u.w;
+  }
+  float ss = 0.f;
+  uint32_t packed[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
+    x0 = bf16_round(x0 + __uint_as_float(pw[i] << 16));
+    x1 = bf16_round(x1 + __uint_as_float(pw[i] & 0xffff0000u));
+    if (sc != nullptr) {
+      x0 = bf16_round(x0 + __uint_as_float(sw[i] << 16));
+      x1 = bf16_round(x1 + __uint_as_float(sw[i] & 0xffff0000u));
+    }
+    ss = fmaf(x0, x0, fmaf(x1, x1, ss));
+    packed[i] = pack_bf16x2(x0, x1);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+  return ss;
+}
+
+// RMSNorm of stored rows in place: y = bf16(y * rsqrt(ss / D + eps) (* w)), one warp per row.
+__global__ void __launch_bounds__(256) rms_apply_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ ss,
+                                                        const float* __restrict__ w, long long rows, int D,
+                                                        float eps) {
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float r = rsqrtf(__ldg(ss + row) / static_cast<float>(D) + eps);
+  __nv_bfloat16* yr = y + row * D;
+  for (int c = lane * 8; c < D; c += 256) {
+    uint4 v = *reinterpret_cast<const uint4*>(yr + c);
+    uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+    float wt[8];
+    if (w != nullptr) {
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c)), w1 = __ldg(reinterpret_cast<const float4*>(w + c) + 1);
+      wt[0] = w0.x; wt[1] = w0.y; wt[2] = w0.z; wt[3] = w0.w; wt[4] = w1.x; wt[5] = w1.y; wt[6] = w1.z; wt[7] = w1.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wt[i] = 1.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = __uint_as_float(wd[i] << 16) * r * wt[2 * i];
+      const float b = __uint_as_float(wd[i] & 0xffff0000u) * r * wt[2 * i + 1];
+      wd[i] = pack_bf16x2(a, b);
+    }
+    *reinterpret_cast<uint4*>(yr + c) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+}
+
 __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constant__ ProjParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -153,7 +232,13 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
         uint8_t* sa = tiles + st * kPStageBytes;
         uint8_t* sb = sa + kPABytes;
         mbar_arrive_expect_tx_elect(&sm.full[st], kPStageBytes);
-        for (int i = 0; i < 2; ++i) tma_load_2d_elect(sa + i * kPBox, &p.tm_a, &sm.full[st], kb * kPBK, mt * kPBM + 64 * i);
+        if (p.a3d) {
+          const int f = kb / p.c_blocks, c = (kb - f * p.c_blocks) * kPBK;
+          for (int i = 0; i < 2; ++i) tma_load_3d_elect(sa + i * kPBox, &p.tm_a, &sm.full[st], c, f, mt * kPBM + 64 * i);
+        } else {
+          for (int i = 0; i < 2; ++i)
+            tma_load_2d_elect(sa + i * kPBox, &p.tm_a, &sm.full[st], kb * kPBK, mt * kPBM + 64 * i);
+        }
         for (int i = 0; i < 4; ++i) tma_load_2d_elect(sb + i * kPBox, &p.tm_w, &sm.full[st], kb * kPBK, nt * kPBN + 64 * i);
       }
     }
@@ -216,11 +301,32 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
       const int m = mt * kPBM + row;
       const bool live = m < p.M;
       const uint32_t tacc = tmem + lane_off + 256u * a;
+      float ss_part = 0.f;      // kDown / kUp: this row's sum of squares over the chunks below
+      long long ss_row = -1;    // ... and the stored row it belongs to
 #pragma unroll 1
       for (int ci = 4 * half; ci < 4 * half + 4; ++ci) {
         const int c0 = nt * kPBN + 32 * ci;  // warp-uniform
         if (c0 >= p.N) break;
         uint32_t acc[32];
+        if (p.mode == kDown || p.mode == kUp) {
+          tmem_ld32(tacc + 32 * ci, acc);
+          tmem_ld_wait();
+          reg_fence<32>(acc);
+          if (live) {
+            // the warpgroup's 128 columns lie in one f block (out_dim % 128 == 0)
+            const int n = p.mode == kDown ? m : m / p.B;
+            const int f = p.mode == kDown ? 0 : c0 / p.out_dim;
+            const int col = c0 - f * p.out_dim;
+            const long long orow = p.mode == kDown ? static_cast<long long>(m) * p.B + p.member
+                                                   : (static_cast<long long>(n) * p.F + f) * p.B + (m - n * p.B);
+            const size_t o = static_cast<size_t>(orow) * p.out_dim + col;
+            ss_part += store_chunk_res(reinterpret_cast<uint4*>(p.out + o), acc,
+                                       p.pos + static_cast<size_t>(n) * p.N + c0,
+                                       p.shortcut != nullptr ? p.shortcut + o : nullptr);
+            ss_row = orow;
+          }
+          continue;
+        }
         if (p.mode == kPlain) {
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
@@ -304,6 +410,7 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           ++ci;  // the second chunk was consumed with the first
         }
       }
+      if (ss_row >= 0) atomicAdd(p.ss + ss_row, ss_part);
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[a]);
     }
@@ -388,6 +495,75 @@ int launch_linear(const LinearLaunch& a, cudaStream_t stream) {
   p.K = a.K;
   p.N = a.N;
   return launch_proj(p, stream);
+}
+
+int launch_rms_apply(void* y, const float* ss, const float* w, long long rows, int D, float eps,
+                     cudaStream_t stream) {
+  if (rows == 0) return MOSAIC_OK;
+  rms_apply_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(y), ss, w, rows, D, eps);
+  return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int launch_healpix_down(const UpDownLaunch& a, cudaStream_t stream) {
+  const long long rows = static_cast<long long>(a.n) * a.B;
+  if (rows == 0) return MOSAIC_OK;
+  if (cudaMemsetAsync(a.ss, 0, static_cast<size_t>(rows) * sizeof(float), stream) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  for (int b = 0; b < a.B; ++b) {  // one GEMM per member: A = member b's children, read in place
+    ProjParams p;
+    memset(&p, 0, sizeof(p));
+    const uint64_t row_bytes = static_cast<uint64_t>(a.B) * a.c_in * 2;
+    if (make_tmap_bf16_3d(&p.tm_a, static_cast<const __nv_bfloat16*>(a.x) + static_cast<size_t>(b) * a.c_in,
+                          static_cast<uint64_t>(a.c_in), static_cast<uint64_t>(a.F), static_cast<uint64_t>(a.n),
+                          row_bytes, row_bytes * a.F) ||
+        make_tmap_bf16_2d(&p.tm_w, a.w, static_cast<uint64_t>(a.c_out), static_cast<uint64_t>(a.F) * a.c_in))
+      return MOSAIC_ERR_CUDA;
+    p.a3d = 1;
+    p.c_blocks = a.c_in / kPBK;
+    p.out = static_cast<__nv_bfloat16*>(a.out);
+    p.pos = static_cast<const __nv_bfloat16*>(a.pos);
+    p.ss = a.ss;
+    p.status = a.status;
+    p.mode = kDown;
+    p.M = a.n;
+    p.K = a.F * a.c_in;
+    p.N = a.c_out;
+    p.B = a.B;
+    p.F = a.F;
+    p.out_dim = a.c_out;
+    p.member = b;
+    const int rc = launch_proj(p, stream);
+    if (rc != MOSAIC_OK) return rc;
+  }
+  return launch_rms_apply(a.out, a.ss, a.norm_w, rows, a.c_out, a.eps, stream);
+}
+
+int launch_healpix_up(const UpDownLaunch& a, cudaStream_t stream) {
+  const long long rows = static_cast<long long>(a.n) * a.F * a.B;
+  if (rows == 0) return MOSAIC_OK;
+  if (cudaMemsetAsync(a.ss, 0, static_cast<size_t>(rows) * sizeof(float), stream) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  ProjParams p;
+  memset(&p, 0, sizeof(p));
+  if (make_tmap_bf16_2d(&p.tm_a, a.x, static_cast<uint64_t>(a.n) * a.B, static_cast<uint64_t>(a.c_in)) ||
+      make_tmap_bf16_2d(&p.tm_w, a.w, static_cast<uint64_t>(a.F) * a.c_out, static_cast<uint64_t>(a.c_in)))
+    return MOSAIC_ERR_CUDA;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.pos = static_cast<const __nv_bfloat16*>(a.pos);
+  p.shortcut = static_cast<const __nv_bfloat16*>(a.shortcut);
+  p.ss = a.ss;
+  p.status = a.status;
+  p.mode = kUp;
+  p.M = a.n * a.B;
+  p.K = a.c_in;
+  p.N = a.F * a.c_out;
+  p.B = a.B;
+  p.F = a.F;
+  p.out_dim = a.c_out;
+  const int rc = launch_proj(p, stream);
+  if (rc != MOSAIC_OK) return rc;
+  return launch_rms_apply(a.out, a.ss, a.norm_w, rows, a.c_out, a.eps, stream);
 }
 
 int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream) {

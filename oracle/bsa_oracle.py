@@ -1,5 +1,6 @@
 """CPU restatement of the reference's block-sparse attention forward, its backward
-and the layers around it (the attention block, the cross-attention interpolation).
+and the layers around it (the attention block, the cross-attention interpolation,
+the HEALPix down/upsampling layers).
 
 TEST INFRASTRUCTURE: the checker for the CUDA path and the timed CPU baseline.
 Only tests/, __graft_entry__.smoke() and bench.py's CPU legs use it; the product
@@ -332,6 +333,54 @@ def cross_attention_interpolate(x_from, neighbors, rel_pos, w_q, w_kv, w_o, num_
     a = torch.softmax(scores, dim=1)
     out = (a * v).sum(dim=1).reshape(neighbors.shape[0], B, dim)
     return out @ w_o.float().t()
+
+
+def rad_to_xyz(lonlat):
+    """utils.rad_to_xyz (utils.py:7-16): (lon, lat) radians -> unit xyz."""
+    lon, lat = lonlat[..., 0], lonlat[..., 1]
+    return torch.stack([torch.cos(lat) * torch.cos(lon), torch.cos(lat) * torch.sin(lon), torch.sin(lat)], dim=-1)
+
+
+def healpix_updown_rel_pos(nside_fine, nside_coarse):
+    """The rel_pos buffer of HEALPixDownsample / HEALPixUpsample (primitives.py:317-322,
+    345-350): per coarse pixel n, its F = (nside_fine / nside_coarse)^2 nested children's
+    unit vectors minus its own, flattened to [n, (f xyz)], then standardised per column
+    (torch.std, unbiased) with 1e-6 added to the deviation. fp32 [n_coarse, 3 F]."""
+    F = (nside_fine // nside_coarse) ** 2
+    fine = rad_to_xyz(torch.deg2rad(healpix_grid_fast(nside_fine).float()))
+    coarse = rad_to_xyz(torch.deg2rad(healpix_grid_fast(nside_coarse).float()))
+    rel = (fine.reshape(-1, F, 3) - coarse[:, None]).reshape(-1, 3 * F)
+    return (rel - rel.mean(dim=0, keepdim=True)) / (rel.std(dim=0, keepdim=True) + 1e-6)
+
+
+def rms_norm(x, eps, weight=None):
+    """torch.nn.RMSNorm.forward in fp32: x / sqrt(mean(x^2, -1) + eps), times weight."""
+    x = x.float()
+    y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+    return y if weight is None else y * weight.float()
+
+
+def healpix_downsample(x, w_x, w_pos, rel_pos, eps, norm_weight=None):
+    """HEALPixDownsample.forward (primitives.py:325-329), fp32: x [(n f), B, C] ->
+    rearrange '(n f) b c -> n b (f c)', proj_x, + proj_pos(rel_pos) broadcast over b,
+    RMSNorm. w_x [out, F C], w_pos [out, 3 F], rel_pos [n, 3 F] -> [n, B, out]."""
+    F = rel_pos.shape[1] // 3
+    nF, B, C = x.shape
+    xr = x.float().reshape(nF // F, F, B, C).permute(0, 2, 1, 3).reshape(nF // F, B, F * C)
+    y = xr @ w_x.float().t() + (rel_pos.float() @ w_pos.float().t()).unsqueeze(1)
+    return rms_norm(y, eps, norm_weight)
+
+
+def healpix_upsample(x, shortcut, w_x, w_pos, rel_pos, eps, norm_weight=None):
+    """HEALPixUpsample.forward (primitives.py:352-357), fp32: x [n, B, C_in] -> proj_x +
+    proj_pos(rel_pos) broadcast over b -> [n, B, (f d)] -> rearrange 'n b (f d) -> (n f) b d',
+    + shortcut [(n f), B, d], RMSNorm. w_x [F d, C_in], w_pos [F d, 3 F] -> [(n f), B, d]."""
+    F = rel_pos.shape[1] // 3
+    n, B, _ = x.shape
+    y = x.float() @ w_x.float().t() + (rel_pos.float() @ w_pos.float().t()).unsqueeze(1)
+    d = y.shape[-1] // F
+    y = y.reshape(n, B, F, d).permute(0, 2, 1, 3).reshape(n * F, B, d) + shortcut.float()
+    return rms_norm(y, eps, norm_weight)
 
 
 def mosaic_attn_func_sample(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,

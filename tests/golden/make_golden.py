@@ -2,7 +2,9 @@
 
 Run from the repository root in a container that has the reference checkout:
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/mosaic/reference
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/mosaic/reference [part ...]
+
+(parts: attn bwd block interp updown; all by default).
 
 It imports the reference's `ops` and `primitives` modules and runs, on the CPU:
   * primitives.mosaic_attn_func / attn_topk / RoPE / the einops pooling as-is;
@@ -45,6 +47,11 @@ The interpolation fixtures (interp_*.npz) run primitives.CrossAttentionInterpola
 (its BallTree neighbour search, relative positions and forward) in fp32 on seeded
 bf16-valued weights and input between a small lat-lon grid and HEALPix nside 4, in
 both directions, and keep the neighbour table, 64 sampled target rows and fp64 sums.
+
+The down/upsampling fixtures (down_*.npz, up_*.npz) run primitives.HEALPixDownsample /
+HEALPixUpsample (their rel_pos construction and forward, with and without the affine
+RMSNorm, factor 4 and 16, batch 1 and 2) in fp32 on seeded bf16-valued weights and input,
+and keep rel_pos, 64 sampled output rows and fp64 per-member sums.
 """
 import os
 import sys
@@ -251,16 +258,66 @@ def main_interp(P):
         print(name, "written")
 
 
-def main(ref_dir):
+UPDOWN_CONFIGS = {
+    # name: kind, nside_before, nside_after, B, c_in, c_out, affine, seed
+    "down_hp8_to_hp4_c64_o128_b2": ("down", 8, 4, 2, 64, 128, False, 40),
+    "down_hp16_to_hp4_c64_o128_b1_affine": ("down", 16, 4, 1, 64, 128, True, 41),
+    "up_hp4_to_hp8_c128_o128_b2_affine": ("up", 4, 8, 2, 128, 128, True, 42),
+}
+
+
+def main_updown(P):
+    """primitives.HEALPixDownsample / HEALPixUpsample themselves (fp32 on the CPU): their
+    rel_pos construction (with the oracle's HEALPix centres, healpy being absent) and
+    forward on seeded bf16-valued weights and input. Keeps rel_pos, 64 sampled output rows
+    (fp16) and fp64 per-member sums."""
+    sys.path.insert(0, ROOT)
+    from oracle import bsa_oracle as O
+    from tests.golden_util import draw_updown_inputs
+    P.get_healpix_grid = O.healpix_grid
+    for name, (kind, nb, na, B, c_in, c_out, affine, seed) in UPDOWN_CONFIGS.items():
+        F = (max(nb, na) // min(nb, na)) ** 2
+        n_coarse = 12 * min(nb, na) ** 2
+        x, sc, w_x, w_pos, w_norm = draw_updown_inputs(kind, n_coarse, F, B, c_in, c_out, affine, seed)
+        cls = P.HEALPixDownsample if kind == "down" else P.HEALPixUpsample
+        mod = cls(c_in, c_out, nb, na, rmsnorm_elementwise_affine=affine)
+        with torch.no_grad():
+            mod.proj_x.weight.copy_(w_x.float())
+            mod.proj_pos.weight.copy_(w_pos.float())
+            if affine:
+                mod.norm.weight.copy_(w_norm.float())
+            out = mod(x.float()) if kind == "down" else mod(x.float(), sc.float())
+        flat = out.reshape(-1, out.shape[-1])
+        rows = torch.sort(torch.randperm(flat.shape[0], generator=torch.Generator().manual_seed(500 + seed))[:64]).values
+        np.savez_compressed(
+            os.path.join(HERE, f"{name}.npz"),
+            meta=np.array([0 if kind == "down" else 1, nb, na, B, c_in, c_out, int(affine), seed], dtype=np.int64),
+            rel_pos=mod.rel_pos.numpy().astype(np.float32),
+            rows=rows.numpy().astype(np.int32),
+            out_rows=flat[rows].to(torch.float16).numpy(),
+            out_sums=out.double().sum(dim=(0, 2)).numpy(),
+        )
+        print(name, "written")
+
+
+def main(ref_dir, parts=("attn", "bwd", "block", "interp", "updown")):
     sys.path.insert(0, ROOT)
     from oracle import bsa_oracle as O
     ops, P = _import_reference(ref_dir)
+    if "updown" in parts:
+        main_updown(P)
+    if "attn" not in parts and "block" not in parts:
+        if "bwd" in parts:
+            main_bwd(ops)
+        if "interp" in parts:
+            main_interp(P)
+        return
     triton_sparse = make_triton_sparse(ops)
     P.flash_attn_func = sdpa_gqa
     P.mosaic_sparse_attn = triton_sparse
     real_topk = P.attn_topk
 
-    for name, (B, N, Hq, Hk, bs, K, bas, seed) in CONFIGS.items():
+    for name, (B, N, Hq, Hk, bs, K, bas, seed) in (CONFIGS.items() if "attn" in parts else ()):
         g = torch.Generator().manual_seed(seed)
         q_raw = torch.randn(B, N, Hq, 64, generator=g).bfloat16()
         k_raw = torch.randn(B, N, Hk, 64, generator=g).bfloat16()
@@ -305,13 +362,16 @@ def main(ref_dir):
             out_sums=sums(out), o_ba_sums=sums(o_ba), o_slc_sums=sums(o_slc),
         )
         print(name, "written")
-    main_bwd(ops)
-    main_block(P)
-    main_interp(P)
+    if "bwd" in parts:
+        main_bwd(ops)
+    if "block" in parts:
+        main_block(P)
+    if "interp" in parts:
+        main_interp(P)
 
 
 if __name__ == "__main__":
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOSAIC_REFERENCE_DIR", "")
     if not ref or not os.path.isdir(ref):
-        raise SystemExit("usage: TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout>")
-    main(ref)
+        raise SystemExit("usage: TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout> [part ...]")
+    main(ref, tuple(sys.argv[2:]) or ("attn", "bwd", "block", "interp", "updown"))

@@ -13,7 +13,7 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 def fixture_names():
     """The forward fixtures."""
-    return sorted(n for n in _all_names() if not n.startswith(("bwd_", "block_", "interp_")))
+    return sorted(n for n in _all_names() if not n.startswith(("bwd_", "block_", "interp_", "down_", "up_")))
 
 
 def bwd_fixture_names():
@@ -120,6 +120,41 @@ def interp_grids(n_lon, n_lat, nside):
     ll = torch.deg2rad(torch.stack(torch.meshgrid(lon, lat, indexing="ij"), -1).reshape(-1, 2))
     hp = torch.deg2rad(O.healpix_grid(nside))
     return ll, hp
+
+
+def draw_updown_inputs(kind, n_coarse, F, B, c_in, c_out, affine, seed):
+    """Seeded bf16 input and weights of a HEALPix down/upsampling case (make_golden.py uses
+    this too): for "down" x [(n f), B, c_in], proj_x.weight [c_out, F c_in]; for "up"
+    x [n, B, c_in], shortcut [(n f), B, c_out], proj_x.weight [F c_out, c_in]; proj_pos.weight
+    [cols, 3 F]; norm weight 1 + 0.1 N(0, 1) when affine, else None. Values ~ N(0, 1),
+    weights ~ N(0, 1 / fan_in)."""
+    g = torch.Generator().manual_seed(seed)
+    if kind == "down":
+        x = torch.randn(n_coarse * F, B, c_in, generator=g).bfloat16()
+        shortcut = None
+        w_x = (torch.randn(c_out, F * c_in, generator=g) * (F * c_in) ** -0.5).bfloat16()
+        cols = c_out
+    else:
+        x = torch.randn(n_coarse, B, c_in, generator=g).bfloat16()
+        shortcut = torch.randn(n_coarse * F, B, c_out, generator=g).bfloat16()
+        w_x = (torch.randn(F * c_out, c_in, generator=g) * c_in ** -0.5).bfloat16()
+        cols = F * c_out
+    w_pos = (torch.randn(cols, 3 * F, generator=g) * (3 * F) ** -0.5).bfloat16()
+    w_norm = (1 + 0.1 * torch.randn(c_out, generator=g)).bfloat16() if affine else None
+    return x, shortcut, w_x, w_pos, w_norm
+
+
+def updown_fixture_names():
+    """The HEALPix down/upsampling fixtures (down_*.npz, up_*.npz)."""
+    return sorted(n for n in _all_names() if n.startswith(("down_", "up_")))
+
+
+def load_updown(name):
+    d = dict(np.load(os.path.join(GOLDEN_DIR, name + ".npz")))
+    kind, nside_before, nside_after, B, c_in, c_out, affine, seed = (int(v) for v in d.pop("meta"))
+    d.update(kind="down" if kind == 0 else "up", nside_before=nside_before, nside_after=nside_after, B=B, c_in=c_in,
+             c_out=c_out, affine=bool(affine), seed=seed)
+    return d
 
 
 def draw_interp_inputs(S_from, B, dim, seed):

@@ -99,3 +99,23 @@ def test_interp_tiles_reject_bad_tables():
         I.build_tiles(torch.tensor([[0, 1, 2], [3, 4, 3]]), None)
     with pytest.raises(ValueError):  # union not a multiple of the mma k step
         I.build_tiles(torch.arange(6).reshape(2, 3), None, max_union=40)
+
+
+@pytest.mark.parametrize("kind", ["down", "up"])
+def test_updown_modules_match_the_reference_structure(kind):
+    """HEALPixDownsample / HEALPixUpsample: the reference's parameters and buffer, and a
+    rel_pos equal to the reference module's own (from the fixtures)."""
+    from tests import golden_util as GU
+    name = [n for n in GU.updown_fixture_names() if n.startswith(kind + "_")][0]
+    d = GU.load_updown(name)
+    cls = M.HEALPixDownsample if kind == "down" else M.HEALPixUpsample
+    m = cls(d["c_in"], d["c_out"], d["nside_before"], d["nside_after"], rmsnorm_elementwise_affine=d["affine"])
+    keys = {"proj_x.weight", "proj_pos.weight", "rel_pos"} | ({"norm.weight"} if d["affine"] else set())
+    assert set(m.state_dict()) == keys
+    F = m.factor
+    fan = d["c_in"] * (F if kind == "down" else 1)
+    assert tuple(m.proj_x.weight.shape) == ((d["c_out"], fan) if kind == "down" else (F * d["c_out"], fan))
+    torch.testing.assert_close(m.rel_pos, torch.from_numpy(d["rel_pos"]), atol=1e-5, rtol=1e-5)
+    x = torch.randn(m.rel_pos.shape[0] * (F if kind == "down" else 1), 1, d["c_in"])
+    with pytest.raises(NotImplementedError):
+        m(x) if kind == "down" else m(x, None)

@@ -256,3 +256,32 @@ def test_linear_and_rms_reject_bad_arguments():
     assert lib.mosaic_linear(FAKE, FAKE, FAKE, None, None, 0, 128, 64, None) == _lib.MOSAIC_OK
     assert lib.mosaic_row_rms(FAKE, FAKE, 10, 100, 1e-6, None) == _lib.MOSAIC_ERR_UNSUPPORTED
     assert lib.mosaic_row_rms(FAKE, None, 10, 128, 1e-6, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+
+
+def _updown_call(kind, **kw):
+    a = dict(x=ctypes.c_void_p(0x10000), sc=ctypes.c_void_p(0x20000), w=ctypes.c_void_p(0x30000),
+             pos=ctypes.c_void_p(0x40000), nw=None, out=ctypes.c_void_p(0x50000), ss=ctypes.c_void_p(0x60000),
+             n=192, F=4, B=1, c_in=768, c_out=1024, eps=1e-2)
+    a.update(kw)
+    lib = _lib.load()
+    if kind == "down":
+        return lib.mosaic_healpix_downsample(a["x"], a["w"], a["pos"], a["nw"], a["out"], a["ss"], None, a["n"], a["F"],
+                                             a["B"], a["c_in"], a["c_out"], a["eps"], None)
+    return lib.mosaic_healpix_upsample(a["x"], a["sc"], a["w"], a["pos"], a["nw"], a["out"], a["ss"], None, a["n"],
+                                       a["F"], a["B"], a["c_in"], a["c_out"], a["eps"], None)
+
+
+@pytest.mark.parametrize("kind", ["down", "up"])
+@pytest.mark.parametrize("kw,code", [
+    (dict(c_in=96), _lib.MOSAIC_ERR_UNSUPPORTED),     # not a multiple of 64
+    (dict(c_out=640 + 64), _lib.MOSAIC_ERR_UNSUPPORTED),  # not a multiple of 128
+    (dict(n=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(F=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(eps=-1.0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(ss=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(pos=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(out=ctypes.c_void_p(0x50008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # misaligned
+    (dict(n=0), _lib.MOSAIC_OK),                      # empty: nothing to do, no CUDA call
+])
+def test_healpix_updown_rejects_bad_arguments(kind, kw, code):
+    assert _updown_call(kind, **kw) == code

@@ -212,3 +212,39 @@ def test_neighbour_search_matches_balltree_up_to_ties(name):
     dist = lambda idx: torch.sort((a.unsqueeze(1) * b[idx]).sum(-1), 1).values
     assert (dist(mine) - dist(nb)).abs().max() < 1e-12
     assert (torch.sort(mine, 1).values == torch.sort(nb, 1).values).all(1).float().mean() > 0.9
+
+
+# ----------------------------------------------------------------------------- HEALPix down/upsampling
+UPDOWN_NAMES = GU.updown_fixture_names()
+
+
+def test_updown_fixtures_present():
+    assert len(UPDOWN_NAMES) >= 3
+
+
+def updown_oracle(d):
+    """The oracle's forward of a down/upsampling fixture case (fp32, RMSNorm epsilon of
+    the fp32 run the fixture made)."""
+    fine, coarse = max(d["nside_before"], d["nside_after"]), min(d["nside_before"], d["nside_after"])
+    F = (fine // coarse) ** 2
+    rel = O.healpix_updown_rel_pos(fine, coarse)
+    x, sc, w_x, w_pos, w_norm = GU.draw_updown_inputs(d["kind"], 12 * coarse ** 2, F, d["B"], d["c_in"], d["c_out"],
+                                                      d["affine"], d["seed"])
+    eps = torch.finfo(torch.float32).eps
+    if d["kind"] == "down":
+        return rel, O.healpix_downsample(x, w_x, w_pos, rel, eps, w_norm)
+    return rel, O.healpix_upsample(x, sc, w_x, w_pos, rel, eps, w_norm)
+
+
+@pytest.mark.parametrize("name", UPDOWN_NAMES)
+def test_healpix_updown_matches_reference(name):
+    """oracle.healpix_downsample / healpix_upsample and healpix_updown_rel_pos against
+    primitives.HEALPixDownsample / HEALPixUpsample (factor 4 and 16, batch 1 and 2,
+    with and without the affine RMSNorm)."""
+    d = GU.load_updown(name)
+    rel, out = updown_oracle(d)
+    torch.testing.assert_close(rel, torch.from_numpy(d["rel_pos"]), atol=1e-5, rtol=1e-5)
+    flat = out.reshape(-1, out.shape[-1])
+    diff = (flat[torch.from_numpy(d["rows"]).long()] - GU.t(d["out_rows"])).abs()
+    assert diff.max() < 3e-3 and diff.mean() < 3e-4, (diff.max(), diff.mean())
+    torch.testing.assert_close(out.double().sum(dim=(0, 2)), torch.from_numpy(d["out_sums"]), atol=1e-2, rtol=1e-4)
