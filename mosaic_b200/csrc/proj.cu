@@ -126,11 +126,10 @@ __device__ __forceinline__ void store_chunk(uint4* dst, const uint32_t (&acc)[32
     dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
 }
 
-// 32 output columns of one row for kDown / kUp: y = bf16(bf16(acc) + pos) (+ shortcut,
-// rounded again), stored as bf16; returns the sum of y^2 (fp32) for the row's RMSNorm.
-__device__ __forceinline__ float store_chunk_res(uint4* dst, const uint32_t (&acc)[32], const __nv_bfloat16* pos,
-                                                 const __nv_bfloat16* sc) {
-  uint32_t pw[16], sw[16];
+// The bias (and shortcut) words of 32 output columns, loaded before the accumulators
+// are read from TMEM so that the two latencies overlap.
+__device__ __forceinline__ void load_chunk_res(uint32_t (&pw)[16], uint32_t (&sw)[16], const __nv_bfloat16* pos,
+                                               const __nv_bfloat16* sc) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint4 t = __ldg(reinterpret_cast<const uint4*>(pos) + i);
@@ -138,6 +137,13 @@ __device__ __forceinline__ float store_chunk_res(uint4* dst, const uint32_t (&ac
     const uint4 u = sc != nullptr ? __ldg(reinterpret_cast<const uint4*>(sc) + i) : make_uint4(0, 0, 0, 0);
     sw[4 * i] = u.x; sw[4 * i + 1] = u.y; sw[4 * i + 2] = u.z; sw[4 * i + 3] = u.w;
   }
+}
+
+// 32 output columns of one row for kDown / kUp: y = bf16(bf16(acc) + pos) (+ shortcut,
+// rounded again), stored as bf16; returns the sum of y^2 (fp32) for the row's RMSNorm.
+__device__ __forceinline__ float store_chunk_res(uint4* dst, const uint32_t (&acc)[32], const uint32_t (&pw)[16],
+                                                 const uint32_t (&sw)[16], bool has_sc) {
+  const bool sc = has_sc;
   float ss = 0.f;
   uint32_t packed[16];
 #pragma unroll
@@ -145,7 +151,7 @@ __device__ __forceinline__ float store_chunk_res(uint4* dst, const uint32_t (&ac
     float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
     x0 = bf16_round(x0 + __uint_as_float(pw[i] << 16));
     x1 = bf16_round(x1 + __uint_as_float(pw[i] & 0xffff0000u));
-    if (sc != nullptr) {
+    if (sc) {
       x0 = bf16_round(x0 + __uint_as_float(sw[i] << 16));
       x1 = bf16_round(x1 + __uint_as_float(sw[i] & 0xffff0000u));
     }
@@ -188,6 +194,8 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(__nv_bfloat16* __restric
   }
 }
 
+// One instantiation per mode, so that each epilogue gets its own register allocation.
+template <int kMode>
 __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constant__ ProjParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -293,41 +301,61 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
     for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++it) {
       const int a = it & 1;
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
+      const int m = mt * kPBM + row;
+      const bool live = m < p.M;
+      const uint32_t tacc = tmem + lane_off + 256u * a;
+      if constexpr (kMode == kDown || kMode == kUp) {
+        // The warpgroup's (up to) 4 chunks of 32 columns lie in one child block f
+        // (out_dim % 128 == 0), so the output row and the bias row are fixed for the
+        // tile. The bias / shortcut words of chunk k + 1 load while chunk k is stored,
+        // and those of chunk 0 while the MMAs of this tile finish.
+        const int cbase = nt * kPBN + 128 * half;
+        const int nch = cbase >= p.N ? 0 : min(4, (p.N - cbase) / 32);
+        const int n = kMode == kDown ? m : m / p.B;
+        const int f = kMode == kDown ? 0 : cbase / p.out_dim;
+        const long long orow = kMode == kDown ? static_cast<long long>(m) * p.B + p.member
+                                              : (static_cast<long long>(n) * p.F + f) * p.B + (m - n * p.B);
+        const size_t o0 = static_cast<size_t>(orow) * p.out_dim + (cbase - f * p.out_dim);
+        const __nv_bfloat16* pos0 = p.pos + static_cast<size_t>(n) * p.N + cbase;
+        const __nv_bfloat16* sc0 = p.shortcut != nullptr ? p.shortcut + o0 : nullptr;
+        uint32_t pw[2][16], sw[2][16];
+        if (live && nch > 0) load_chunk_res(pw[0], sw[0], pos0, sc0);
+        if (!bounded_wait(&sm.acc_full[a], (it >> 1) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float ss_part = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (k >= nch) break;
+          if (live && k + 1 < nch)
+            load_chunk_res(pw[(k + 1) & 1], sw[(k + 1) & 1], pos0 + 32 * (k + 1),
+                           sc0 != nullptr ? sc0 + 32 * (k + 1) : nullptr);
+          uint32_t acc[32];
+          tmem_ld32(tacc + 32 * (4 * half + k), acc);
+          tmem_ld_wait();
+          reg_fence<32>(acc);
+          if (live)
+            ss_part += store_chunk_res(reinterpret_cast<uint4*>(p.out + o0 + 32 * k), acc, pw[k & 1], sw[k & 1],
+                                       sc0 != nullptr);
+        }
+        if (live && nch > 0) atomicAdd(p.ss + orow, ss_part);
+        tc_fence_before();
+        mbar_arrive(&sm.acc_empty[a]);
+        continue;
+      }
       if (!bounded_wait(&sm.acc_full[a], (it >> 1) & 1, abort_flag, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int m = mt * kPBM + row;
-      const bool live = m < p.M;
-      const uint32_t tacc = tmem + lane_off + 256u * a;
-      float ss_part = 0.f;      // kDown / kUp: this row's sum of squares over the chunks below
-      long long ss_row = -1;    // ... and the stored row it belongs to
 #pragma unroll 1
       for (int ci = 4 * half; ci < 4 * half + 4; ++ci) {
         const int c0 = nt * kPBN + 32 * ci;  // warp-uniform
         if (c0 >= p.N) break;
         uint32_t acc[32];
-        if (p.mode == kDown || p.mode == kUp) {
-          tmem_ld32(tacc + 32 * ci, acc);
-          tmem_ld_wait();
-          reg_fence<32>(acc);
-          if (live) {
-            // the warpgroup's 128 columns lie in one f block (out_dim % 128 == 0)
-            const int n = p.mode == kDown ? m : m / p.B;
-            const int f = p.mode == kDown ? 0 : c0 / p.out_dim;
-            const int col = c0 - f * p.out_dim;
-            const long long orow = p.mode == kDown ? static_cast<long long>(m) * p.B + p.member
-                                                   : (static_cast<long long>(n) * p.F + f) * p.B + (m - n * p.B);
-            const size_t o = static_cast<size_t>(orow) * p.out_dim + col;
-            ss_part += store_chunk_res(reinterpret_cast<uint4*>(p.out + o), acc,
-                                       p.pos + static_cast<size_t>(n) * p.N + c0,
-                                       p.shortcut != nullptr ? p.shortcut + o : nullptr);
-            ss_row = orow;
-          }
-          continue;
-        }
-        if (p.mode == kPlain) {
+        if (kMode == kPlain) {
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
@@ -339,7 +367,7 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           }
           continue;
         }
-        if (p.mode == kLinear) {
+        if (kMode == kLinear) {
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
@@ -410,7 +438,6 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           ++ci;  // the second chunk was consumed with the first
         }
       }
-      if (ss_row >= 0) atomicAdd(p.ss + ss_row, ss_part);
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[a]);
     }
@@ -433,16 +460,35 @@ int sm_count_p() {
   return count[dev];
 }
 
-int launch_proj(ProjParams& p, cudaStream_t stream) {
+template <int kMode>
+int set_proj_smem(int dev) {
   static bool done[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOSAIC_ERR_CUDA;
   if (!done[dev]) {
-    if (cudaFuncSetAttribute(proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(proj_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kProjSmemBytes)) != cudaSuccess)
       return MOSAIC_ERR_CUDA;
     done[dev] = true;
   }
+  return MOSAIC_OK;
+}
+
+template <int kMode>
+void launch_proj_mode(const ProjParams& p, int grid, cudaStream_t stream) {
+  proj_kernel<kMode><<<grid, kPThreads, kProjSmemBytes, stream>>>(p);
+}
+
+int launch_proj(ProjParams& p, cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOSAIC_ERR_CUDA;
+  int rc = MOSAIC_ERR_INVALID_ARGUMENT;
+  switch (p.mode) {
+    case kQkv: rc = set_proj_smem<kQkv>(dev); break;
+    case kPlain: rc = set_proj_smem<kPlain>(dev); break;
+    case kLinear: rc = set_proj_smem<kLinear>(dev); break;
+    case kDown: rc = set_proj_smem<kDown>(dev); break;
+    case kUp: rc = set_proj_smem<kUp>(dev); break;
+  }
+  if (rc != MOSAIC_OK) return rc;
   const int sms = sm_count_p();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   p.m_tiles = (p.M + kPBM - 1) / kPBM;
@@ -450,7 +496,15 @@ int launch_proj(ProjParams& p, cudaStream_t stream) {
   p.tiles = p.m_tiles * p.n_tiles;
   p.k_blocks = p.K / kPBK;
   const int grid = p.tiles < sms ? p.tiles : sms;
-  if (grid > 0) proj_kernel<<<grid, kPThreads, kProjSmemBytes, stream>>>(p);
+  if (grid > 0) {
+    switch (p.mode) {
+      case kQkv: launch_proj_mode<kQkv>(p, grid, stream); break;
+      case kPlain: launch_proj_mode<kPlain>(p, grid, stream); break;
+      case kLinear: launch_proj_mode<kLinear>(p, grid, stream); break;
+      case kDown: launch_proj_mode<kDown>(p, grid, stream); break;
+      case kUp: launch_proj_mode<kUp>(p, grid, stream); break;
+    }
+  }
   return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
