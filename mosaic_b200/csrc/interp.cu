@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(256) interp_kw_kernel(const __nv_bfloat16* __r
 // and the P_s positions it writes stay the same from head to head. Shared memory:
 //   V_s[2]  U x (2 heads x 64 bf16), rows padded to 272 B  (cp.async 16-byte copies,
 //                                                          double-buffered over chunks)
-//   kw_s    U x H x float4                                (cp.async, once)
+//   kw_s    H x U x float4, head-major                    (cp.async, once; at fixed head,
+//                                                          random points spread over all banks)
 //   P_s     per warp 16 x U bf16, rows padded (+16 B)     (scattered softmax weights)
 //   pts_s   U int32
 // The copies are the per-thread asynchronous kind: a tile moves a few hundred 256-byte
@@ -314,7 +315,8 @@ __global__ void __launch_bounds__(kTileThreads) interp_tiled_kernel(
   __syncthreads();
   for (int u = threadIdx.x >> 4; u < U; u += kTileThreads >> 4) {  // 16 threads per point
     const float4* src = kw + (static_cast<size_t>(pts_s[u]) * B + b) * H;
-    for (int hh = threadIdx.x & 15; hh < H; hh += 16) cp_async16(smem + L.kw + (static_cast<size_t>(u) * H + hh) * 16, src + hh);
+    for (int hh = threadIdx.x & 15; hh < H; hh += 16)
+      cp_async16(smem + L.kw + (static_cast<size_t>(hh) * U + u) * 16, src + hh);
   }
   stage_v_chunk(v_s0, pts_s, kv, U, row_elems, b_off, 0);
   cp_async_commit();
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(kTileThreads) interp_tiled_kernel(
       float m = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float4 w = kw_s[max(ku[i], 0) * H + h];
+        const float4 w = kw_s[h * U + max(ku[i], 0)];
         sc[i] = ku[i] >= 0 ? fmaf(r2[i], w.z, fmaf(r1[i], w.y, r0[i] * w.x)) * scale_log2 : -INFINITY;
         m = fmaxf(m, sc[i]);
       }
