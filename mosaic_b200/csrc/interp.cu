@@ -205,6 +205,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -294,7 +295,11 @@ __global__ void __launch_bounds__(kTileThreads) interp_tiled_kernel(
   }
   const int H = dim >> 6, n_chunks = H >> 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rb = warp >> 1, hl = warp & 1;
+  // Warp w takes the head of parity w % 2 in every chunk, for row block w / 2; a tile of
+  // at most 16 targets has one row block, and then warps 2 and 3 take the next chunk
+  // instead (two chunks per step, both buffers in use).
+  const bool pair = T <= 16 && n_chunks > 1;
+  const int rb = pair ? 0 : warp >> 1, hl = warp & 1, cw_off = pair ? warp >> 1 : 0;
   const TiledSmem L = tiled_layout(U, H);
   uint8_t* const v_s0 = smem + L.v0;  // chunk c lives in v_s0 + (c & 1) * v_step
   const size_t v_step = L.v1 - L.v0;
@@ -372,11 +377,15 @@ __global__ void __launch_bounds__(kTileThreads) interp_tiled_kernel(
   // mma lanes: ldmatrix row addresses
   const uint32_t a_addr = smem_u32(p_w) + (((lane >> 3) & 1) * 8 + (lane & 7)) * L.p_stride + (lane >> 4) * 16;
   const uint32_t b_off_s = (((lane >> 3) & 1) * 8 + (lane & 7)) * kVRow + (lane >> 4) * 16 + hl * 128;
-  for (int c = 0; c < n_chunks; ++c) {
-    cp_async_wait1();  // this thread's copies of chunk c (and of kw) have landed
-    __syncthreads();   // ... and everyone's
-    if (warp_busy) {
-      const int h = 2 * c + hl;
+  for (int c = 0; c < n_chunks; c += pair ? 2 : 1) {
+    if (pair)
+      cp_async_wait0();  // both chunks of this step (and kw) have landed for this thread
+    else
+      cp_async_wait1();  // this thread's copies of chunk c (and of kw) have landed
+    __syncthreads();     // ... and everyone's
+    const int cw = c + cw_off;  // this warp's chunk
+    if (warp_busy && cw < n_chunks) {
+      const int h = 2 * cw + hl;
       // ---- scores and softmax of the block's 16 targets for head h, into P_s
       float sc[16];
       float m = -INFINITY;
@@ -404,7 +413,7 @@ __global__ void __launch_bounds__(kTileThreads) interp_tiled_kernel(
       float acc[8][4];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-      const uint32_t bb = smem_u32(v_s0 + (c & 1) * v_step) + b_off_s;
+      const uint32_t bb = smem_u32(v_s0 + (cw & 1) * v_step) + b_off_s;
       for (uint32_t km = kmask; km != 0; km &= km - 1) {
         const int ks = __ffs(km) - 1;
         uint32_t a0, a1, a2, a3;
@@ -424,9 +433,13 @@ __global__ void __launch_bounds__(kTileThreads) interp_tiled_kernel(
       store_quad_rows(acc, 2, orow1, h, lane);
       __syncwarp();  // the next head rewrites the same P_s positions
     }
-    __syncthreads();  // chunk c's buffer is free: refill it with chunk c + 2
+    __syncthreads();  // the step's buffers are free: refill them with the chunks two ahead
     if (c + 2 < n_chunks) stage_v_chunk(v_s0 + (c & 1) * v_step, pts_s, kv, U, row_elems, b_off, c + 2);
-    cp_async_commit();  // one group per iteration (possibly empty) keeps wait_group 1 exact
+    cp_async_commit();  // one group per chunk (possibly empty) keeps wait_group 1 exact
+    if (pair) {
+      if (c + 3 < n_chunks) stage_v_chunk(v_s0 + v_step, pts_s, kv, U, row_elems, b_off, c + 3);
+      cp_async_commit();
+    }
   }
 }
 
