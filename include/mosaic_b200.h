@@ -200,7 +200,7 @@ MOSAIC_API int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out
  * accumulation), row_scale optional (NULL = 1): a Linear layer without bias on the
  * tensor core. Serves CrossAttentionInterpolate's to_kv (primitives.py:275, with the
  * row factor of its RMSNorm, primitives.py:273, as row_scale) and to_o (:283).
- * in_features a multiple of 64, out_features a multiple of 8. */
+ * in_features a multiple of 64, out_features a multiple of 32. */
 MOSAIC_API int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
                              int in_features, int out_features, void* stream);
 

@@ -471,7 +471,8 @@ int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* stat
 int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
                   int in_features, int out_features, void* stream) {
   if (rows < 0 || in_features <= 0 || out_features <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
-  if (in_features % 64 != 0 || out_features % 8 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  // the epilogue writes whole 32-column chunks of a row
+  if (in_features % 64 != 0 || out_features % 32 != 0) return MOSAIC_ERR_UNSUPPORTED;
   if (rows == 0) return MOSAIC_OK;
   if (!a || !w || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(a) || !aligned16(w) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;

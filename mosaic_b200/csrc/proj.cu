@@ -83,7 +83,12 @@ struct ProjSmem {
   int abort_flag;
 };
 
-constexpr size_t kProjSmemBytes = 1024 + kPStages * kPStageBytes + sizeof(ProjSmem);
+// Per epilogue warp, a 32-row x 64-byte staging area for the bf16 chunk it stores
+// (80-byte row pitch: the row-per-lane writes and the 4-lanes-per-row reads are
+// bank-conflict-free or nearly so).
+constexpr int kStagePitch = 80;
+constexpr size_t kStageBytes = 8 * 32 * kStagePitch;
+constexpr size_t kProjSmemBytes = 1024 + kPStages * kPStageBytes + ((sizeof(ProjSmem) + 15) / 16) * 16 + kStageBytes;
 
 __device__ __forceinline__ bool wait_noabort_p(uint64_t* bar, uint32_t parity, int* status) {
   int dummy = 0;
@@ -92,38 +97,35 @@ __device__ __forceinline__ bool wait_noabort_p(uint64_t* bar, uint32_t parity, i
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// 32 consecutive output columns of one row (fp32 accumulators) -> bf16, with RoPE when
-// cos / sin are given (pair i of the chunk uses frequency p0 + i). The reference rounds
-// the Linear output to bf16 first, then rotates in fp32: out[2i] = x[2i] cos - x[2i+1]
-// sin and out[2i+1] = x[2i+1] cos + x[2i] sin, each product and the sum rounded.
-// `rs` scales every accumulator first (kLinear's row factor; 1 otherwise).
-__device__ __forceinline__ void store_chunk(uint4* dst, const uint32_t (&acc)[32], const float* cos_row,
-                                            const float* sin_row, int p0, float rs = 1.0f) {
-  uint32_t packed[16];
-  float cs[16], sn[16];
-  if (cos_row != nullptr) {
+// 32 consecutive output columns of one row (fp32 accumulators) -> packed bf16 words,
+// each scaled by `rs` first (kLinear's row factor; 1 otherwise).
+__device__ __forceinline__ void pack_chunk(uint32_t (&packed)[16], const uint32_t (&acc)[32], float rs = 1.0f) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {  // 16 frequencies: four 16-byte loads of each table row
-      const float4 c = __ldg(reinterpret_cast<const float4*>(cos_row + p0) + i);
-      const float4 s = __ldg(reinterpret_cast<const float4*>(sin_row + p0) + i);
-      cs[4 * i] = c.x; cs[4 * i + 1] = c.y; cs[4 * i + 2] = c.z; cs[4 * i + 3] = c.w;
-      sn[4 * i] = s.x; sn[4 * i + 1] = s.y; sn[4 * i + 2] = s.z; sn[4 * i + 3] = s.w;
-    }
+  for (int i = 0; i < 16; ++i)
+    packed[i] = pack_bf16x2(bf16_round(__uint_as_float(acc[2 * i]) * rs),
+                            bf16_round(__uint_as_float(acc[2 * i + 1]) * rs));
+}
+
+// Stores a warp's 32 rows x 32 bf16 columns (row = lane, `packed` its 16 words, `dst`
+// its destination or null) through the warp's staging area, so that each store
+// instruction writes 64 contiguous bytes of each of 8 rows instead of 16 bytes of each
+// of 32 rows. Every lane of the warp must call it.
+__device__ __forceinline__ void warp_store_rows(uint8_t* stage, const uint32_t (&packed)[16], __nv_bfloat16* dst,
+                                                int lane) {
+  uint4* mine = reinterpret_cast<uint4*>(stage + lane * kStagePitch);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mine[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+  __syncwarp();
+  const int q = lane & 3;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2);
+    const unsigned long long d =
+        __shfl_sync(0xffffffffu, static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(dst)), r);
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * kStagePitch + q * 16);
+    if (d != 0ull) reinterpret_cast<uint4*>(static_cast<uintptr_t>(d))[q] = v;
   }
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    float x0 = bf16_round(__uint_as_float(acc[2 * i]) * rs), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]) * rs);
-    if (cos_row != nullptr) {
-      const float o0 = __fadd_rn(__fmul_rn(x0, cs[i]), __fmul_rn(-x1, sn[i]));
-      const float o1 = __fadd_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x0, sn[i]));
-      x0 = o0;
-      x1 = o1;
-    }
-    packed[i] = pack_bf16x2(x0, x1);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+  __syncwarp();  // the stage is rewritten by the next chunk
 }
 
 // The bias (and shortcut) words of 32 output columns, loaded before the accumulators
@@ -140,12 +142,11 @@ __device__ __forceinline__ void load_chunk_res(uint32_t (&pw)[16], uint32_t (&sw
 }
 
 // 32 output columns of one row for kDown / kUp: y = bf16(bf16(acc) + pos) (+ shortcut,
-// rounded again), stored as bf16; returns the sum of y^2 (fp32) for the row's RMSNorm.
-__device__ __forceinline__ float store_chunk_res(uint4* dst, const uint32_t (&acc)[32], const uint32_t (&pw)[16],
-                                                 const uint32_t (&sw)[16], bool has_sc) {
+// rounded again) packed as bf16; returns the sum of y^2 (fp32) for the row's RMSNorm.
+__device__ __forceinline__ float pack_chunk_res(uint32_t (&packed)[16], const uint32_t (&acc)[32],
+                                                const uint32_t (&pw)[16], const uint32_t (&sw)[16], bool has_sc) {
   const bool sc = has_sc;
   float ss = 0.f;
-  uint32_t packed[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
@@ -158,9 +159,6 @@ __device__ __forceinline__ float store_chunk_res(uint4* dst, const uint32_t (&ac
     ss = fmaf(x0, x0, fmaf(x1, x1, ss));
     packed[i] = pack_bf16x2(x0, x1);
   }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
   return ss;
 }
 
@@ -194,12 +192,44 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(__nv_bfloat16* __restric
   }
 }
 
+// 16 RoPE frequencies p0 .. p0 + 15 of one table row (four 16-byte loads of each table).
+__device__ __forceinline__ void load_rope16(float (&cs)[16], float (&sn)[16], const float* cos_row,
+                                            const float* sin_row, int p0) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 c = __ldg(reinterpret_cast<const float4*>(cos_row + p0) + i);
+    const float4 t = __ldg(reinterpret_cast<const float4*>(sin_row + p0) + i);
+    cs[4 * i] = c.x; cs[4 * i + 1] = c.y; cs[4 * i + 2] = c.z; cs[4 * i + 3] = c.w;
+    sn[4 * i] = t.x; sn[4 * i + 1] = t.y; sn[4 * i + 2] = t.z; sn[4 * i + 3] = t.w;
+  }
+}
+
+// 32 output columns of one row -> packed bf16, rotated by RoPE with the chunk's table
+// values already in registers (rot). The reference rounds the Linear output to bf16
+// first, then rotates in fp32: out[2i] = x[2i] cos - x[2i+1] sin and out[2i+1] =
+// x[2i+1] cos + x[2i] sin, each product and the sum rounded.
+__device__ __forceinline__ void pack_chunk_tab(uint32_t (&packed)[16], const uint32_t (&acc)[32],
+                                               const float (&cs)[16], const float (&sn)[16], bool rot) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
+    if (rot) {
+      const float o0 = __fadd_rn(__fmul_rn(x0, cs[i]), __fmul_rn(-x1, sn[i]));
+      const float o1 = __fadd_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x0, sn[i]));
+      x0 = o0;
+      x1 = o1;
+    }
+    packed[i] = pack_bf16x2(x0, x1);
+  }
+}
+
 // One instantiation per mode, so that each epilogue gets its own register allocation.
 template <int kMode>
 __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constant__ ProjParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   ProjSmem& sm = *reinterpret_cast<ProjSmem*>(tiles + kPStages * kPStageBytes);
+  uint8_t* stage_all = tiles + kPStages * kPStageBytes + ((sizeof(ProjSmem) + 15) / 16) * 16;
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -293,6 +323,7 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
     // ---------------------------------------------------------------- epilogue, one output row per thread
     const int half = (warp - 4) >> 2;  // warpgroup: columns [128 half, 128 half + 128) of each tile
     const int row = (warp & 3) * 32 + lane;
+    uint8_t* stage = stage_all + (warp - 4) * 32 * kStagePitch;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int qcols = p.Hq * 64, kcols = p.Hk * 64;
     const int gbase = qcols + 2 * kcols;  // first gate-logit column (kQkv)
@@ -336,9 +367,10 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           tmem_ld32(tacc + 32 * (4 * half + k), acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
-          if (live)
-            ss_part += store_chunk_res(reinterpret_cast<uint4*>(p.out + o0 + 32 * k), acc, pw[k & 1], sw[k & 1],
-                                       sc0 != nullptr);
+          uint32_t packed[16];
+          const float ss = pack_chunk_res(packed, acc, pw[k & 1], sw[k & 1], sc0 != nullptr);
+          if (live) ss_part += ss;
+          warp_store_rows(stage, packed, live ? p.out + o0 + 32 * k : nullptr, lane);
         }
         if (live && nch > 0) atomicAdd(p.ss + orow, ss_part);
         tc_fence_before();
@@ -350,30 +382,39 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
         break;
       }
       tc_fence_after();
+      // kQkv visits the warpgroup's chunks in the order 0, 2, 1, 3: chunks 0 and 2 rotate
+      // with RoPE frequencies 0-15 and chunks 1 and 3 with 16-31 (d0 = 0 or 32 of a head),
+      // so each half of the row's table is loaded once per tile instead of twice.
+      float cs[16], sn[16];
+      int tab_p0 = -1;
 #pragma unroll 1
-      for (int ci = 4 * half; ci < 4 * half + 4; ++ci) {
+      for (int k = 0; k < 4; ++k) {
+        const int ci = 4 * half + (kMode == kQkv ? (k & 1) * 2 + (k >> 1) : k);
         const int c0 = nt * kPBN + 32 * ci;  // warp-uniform
-        if (c0 >= p.N) break;
+        if (c0 >= p.N) {
+          if (kMode == kQkv) continue;
+          break;
+        }
+        if (kMode == kQkv && c0 == gbase + 32) continue;  // second gate chunk: taken with the first
         uint32_t acc[32];
         if (kMode == kPlain) {
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
-          if (live) {
-            // A rows are (b, s) (attention output), out rows (s, b)
-            const int b = m / p.S, s = m % p.S;
-            store_chunk(reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(s) * p.B + b) * p.N + c0), acc,
-                        nullptr, nullptr, 0);
-          }
+          // A rows are (b, s) (attention output), out rows (s, b)
+          const int b = m / p.S, s = m % p.S;
+          uint32_t packed[16];
+          pack_chunk(packed, acc);
+          warp_store_rows(stage, packed, live ? p.out + (static_cast<size_t>(s) * p.B + b) * p.N + c0 : nullptr, lane);
           continue;
         }
         if (kMode == kLinear) {
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
-          if (live)
-            store_chunk(reinterpret_cast<uint4*>(p.out + static_cast<size_t>(m) * p.N + c0), acc, nullptr, nullptr,
-                        0, p.rscale != nullptr ? __ldg(p.rscale + m) : 1.0f);
+          uint32_t packed[16];
+          pack_chunk(packed, acc, live && p.rscale != nullptr ? __ldg(p.rscale + m) : 1.0f);
+          warp_store_rows(stage, packed, live ? p.out + static_cast<size_t>(m) * p.N + c0 : nullptr, lane);
           continue;
         }
         const int s = m / p.B, b = m % p.B;  // x rows are (s, b)
@@ -381,30 +422,29 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
-          if (!live) continue;
           __nv_bfloat16* dst;
-          const float* cr = nullptr;
-          const float* sr = nullptr;
+          bool rot = false;
           int d0;
           if (c0 < qcols) {
             d0 = c0 % 64;
             dst = p.q + ((static_cast<size_t>(b) * p.S + s) * p.Hq + c0 / 64) * 64 + d0;
-            if (p.rope_cos) {
-              cr = p.rope_cos + static_cast<size_t>(s) * 32;
-              sr = p.rope_sin + static_cast<size_t>(s) * 32;
-            }
+            rot = p.rope_cos != nullptr;
           } else if (c0 < qcols + kcols) {
             d0 = (c0 - qcols) % 64;
             dst = p.k + ((static_cast<size_t>(b) * p.S + s) * p.Hk + (c0 - qcols) / 64) * 64 + d0;
-            if (p.rope_cos) {
-              cr = p.rope_cos + static_cast<size_t>(s) * 32;
-              sr = p.rope_sin + static_cast<size_t>(s) * 32;
-            }
+            rot = p.rope_cos != nullptr;
           } else {
             d0 = (c0 - qcols - kcols) % 64;
             dst = p.v + ((static_cast<size_t>(b) * p.S + s) * p.Hk + (c0 - qcols - kcols) / 64) * 64 + d0;
           }
-          store_chunk(reinterpret_cast<uint4*>(dst), acc, cr, sr, d0 / 2);
+          if (rot && live && tab_p0 != d0 / 2) {
+            load_rope16(cs, sn, p.rope_cos + static_cast<size_t>(s) * 32, p.rope_sin + static_cast<size_t>(s) * 32,
+                        d0 / 2);
+            tab_p0 = d0 / 2;
+          }
+          uint32_t packed[16];
+          pack_chunk_tab(packed, acc, cs, sn, rot && live);
+          warp_store_rows(stage, packed, live ? dst : nullptr, lane);
         } else if (c0 == gbase) {
           // The 3 Hq gate logits (at most 64 columns, starting 64-aligned, so inside this
           // tile): logits are bf16 Linear outputs laid out (head, strategy); softmax over
@@ -435,7 +475,6 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
               p.g[2 * plane + o] = __float2bfloat16_rn(e2 / sum);
             }
           }
-          ++ci;  // the second chunk was consumed with the first
         }
       }
       tc_fence_before();

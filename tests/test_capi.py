@@ -252,6 +252,8 @@ def test_interp_attend_rejects_bad_arguments(kw, code):
 def test_linear_and_rms_reject_bad_arguments():
     lib = _lib.load()
     assert lib.mosaic_linear(FAKE, FAKE, FAKE, None, None, 100, 100, 64, None) == _lib.MOSAIC_ERR_UNSUPPORTED
+    # widths that end inside a 32-column chunk: the epilogue stores whole chunks
+    assert lib.mosaic_linear(FAKE, FAKE, FAKE, None, None, 100, 128, 40, None) == _lib.MOSAIC_ERR_UNSUPPORTED
     assert lib.mosaic_linear(None, FAKE, FAKE, None, None, 100, 128, 64, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
     assert lib.mosaic_linear(FAKE, FAKE, FAKE, None, None, 0, 128, 64, None) == _lib.MOSAIC_OK
     assert lib.mosaic_row_rms(FAKE, FAKE, 10, 100, 1e-6, None) == _lib.MOSAIC_ERR_UNSUPPORTED
