@@ -78,17 +78,6 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2D tiled bulk tensor load global -> shared, completion counted on `bar` in bytes.
-// x is the innermost (element) coordinate, y the row coordinate. Callers keep x a
-// multiple of 64 bf16 elements (128 bytes), so the 16-byte rule always holds.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
@@ -251,6 +240,9 @@ __device__ __forceinline__ void tc_commit_elect(uint64_t* bar) {
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
       : "memory");
 }
+// 2D tiled bulk tensor load global -> shared by one elected lane, completion counted on
+// `bar` in bytes. x is the innermost (element) coordinate, y the row coordinate. Callers
+// keep x a multiple of 64 bf16 elements (128 bytes), so the 16-byte rule always holds.
 __device__ __forceinline__ void tma_load_2d_elect(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
