@@ -34,11 +34,20 @@ directions at the model's sizes, likewise beside its eager sequence (--no-interp
 `updown`: HEALPixDownsample 64 -> 32 and HEALPixUpsample 32 -> 64 at the U-Net's first
 stage dims, beside their eager sequences (--no-updown).
 
+For S1 the line also carries `ensemble`: one 24-member ensemble step of the U-Net's
+attention work sharded by member over the ranks (the 14 mosaic_attn_func calls of a step
+per member at the reference presets, then an NCCL all-gather of per-member output
+fields), as step/s with the gather's share (--no-ensemble skips it); and, on one GPU,
+`reference_gpu`: the reference's own GPU code from baseline/_ref (its Triton
+selected-block kernel, its flash-attn local branch, its whole mosaic_attn_func) timed
+on the same inputs beside ours, with the output differences (--no-reference-gpu).
+
 `--impl reference` times the reference algorithm on the host cores instead: the
-reference is a CUDA-only Python project (Triton + flash-attn), so its CPU form is
-the oracle port (oracle/bsa_oracle.py), run on a bounded sample of the same
-workload (all of the global compression/top-k, local + selected branches for 4
-of the 48 windows per step).
+reference's CPU form is the oracle port (oracle/bsa_oracle.py; the reference itself
+needs CUDA for flash-attn and Triton), run on a bounded sample of the same workload
+per step: the sequence-global part (pooling, coarse attention, top-k over all tokens)
+once and the local + selected branches of 4 of the 48 windows; the full call is
+extrapolated as t_global + t_windows x 48 / 4.
 """
 import argparse
 import ctypes
@@ -97,6 +106,8 @@ def parse():
     p.add_argument("--no-block", action="store_true")
     p.add_argument("--no-interp", action="store_true")
     p.add_argument("--no-updown", action="store_true")
+    p.add_argument("--no-ensemble", action="store_true")
+    p.add_argument("--no-reference-gpu", action="store_true")
     return p.parse_args()
 
 
@@ -460,21 +471,39 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- CPU legs
 def cpu_sample(c, windows, reps, warm=1):
-    """Times oracle.mosaic_attn_func_sample on the host cores; returns (tokens/s, cores, seconds)."""
+    """Times the oracle port of mosaic_attn_func on the host cores over a bounded sample:
+    per rep, the sequence-global part once (pooling, coarse attention, top-k over all
+    tokens: oracle.mosaic_attn_global) and the local + selected branches of the sampled
+    windows (oracle.mosaic_attn_window). The full call is extrapolated as
+    t_full = t_global + t_windows * (windows in the sequence / windows sampled), and the
+    rate is B * N / t_full. Returns (tokens/s, cores, seconds spent, t_full seconds)."""
     from oracle import bsa_oracle as O
 
     torch.set_num_threads(os.cpu_count() or 1)
     x = O.make_inputs(c["B"], c["N"], c["Hq"], c["Hk"], seed=0, rope=False)
-    args = (x["q"], x["k"], x["v"], x["w"], c["bas"], c["bs"], c["K"])
-    for _ in range(warm):
-        O.mosaic_attn_func_sample(*args, windows=windows)
-    times = []
-    for _ in range(reps):
+    q, k, v, w = x["q"], x["k"], x["v"], x["w"]
+
+    def one():
         t0 = time.perf_counter()
-        O.mosaic_attn_func_sample(*args, windows=windows)
-        times.append(time.perf_counter() - t0)
-    tok = c["B"] * len(windows) * c["bas"]
-    return tok * reps / sum(times), torch.get_num_threads(), sum(times)
+        o_cmp, idx = O.mosaic_attn_global(q, k, v, c["bs"], c["K"])
+        t1 = time.perf_counter()
+        for win in windows:
+            O.mosaic_attn_window(q, k, v, w, c["bas"], c["bs"], win, o_cmp, idx)
+        return t1 - t0, time.perf_counter() - t1
+
+    for _ in range(warm):
+        one()
+    tg, tw = zip(*[one() for _ in range(reps)])
+    nw = c["N"] // c["bas"]
+    t_full = statistics.mean(tg) + statistics.mean(tw) * nw / len(windows)
+    return c["B"] * c["N"] / t_full, torch.get_num_threads(), sum(tg) + sum(tw), t_full
+
+
+def cpu_sample_text(name, c, windows, reps, warm):
+    return (f"oracle port (fp32 torch) of mosaic_attn_func on {name} inputs: per step the global part (pooling, "
+            f"coarse attention, top-k over all {c['N']} tokens) once and the local + selected branches of "
+            f"{len(windows)} of the {c['N'] // c['bas']} windows; full call = t_global + t_windows x "
+            f"{c['N'] // c['bas']}/{len(windows)}, value = B*N / full call; {reps} timed step(s) after {warm} warm-up")
 
 
 def sample_windows(c, count):
@@ -491,17 +520,15 @@ def reference_arm(args):
     name = args.workload
     c = WORKLOADS[name]
     windows = sample_windows(c, 4)
-    value, cores, secs = cpu_sample(c, windows, reps=args.steps, warm=args.warmup)
-    sample = (f"per step: oracle port (fp32 torch) of mosaic_attn_func on {name} inputs, global pooling/coarse "
-              f"attention/top-k over all {c['N']} tokens, local + selected branches for {len(windows)} of "
-              f"{c['N'] // c['bas']} windows ({len(windows) * c['bas']} query tokens); {args.steps} steps after "
-              f"{args.warmup} warm-up")
+    value, cores, secs, t_full = cpu_sample(c, windows, reps=args.steps, warm=args.warmup)
+    sample = cpu_sample_text(name, c, windows, args.steps, args.warmup)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": describe(name, c) + " (CPU sample)", "B": c["B"], "N": c["N"]},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                         "full_call_ms_extrapolated": 1000 * t_full},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -599,6 +626,164 @@ def dense_sdpa(x, c, reps=3):
         except RuntimeError as e:  # backend not available for this shape: try the next one
             err = str(e).splitlines()[0][:120]
     return {"backend": None, "error": err}
+
+
+def _timed(fn, stream, reps, warmup):
+    """Mean device milliseconds of fn() over `reps` calls (CUDA events on `stream`)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def reference_gpu_leg(c, x, stream, reps, warmup):
+    """The reference's own GPU code on the same B200 and inputs (baseline/reference.py):
+    its Triton selected-block kernel (ops.mosaic_attn_fwd_kernel, every autotuner config
+    valid for the block size, best one reported) against the selected-only mode of
+    kernel (c) on the same block indices; its local branch (primitives.block_attention
+    = flash_attn_func) against mosaic_block_attn_fwd; and its whole
+    primitives.mosaic_attn_func against ours. Outputs are compared too."""
+    from baseline import reference as R
+
+    if not R.available():
+        return {"unavailable": "baseline/_ref is empty (the reference checkout was absent when build() ran)"}
+    import mosaic_b200 as M
+    from mosaic_b200 import ops as mops
+
+    ref = R.load(x["q"].device)
+    B, N, Hq, D, bs, K, bas = (c[k] for k in ("B", "N", "Hq", "D", "bs", "K", "bas"))
+    q, k, v = x["q"], x["k"], x["v"]
+    w5 = x["w"].unsqueeze(-1)
+    scale = D ** -0.5
+    qc, kc, _ = M.block_pool(q, k, v, bs)
+    idx = M.attn_topk(qc, kc, K)
+    res = {"what": "reference GPU code (Triton kernel, flash-attn / torch ops) on the same B200 and inputs",
+           "notes": ref.notes}
+    cfg_ms = {}
+    for cfg in ref.configs(bs):
+        cfg_ms[json.dumps(cfg)] = _timed(lambda: ref.sparse_attn_fwd(q, k, v, idx, bs, scale, cfg), stream, reps,
+                                         warmup)
+    best = min(cfg_ms, key=cfg_ms.get)
+    ref.config = json.loads(best)
+    ours_sel = _timed(lambda: mops.mosaic_attn_fwd(q, k, v, idx, bs, scale), stream, reps, warmup)
+    r_out, r_lse = ref.sparse_attn_fwd(q, k, v, idx, bs, scale)
+    o_out, o_lse = mops.mosaic_attn_fwd(q, k, v, idx, bs, scale)
+    d = (r_out.float() - o_out.float()).abs()
+    flop_sel = 4 * B * N * Hq * D * K * bs
+    res["selected"] = {
+        "reference_triton_us": 1000 * cfg_ms[best], "reference_triton_config": ref.config,
+        "reference_triton_us_by_config": {k_: 1000 * v_ for k_, v_ in cfg_ms.items()},
+        "ours_us": 1000 * ours_sel, "speedup": cfg_ms[best] / ours_sel,
+        "reference_triton_tflops": flop_sel / (cfg_ms[best] / 1000) / 1e12,
+        "ours_tflops": flop_sel / (ours_sel / 1000) / 1e12,
+        "max_abs_diff": float(d.max()), "mean_abs_diff": float(d.mean()),
+        "lse_max_abs_diff": float((r_lse - o_lse).abs().max())}
+    ref_loc = _timed(lambda: ref.primitives.block_attention(q, k, v, bas), stream, reps, warmup)
+    ours_loc = _timed(lambda: M.block_attention(q, k, v, bas), stream, reps, warmup)
+    d = (ref.primitives.block_attention(q, k, v, bas).float() - M.block_attention(q, k, v, bas).float()).abs()
+    res["local"] = {"reference_us": 1000 * ref_loc, "ours_us": 1000 * ours_loc, "speedup": ref_loc / ours_loc,
+                    "max_abs_diff": float(d.max()), "mean_abs_diff": float(d.mean())}
+    ref_full = _timed(lambda: ref.primitives.mosaic_attn_func(q, k, v, w5, bas, bs, K, False), stream, reps, warmup)
+    ours_full = _timed(lambda: M.mosaic_attn_func(q, k, v, w5, bas, bs, K, False), stream, reps, warmup)
+    r_full = ref.primitives.mosaic_attn_func(q, k, v, w5, bas, bs, K, False).float()
+    o_full, o_idx = M.mosaic_attn_func(q, k, v, w5, bas, bs, K, False, return_block_indices=True)
+    d = (r_full - o_full.float()).abs()
+    r_idx = ref.primitives.attn_topk(qc, kc, K)
+    same_sel = (torch.sort(r_idx, -1).values == torch.sort(o_idx, -1).values).all(-1).float().mean()
+    res["mosaic_attn_func"] = {"reference_ms": ref_full, "ours_ms": ours_full, "speedup": ref_full / ours_full,
+                               "max_abs_diff": float(d.max()), "mean_abs_diff": float(d.mean()),
+                               "rows_with_same_selection": float(same_sel)}
+    res["reps"] = reps
+    return res
+
+
+# One step of the Mosaic U-Net calls the block-sparse attention 14 times per member, with
+# the reference presets (inference.py:71-88: 128-token blocks, window 1024, GQA 4): stage 1
+# (nside 64, 12 heads, top-k 24) and stage 2 (nside 32, 16 heads, top-k 12) with 4 encoder
+# + 2 decoder blocks each, the bottleneck (nside 16, 20 heads, top-k 4) with 2 blocks.
+UNET_ATTENTION = [  # (label, nside, q heads, top-k, calls), in the order of one step
+    ("enc1", 64, 12, 24, 4), ("enc2", 32, 16, 12, 4), ("bottleneck", 16, 20, 4, 2),
+    ("dec2", 32, 16, 12, 2), ("dec1", 64, 12, 24, 2)]
+FIELD_NUMEL = 240 * 121 * 82  # the model's output field per member (lat-lon grid x channels)
+
+
+def ensemble_leg(dev, rank, world, dist, stream, steps, warmup):
+    """One 24-member ensemble step of the attention work, sharded by member: this rank
+    runs the 14 block-sparse attention calls of one U-Net step (UNET_ATTENTION) for its
+    members (ensemble.member_range, batched along the attention batch as mosaic.py:308
+    batches them), then `ensemble.gather_members` all-gathers the per-member output
+    fields (NCCL all_gather_into_tensor; 240 x 121 x 82 fp32 per member, the model's
+    output size, taken from the last attention output) to every rank. Step time =
+    max over ranks of the device time of the whole step, gather included."""
+    import mosaic_b200 as M
+    from mosaic_b200 import ensemble as E
+
+    lo, hi = E.member_range(MEMBERS, rank, world)
+    m = hi - lo
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    stages = {}
+    for label, nside, Hq, K, calls in UNET_ATTENTION:
+        if nside in stages:
+            continue
+        N, Hk = 12 * nside * nside, Hq // 4
+        stages[nside] = dict(
+            q=torch.randn(m, N, Hq, 64, generator=g, device=dev).bfloat16(),
+            k=torch.randn(m, N, Hk, 64, generator=g, device=dev).bfloat16(),
+            v=torch.randn(m, N, Hk, 64, generator=g, device=dev).bfloat16(),
+            w=torch.sigmoid(torch.randn(3, m, N, Hq, 1, generator=g, device=dev)).bfloat16())
+    field = torch.empty(m, FIELD_NUMEL, dtype=torch.float32, device=dev)
+
+    def step(ev=None):
+        out = None
+        for label, nside, Hq, K, calls in UNET_ATTENTION:
+            s = stages[nside]
+            for _ in range(calls):
+                out = M.mosaic_attn_func(s["q"], s["k"], s["v"], s["w"], 1024, 128, K, False)
+        field.copy_(out.reshape(m, -1)[:, :FIELD_NUMEL])
+        if ev:
+            ev[0].record(stream)
+        full = E.gather_members(field, MEMBERS) if dist is not None else field
+        if ev:
+            ev[1].record(stream)
+        return full
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        full = step(evs[i])
+    b.record(stream)
+    torch.cuda.synchronize()
+    step_ms = a.elapsed_time(b) / steps
+    gather_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+    if dist is not None:
+        t = torch.tensor([step_ms, gather_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, gather_ms = (float(x_) for x_ in t.tolist())
+        dist.barrier()
+    assert full.shape[0] == MEMBERS
+    flop = sum(calls * 4 * (12 * ns * ns) * Hq * 64 * (K * 128 + 1024) for _, ns, Hq, K, calls in UNET_ATTENTION)
+    return {"what": "one 24-member step of the U-Net's attention work: 14 mosaic_attn_func calls per member "
+                    "(reference presets: 6 at nside 64 / 12 heads / top-k 24, 6 at nside 32 / 16 heads / top-k 12, "
+                    "2 at nside 16 / 20 heads / top-k 4; blocks 128, window 1024), members batched per rank, then "
+                    "an all-gather of 240x121x82 fp32 output fields per member (taken from the last attention "
+                    "output); synthetic inputs; device time, max over ranks",
+            "members": MEMBERS, "members_per_rank": m, "steps": steps, "step_ms": step_ms,
+            "step_per_s": 1000.0 / step_ms, "gather_ms": gather_ms, "gather_share": gather_ms / step_ms,
+            "gathered_bytes_per_rank": MEMBERS * FIELD_NUMEL * 4,
+            "attention_flop_per_member": flop,
+            "attention_tflops_per_gpu": flop * m / ((step_ms - gather_ms) / 1000) / 1e12}
 
 
 def b200_arm(args):
@@ -704,10 +889,21 @@ def b200_arm(args):
             t = torch.tensor([e_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
+        pcie = (h2d + d2h) * n_e2e / (e_ms / 1000.0) / 1e9
         e2e = {"value": world * B * N * n_e2e / (e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": n_e2e,
-               "path": "mosaic_b200.streaming.StreamedAttention -> mosaic_attn_func, pinned host inputs/outputs"}
+               "path": "mosaic_b200.streaming.StreamedAttention -> mosaic_attn_func, pinned host inputs/outputs",
+               "host_copy_gbs_per_rank": pcie, "host_copy_gbs_all_ranks": pcie * world,
+               "limiter": "host<->device copies (the device step takes a fraction of the copy time); with several "
+                          "ranks all copies share the host's memory and PCIe root complex"}
         del host, out_host, pipe
+
+    ens = None
+    if not args.no_ensemble and name == "S1":
+        ens = ensemble_leg(dev, rank, world, dist, stream, steps=max(2, min(args.steps, 4)), warmup=1)
+    ref_gpu = None
+    if not args.no_reference_gpu and rank == 0 and world == 1 and name in ("S1", "S1_bs128"):
+        ref_gpu = reference_gpu_leg(c, sets[0], stream, reps=max(3, min(args.steps, 20)), warmup=2)
 
     sdpa = None
     if name.startswith("X") and rank == 0:
@@ -719,12 +915,10 @@ def b200_arm(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         windows = sample_windows(c, 8)
         reps = 3 if N <= 49152 else 1
-        v_cpu, cores, secs = cpu_sample(c, windows, reps=reps)
+        v_cpu, cores, secs, t_full = cpu_sample(c, windows, reps=reps)
         cpu = {"value": v_cpu, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"oracle port (fp32 torch) of mosaic_attn_func on {name}: global pooling/coarse "
-                         f"attention/top-k over all tokens, local + selected branches for {len(windows)} of "
-                         f"{N // c['bas']} windows ({len(windows) * c['bas']} query tokens), {reps} timed rep(s) "
-                         f"after 1 warm-up, {secs:.1f} s"}
+               "sample": cpu_sample_text(name, c, windows, reps, 1) + f", {secs:.1f} s of CPU work",
+               "full_call_ms_extrapolated": 1000 * t_full}
 
     hbm, tf, src = peaks()
     bwd = None
@@ -761,7 +955,7 @@ def b200_arm(args):
                    "B_per_gpu": B, "N": N, "Hq": Hq, "Hk": Hk, "head_dim": D, "sparse_block": c["bs"],
                    "topk": c["K"], "window": c["bas"], "parallelism": f"members x{world}",
                    "l2": f"{nsets} rotating input sets of {set_bytes / 1e6:.0f} MB (L2 126 MB)"},
-        "ensemble_step_per_s": value / (MEMBERS * N),
+        "value_per_gpu": value / world,
         "roofline": {"bound": "tensor", "kernel": "bsa_engine_kernel (c: local + selected + gated combine)",
                      "achieved": achieved, "peak": tf, "unit": "TFLOP/s", "frac": achieved / tf,
                      "peak_source": src + " bf16_tflops (burst)", "traffic": ATTEND_TRAFFIC_BYTES.get(name),
@@ -776,6 +970,10 @@ def b200_arm(args):
         "e2e": e2e,
         "cpu_baseline": cpu,
     }
+    if ens is not None:
+        line["ensemble"] = ens
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
     if sdpa is not None:
         line["dense_sdpa"] = sdpa
     if bwd is not None:

@@ -160,33 +160,44 @@ def sparse_attention(q, k, v, block_indices, block_size, softmax_scale=None, ret
     `qblocks=(lo, hi)` restricts the work to query blocks lo..hi-1 (other rows are
     left uninitialised); the CPU timing sample uses it."""
     B, N, Hq, D = q.shape
+    nb = N // block_size
+    out = torch.empty(B, N, Hq, D, dtype=torch.float32)
+    lse = torch.empty(B, N, Hq, dtype=torch.float32)
+    lo, hi = (0, nb) if qblocks is None else qblocks
+    n0, n1 = lo * block_size, hi * block_size
+    out[:, n0:n1], lse[:, n0:n1] = sparse_attention_rows(q, k, v, block_indices, block_size, lo, hi, softmax_scale)
+    return (out, lse) if return_lse else out
+
+
+def sparse_attention_rows(q, k, v, block_indices, block_size, lo, hi, softmax_scale=None):
+    """The rows of query blocks lo..hi-1 of `sparse_attention` (ops.py:25-134), compact:
+    (out [B, (hi-lo)*bs, Hq, D], lse [B, (hi-lo)*bs, Hq]) fp32. Works on full-size
+    inputs without allocating an output of the whole sequence."""
+    B, N, Hq, D = q.shape
     Hk = k.shape[2]
     G = Hq // Hk
     K = block_indices.shape[-1]
     scale = D ** -0.5 if softmax_scale is None else softmax_scale
-    nb = N // block_size
-    out = torch.empty(B, N, Hq, D, dtype=torch.float32)
-    lse = torch.empty(B, N, Hq, dtype=torch.float32)
-    qf, kf, vf = q.float(), k.float(), v.float()
-    ar = torch.arange(block_size)
-    lo, hi = (0, nb) if qblocks is None else qblocks
     n0, n1 = lo * block_size, hi * block_size
+    out = torch.empty(B, n1 - n0, Hq, D, dtype=torch.float32)
+    lse = torch.empty(B, n1 - n0, Hq, dtype=torch.float32)
+    ar = torch.arange(block_size)
     for b in range(B):
         for h in range(Hk):
             sel = block_indices[b, lo:hi, h, :].long()
             rows = (sel.unsqueeze(-1) * block_size + ar).reshape(hi - lo, K * block_size)
-            ks = kf[b, :, h][rows]                                   # nblk, K*bs, D
-            vs = vf[b, :, h][rows]
+            ks = k[b, :, h][rows].float()                            # nblk, K*bs, D
+            vs = v[b, :, h][rows].float()
             for g in range(G):
                 j = h * G + g
-                qq = qf[b, n0:n1, j].reshape(hi - lo, block_size, D) * (scale * LOG2_E)
+                qq = q[b, n0:n1, j].float().reshape(hi - lo, block_size, D) * (scale * LOG2_E)
                 s2 = qq @ ks.transpose(-1, -2)                       # nblk, bs, K*bs  (log2 domain)
                 m = s2.amax(dim=-1, keepdim=True)
                 p = torch.exp2(s2 - m)
                 l = p.sum(dim=-1, keepdim=True)
-                out[b, n0:n1, j] = ((p @ vs) / l).reshape(n1 - n0, D)
-                lse[b, n0:n1, j] = (m + torch.log2(l)).reshape(n1 - n0)
-    return (out, lse) if return_lse else out
+                out[b, :, j] = ((p @ vs) / l).reshape(n1 - n0, D)
+                lse[b, :, j] = (m + torch.log2(l)).reshape(n1 - n0)
+    return out, lse
 
 
 def sparse_attention_bwd(q, k, v, block_indices, block_size, grad_out, softmax_scale=None, out=None, lse=None):
@@ -389,19 +400,29 @@ def mosaic_attn_func_sample(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_
     compression and top-k run over the whole sequence (they are global), the
     local and selected branches only for those windows. A bounded, proportional
     sample of the full forward for CPU timing. Returns [B, len(windows)*bas, Hq, D]."""
-    bas, bs, K = block_attn_size, sparse_block_size, sparse_block_count
-    w = weight_ba_cmp_slc.float()
+    o_cmp, idx = mosaic_attn_global(q, k, v, sparse_block_size, sparse_block_count)
+    return torch.cat([mosaic_attn_window(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, win,
+                                         o_cmp, idx) for win in windows], dim=1)
+
+
+def mosaic_attn_global(q, k, v, sparse_block_size, sparse_block_count):
+    """The sequence-global part of mosaic_attn_func (primitives.py:65-78, 86): pooled
+    coarse attention o_cmp [B, nb, Hq, D] (not yet repeated) and the top-k indices."""
+    bs = sparse_block_size
     q_cmp, k_cmp, v_cmp = pool_mean(q, bs), pool_mean(k, bs), pool_mean(v, bs)
-    o_cmp = dense_attention(q_cmp, k_cmp, v_cmp)
-    idx = attn_topk(q_cmp, k_cmp, K)
-    outs = []
-    for win in windows:
-        n0, n1 = win * bas, (win + 1) * bas
-        o_ba = dense_attention(q[:, n0:n1], k[:, n0:n1], v[:, n0:n1])
-        o_slc = sparse_attention(q, k, v, idx, bs, qblocks=(n0 // bs, n1 // bs))[:, n0:n1]
-        o_c = o_cmp.repeat_interleave(bs, dim=1)[:, n0:n1]
-        outs.append(o_ba * w[0, :, n0:n1] + o_c * w[1, :, n0:n1] + o_slc * w[2, :, n0:n1])
-    return torch.cat(outs, dim=1)
+    return dense_attention(q_cmp, k_cmp, v_cmp), attn_topk(q_cmp, k_cmp, sparse_block_count)
+
+
+def mosaic_attn_window(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, win, o_cmp, idx):
+    """mosaic_attn_func's output rows of local window `win` (primitives.py:31, 87-89) given
+    the global part: [B, block_attn_size, Hq, D] fp32."""
+    bas, bs = block_attn_size, sparse_block_size
+    w = weight_ba_cmp_slc.float()
+    n0, n1 = win * bas, (win + 1) * bas
+    o_ba = dense_attention(q[:, n0:n1], k[:, n0:n1], v[:, n0:n1])
+    o_slc, _ = sparse_attention_rows(q, k, v, idx, bs, n0 // bs, n1 // bs)
+    o_c = o_cmp[:, n0 // bs:n1 // bs].repeat_interleave(bs, dim=1)
+    return o_ba * w[0, :, n0:n1] + o_c * w[1, :, n0:n1] + o_slc * w[2, :, n0:n1]
 
 
 # --------------------------------------------------------------------------- checkers

@@ -248,3 +248,12 @@ def test_healpix_updown_matches_reference(name):
     diff = (flat[torch.from_numpy(d["rows"]).long()] - GU.t(d["out_rows"])).abs()
     assert diff.max() < 3e-3 and diff.mean() < 3e-4, (diff.max(), diff.mean())
     torch.testing.assert_close(out.double().sum(dim=(0, 2)), torch.from_numpy(d["out_sums"]), atol=1e-2, rtol=1e-4)
+
+
+def test_sampled_oracle_equals_full_oracle_on_its_windows():
+    """The CPU baseline's sample (global part once + chosen windows) computes exactly the
+    full oracle's rows of those windows."""
+    x = O.make_inputs(1, 3072, 4, 1, seed=0, rope=False)
+    full = O.mosaic_attn_func(x["q"], x["k"], x["v"], x["w"], 1024, 64, 8, False)
+    s = O.mosaic_attn_func_sample(x["q"], x["k"], x["v"], x["w"], 1024, 64, 8, windows=[0, 2])
+    assert torch.equal(torch.cat([full[:, :1024], full[:, 2048:]], 1), s)
