@@ -577,16 +577,17 @@ class Stages:
         null = ctypes.c_void_p(0)
         rec = (lambda i: events[i].record(stream)) if events else (lambda i: None)
         rec(0)
+        dt = 0  # MOSAIC_DTYPE_BF16
         rc = L.mosaic_block_pool(p(x["q"]), p(x["k"]), p(x["v"]), null, null, null, null, p(self.q_cmp),
-                                 p(self.k_cmp), p(self.v_cmp), B, N, Hq, Hk, D, bs, s)
+                                 p(self.k_cmp), p(self.v_cmp), B, N, Hq, Hk, D, bs, dt, s)
         rec(1)
         rc |= L.mosaic_cmp_attn_fwd(p(self.q_cmp), p(self.k_cmp), p(self.v_cmp), p(self.o_cmp), p(self.status),
-                                    B, nb, Hq, Hk, D, 0.125, s)
+                                    B, nb, Hq, Hk, D, 0.125, dt, s)
         rec(2)
-        rc |= L.mosaic_attn_topk(p(self.q_cmp), p(self.k_cmp), p(self.idx), B, nb, Hq, Hk, D, K, s)
+        rc |= L.mosaic_attn_topk(p(self.q_cmp), p(self.k_cmp), p(self.idx), B, nb, Hq, Hk, D, K, dt, s)
         rec(3)
         rc |= L.mosaic_bsa_attend_fwd(p(x["q"]), p(x["k"]), p(x["v"]), p(self.idx), p(x["w"]), p(self.o_cmp),
-                                      p(self.out), p(self.status), B, N, Hq, Hk, D, bas, bs, K, 0, 0.125, s)
+                                      p(self.out), p(self.status), B, N, Hq, Hk, D, bas, bs, K, 0, 0.125, dt, s)
         rec(4)
         if rc:
             raise RuntimeError(f"mosaic_b200 stage launch failed (rc={rc})")
@@ -701,6 +702,59 @@ def reference_gpu_leg(c, x, stream, reps, warmup):
                                "rows_with_same_selection": float(same_sel)}
     res["reps"] = reps
     return res
+
+
+def fp16_leg(c, sets, stream, steps, warmup):
+    """The same op with fp16 activations (the reference rollout's dtype under fp16 autocast):
+    mosaic_attn_func on fp16 copies of the input sets (pooling, top-k scores and attention
+    operands in fp16), device time per call."""
+    import mosaic_b200 as M
+
+    xs = [{k: v.half() for k, v in x.items()} for x in sets[:4]]
+    ms = _timed_rot(lambda i: M.mosaic_attn_func(xs[i % 4]["q"], xs[i % 4]["k"], xs[i % 4]["v"],
+                                                 xs[i % 4]["w"].unsqueeze(-1), c["bas"], c["bs"], c["K"], False),
+                    stream, steps, warmup)
+    return {"what": "mosaic_attn_func with fp16 q/k/v/gates (native fp16 kernels)", "ms": ms,
+            "tokens_per_s": c["B"] * c["N"] / (ms / 1000), "steps": steps}
+
+
+def rope_leg(c, sets, stream, steps, warmup):
+    """Where Mosaic's 2D RoPE (primitives.py:132-135) is applied: (a) by the producer of q
+    and k (the fused QKV-projection epilogue of MosaicAttention, so the op reads rotated
+    q/k: the `value` path), against (b) inside the op (`rope_tables`: the pool kernel
+    rotates un-rotated q/k on their way in and writes rotated copies that kernel (c)
+    then reads). Device time of mosaic_attn_func per call for both, same inputs."""
+    import mosaic_b200 as M
+    from mosaic_b200.healpix import healpix_rope_tables
+
+    cos, sin = (t.to(sets[0]["q"].device) for t in healpix_rope_tables(c["nside"]))
+    args = (c["bas"], c["bs"], c["K"], False)
+
+    def call(i, tables):
+        x = sets[i % 4]
+        return M.mosaic_attn_func(x["q"], x["k"], x["v"], x["w"].unsqueeze(-1), *args, rope_tables=tables)
+
+    pre = _timed_rot(lambda i: call(i, None), stream, steps, warmup)
+    fused = _timed_rot(lambda i: call(i, (cos, sin)), stream, steps, warmup)
+    B, N, Hq, Hk, D = c["B"], c["N"], c["Hq"], c["Hk"], c["D"]
+    return {"what": "mosaic_attn_func on pre-rotated q/k (RoPE in the producer's epilogue) vs rope_tables "
+                    "(RoPE in the pool kernel, rotated copies written to the workspace and re-read)",
+            "prerotated_ms": pre, "rope_tables_ms": fused, "rope_tables_extra_ms": fused - pre,
+            "rotated_copy_bytes": B * N * (Hq + Hk) * D * 2, "steps": steps}
+
+
+def _timed_rot(fn, stream, reps, warmup):
+    """Like _timed, with the call index passed to fn (rotating input sets)."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(reps):
+        fn(i)
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
 
 
 # One step of the Mosaic U-Net calls the block-sparse attention 14 times per member, with
@@ -898,6 +952,11 @@ def b200_arm(args):
                           "ranks all copies share the host's memory and PCIe root complex"}
         del host, out_host, pipe
 
+    f16 = rope = None
+    if rank == 0 and world == 1:
+        f16 = fp16_leg(c, sets, stream, max(3, min(args.steps, 50)), max(3, args.warmup))
+        if "nside" in c:
+            rope = rope_leg(c, sets, stream, max(3, min(args.steps, 50)), max(3, args.warmup))
     ens = None
     if not args.no_ensemble and name == "S1":
         ens = ensemble_leg(dev, rank, world, dist, stream, steps=max(2, min(args.steps, 4)), warmup=1)
@@ -970,6 +1029,10 @@ def b200_arm(args):
         "e2e": e2e,
         "cpu_baseline": cpu,
     }
+    if f16 is not None:
+        line["fp16"] = f16
+    if rope is not None:
+        line["rope_placement"] = rope
     if ens is not None:
         line["ensemble"] = ens
     if ref_gpu is not None:

@@ -3,8 +3,10 @@
  * Mosaic (maxxxzdn/mosaic). Every entry point takes plain device pointers,
  * sizes and a cudaStream_t (passed as void*), launches asynchronously on that
  * stream, allocates nothing and synchronises nothing. Tensors are dense and
- * row-major in the reference's layouts ([batch, seq, heads, head_dim]); all
- * activations are bf16, head_dim is 64, and query heads per kv head (G) is 4.
+ * row-major in the reference's layouts ([batch, seq, heads, head_dim]); head_dim
+ * is 64 and query heads per kv head (G) is 4. The attention entry points take a
+ * `dtype` (MOSAIC_DTYPE_BF16 or MOSAIC_DTYPE_F16) for all their 16-bit tensors; the
+ * projection, interpolation, resampling and backward entry points are bf16.
  *
  * Return value: MOSAIC_OK or a MOSAIC_ERR_* code (argument errors are detected
  * on the host before anything is launched). Faults detected on the device are
@@ -34,19 +36,25 @@ extern "C" {
 #define MOSAIC_ERR_WORKSPACE 3        /* workspace missing or smaller than mosaic_bsa_workspace_bytes() */
 #define MOSAIC_ERR_CUDA 4             /* a CUDA runtime / driver call failed (launch, tensor map) */
 
+/* ---- activation types (the `dtype` arguments) --------------------------- */
+#define MOSAIC_DTYPE_BF16 0 /* bfloat16 */
+#define MOSAIC_DTYPE_F16 1  /* IEEE half: the reference's dtype under torch.autocast(float16)
+                               (inference.py:59,379); pooled means and top-k scores are then
+                               rounded to fp16 as its attn_topk does (primitives.py:37-49) */
+
 /* ---- device status bits (OR-ed into *status) -------------------------- */
 #define MOSAIC_STATUS_TIMEOUT 1   /* a pipeline wait exceeded its time limit; the kernel gave up */
 #define MOSAIC_STATUS_BAD_INDEX 2 /* a block index was outside [0, seq_len / block_size); it was clamped to 0 */
 
 /* Arguments of mosaic_bsa_fwd (the flags mirror primitives.mosaic_attn_func). */
 typedef struct MosaicBsaArgs {
-  const void* q;        /* [B, N, Hq, 64] bf16                                            */
-  const void* k;        /* [B, N, Hk, 64] bf16                                            */
-  const void* v;        /* [B, N, Hk, 64] bf16                                            */
-  const void* gates;    /* [3, B, N, Hq] bf16 = weight_ba_cmp_slc; NULL iff block_attn_only */
+  const void* q;        /* [B, N, Hq, 64] dtype                                           */
+  const void* k;        /* [B, N, Hk, 64] dtype                                           */
+  const void* v;        /* [B, N, Hk, 64] dtype                                           */
+  const void* gates;    /* [3, B, N, Hq] dtype = weight_ba_cmp_slc; NULL iff block_attn_only */
   const float* rope_cos; /* [N, 32] fp32 or NULL. When set, q and k are NOT yet rotated:   */
   const float* rope_sin; /*   the library applies Mosaic's 2D RoPE before pooling.          */
-  void* out;            /* [B, N, Hq, 64] bf16                                            */
+  void* out;            /* [B, N, Hq, 64] dtype                                           */
   int64_t* block_indices; /* [B, N/bs, Hk, K] int64 selected blocks (written); may be NULL */
   void* workspace;      /* device scratch of >= mosaic_bsa_workspace_bytes() bytes, 256-aligned */
   size_t workspace_bytes;
@@ -62,6 +70,7 @@ typedef struct MosaicBsaArgs {
   int block_attn_only;  /* != 0: return the local branch only                              */
   int no_compression;   /* != 0: drop the compressed branch, renormalise w_ba / w_slc       */
   float softmax_scale;  /* <= 0 selects head_dim^-0.5                                      */
+  int dtype;            /* MOSAIC_DTYPE_BF16 or MOSAIC_DTYPE_F16                           */
 } MosaicBsaArgs;
 
 /* Version of this ABI (bumped on any signature or struct change). */
@@ -98,9 +107,13 @@ MOSAIC_API int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream);
  * compiled into the library (held on every device that loads it until exit), so
  * calls needing more than 8 MiB of scratch (mosaic_bsa_workspace_bytes) return
  * MOSAIC_ERR_WORKSPACE, and fused RoPE (rope_cos/rope_sin) returns
- * MOSAIC_ERR_UNSUPPORTED. The first call on a device looks up the array's address;
- * make it before any stream capture. All calls on a device share the array: calls
- * that overlap on the GPU race and must be serialised by the caller. */
+ * MOSAIC_ERR_UNSUPPORTED; a rejected call launches nothing and writes nothing to
+ * out or block_indices. The first call on a device looks up the array's address
+ * and keeps it for the life of the process: make that call before any stream
+ * capture, and do not use this entry point on a device after cudaDeviceReset (the
+ * kept address then belongs to the destroyed context). All calls on a device share
+ * the array: calls that overlap on the GPU race and must be serialised by the
+ * caller. */
 MOSAIC_API int mosaic_bsa_fwd_noalloc(const MosaicBsaArgs* args, void* stream);
 
 /* The fused attention stage of mosaic_bsa_fwd on its own: local-window attention
@@ -114,7 +127,7 @@ MOSAIC_API int mosaic_bsa_attend_fwd(const void* q, const void* k, const void* v
                                      const void* gates, const void* o_cmp, void* out, int* status, int batch,
                                      int seq_len, int num_q_heads, int num_kv_heads, int head_dim,
                                      int block_attn_size, int sparse_block_size, int sparse_block_count,
-                                     int combine, float softmax_scale, void* stream);
+                                     int combine, float softmax_scale, int dtype, void* stream);
 
 /* Selected-block attention: out[b,n,j] = softmax over the K*bs keys of blocks
  * block_indices[b, n/bs, j/G, :] of kv head j/G. Optional lse (log2 units, fp32
@@ -122,23 +135,25 @@ MOSAIC_API int mosaic_bsa_attend_fwd(const void* q, const void* k, const void* v
  * (ops.py:137-176, ops.py:25-134) behind ops.mosaic_sparse_attn (ops.py:557). */
 MOSAIC_API int mosaic_sparse_attn_fwd(const void* q, const void* k, const void* v, const int64_t* block_indices, void* out,
                            float* lse, int* status, int batch, int seq_len, int num_q_heads, int num_kv_heads,
-                           int head_dim, int block_size, int block_count, float softmax_scale, void* stream);
+                           int head_dim, int block_size, int block_count, float softmax_scale, int dtype,
+                           void* stream);
 
 /* Local block attention: full (non-causal) GQA attention inside each window of
  * block_size consecutive tokens. Replaces primitives.block_attention
  * (primitives.py:28-32) = flash_attn_func on [(B*N/bs), bs, H, 64]. */
 MOSAIC_API int mosaic_block_attn_fwd(const void* q, const void* k, const void* v, void* out, int* status, int batch,
                           int seq_len, int num_q_heads, int num_kv_heads, int head_dim, int block_size,
-                          float softmax_scale, void* stream);
+                          float softmax_scale, int dtype, void* stream);
 
 /* Mean-pool q, k, v over contiguous blocks of block_size tokens (fp32 sums,
- * bf16 results); with rope_cos/rope_sin set, rotate q and k first and also write
+ * results rounded to dtype); with rope_cos/rope_sin set, rotate q and k first and also write
  * the rotated tensors to q_rot / k_rot. q_cmp and v_cmp may be NULL to skip them.
  * Replaces the einops reduce calls at primitives.py:65-66,76 and, with RoPE,
  * RoPE.forward (primitives.py:132-135) for q and k. */
 MOSAIC_API int mosaic_block_pool(const void* q, const void* k, const void* v, const float* rope_cos, const float* rope_sin,
                       void* q_rot, void* k_rot, void* q_cmp, void* k_cmp, void* v_cmp, int batch, int seq_len,
-                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, void* stream);
+                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, int dtype,
+                      void* stream);
 
 /* Coarse (compressed) attention over nb pooled tokens: full GQA attention with
  * scale softmax_scale. Replaces flash_attn_func(q_cmp, k_cmp, v_cmp) at
@@ -146,15 +161,17 @@ MOSAIC_API int mosaic_block_pool(const void* q, const void* k, const void* v, co
  * epilogue of mosaic_bsa_fwd does by indexing). */
 MOSAIC_API int mosaic_cmp_attn_fwd(const void* q_cmp, const void* k_cmp, const void* v_cmp, void* o_cmp, int* status,
                         int batch, int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
-                        float softmax_scale, void* stream);
+                        float softmax_scale, int dtype, void* stream);
 
-/* Top-k block selection: scores_j = q_cmp[:, :, j] . k_cmp[:, :, j/G]^T (bf16),
- * mean over the strided head group {h, h+Hk, ...} (bf16), then the indices of
+/* Top-k block selection: scores_j = q_cmp[:, :, j] . k_cmp[:, :, j/G]^T (fp32 sums
+ * rounded to dtype), mean over the strided head group {h, h+Hk, ...} (rounded to
+ * dtype), then the indices of
  * the block_count largest per (b, query block, kv head), sorted by score
  * descending, ties to the lower index. Replaces primitives.attn_topk
  * (primitives.py:35-51). */
 MOSAIC_API int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indices, int batch, int num_blocks,
-                     int num_q_heads, int num_kv_heads, int head_dim, int block_count, void* stream);
+                     int num_q_heads, int num_kv_heads, int head_dim, int block_count, int dtype,
+                     void* stream);
 
 /* Scratch bytes mosaic_sparse_attn_bwd needs for these sizes (row dot products
  * D = rowsum(out * grad_out) and the inverted block index). */

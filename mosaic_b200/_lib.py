@@ -17,6 +17,9 @@ MOSAIC_ERR_CUDA = 4
 MOSAIC_STATUS_TIMEOUT = 1
 MOSAIC_STATUS_BAD_INDEX = 2
 
+MOSAIC_DTYPE_BF16 = 0
+MOSAIC_DTYPE_F16 = 1
+
 # Every symbol include/mosaic_b200.h declares, with its ctypes signature.
 _vp, _i, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
 
@@ -34,6 +37,7 @@ class MosaicBsaArgs(ctypes.Structure):
         ("block_attn_size", _i), ("sparse_block_size", _i), ("sparse_block_count", _i),
         ("block_attn_only", _i), ("no_compression", _i),
         ("softmax_scale", _f),
+        ("dtype", _i),
     ]
 
 
@@ -44,12 +48,12 @@ SIGNATURES = {
     "mosaic_bsa_workspace_bytes": ([_i, _i, _i, _i, _i, _i, _i, _i], _sz),
     "mosaic_bsa_fwd": ([ctypes.POINTER(MosaicBsaArgs), _vp], _i),
     "mosaic_bsa_fwd_noalloc": ([ctypes.POINTER(MosaicBsaArgs), _vp], _i),
-    "mosaic_bsa_attend_fwd": ([_vp] * 8 + [_i] * 9 + [_f, _vp], _i),
-    "mosaic_sparse_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp], _i),
-    "mosaic_block_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp], _i),
-    "mosaic_block_pool": ([_vp] * 10 + [_i] * 6 + [_vp], _i),
-    "mosaic_cmp_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp], _i),
-    "mosaic_attn_topk": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp], _i),
+    "mosaic_bsa_attend_fwd": ([_vp] * 8 + [_i] * 9 + [_f, _i, _vp], _i),
+    "mosaic_sparse_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _i, _vp], _i),
+    "mosaic_block_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp], _i),
+    "mosaic_block_pool": ([_vp] * 10 + [_i] * 7 + [_vp], _i),
+    "mosaic_cmp_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _vp], _i),
+    "mosaic_attn_topk": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp], _i),
     "mosaic_sparse_attn_bwd_workspace_bytes": ([_i] * 7, _sz),
     "mosaic_sparse_attn_bwd": ([_vp] * 10 + [_vp, _sz, _vp] + [_i] * 7 + [_f, _vp], _i),
     "mosaic_attn_qkv_proj": ([_vp] * 9 + [_i] * 6 + [_vp], _i),
@@ -62,7 +66,7 @@ SIGNATURES = {
     "mosaic_healpix_upsample": ([_vp] * 8 + [_i] * 5 + [_f, _vp], _i),
 }
 
-EXPECTED_ABI_VERSION = 1
+EXPECTED_ABI_VERSION = 2
 
 _lib = None
 

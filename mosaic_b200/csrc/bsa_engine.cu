@@ -30,8 +30,13 @@
 // core, is the first limit.
 //
 // TMEM (512 columns, fp32): S/P buffer b of M-tile m at 64*(2m+b) (P overwrites
-// the first 32 columns of its S buffer as packed bf16 pairs and feeds P*V from
+// the first 32 columns of its S buffer as packed 16-bit pairs and feeds P*V from
 // TMEM), O_local of M-tile m at 256+128m, O_selected at 320+128m.
+//
+// Activation type: bf16, or fp16 (the reference's dtype under fp16 autocast). The
+// kernel is instantiated for both; with fp16, Q, K, V and P enter the tensor core
+// as fp16 (kind::f16 with f16 operands, fp32 accumulation) and the gates, coarse
+// rows and output are fp16.
 #include <cmath>
 #include <cstring>
 
@@ -42,13 +47,18 @@ namespace mosaic {
 
 #ifdef MOSAIC_TRACE
 // Development timeline (off in the library build): clock64() stamps of one CTA's
-// pipeline events, read back by a tracing build's host code.
+// pipeline events during its MOSAIC_TRACE_IT-th work unit, read back by a tracing
+// build's host code.
 __device__ long long g_engine_trace[4096];
+#ifndef MOSAIC_TRACE_IT
+#define MOSAIC_TRACE_IT 0
+#endif
 #define MOSAIC_TRACE_AT(cond, slot) \
   do {                              \
     if (cond) g_engine_trace[(slot)] = clock64(); \
   } while (0)
 #else
+#define MOSAIC_TRACE_IT 0
 #define MOSAIC_TRACE_AT(cond, slot) \
   do {                              \
     (void)(cond);                   \
@@ -73,9 +83,9 @@ constexpr int kPolyNum = MOSAIC_POLY_NUM;
 struct EngineParams {
   CUtensorMap tm_q, tm_k, tm_v;
   const int64_t* block_idx;
-  const __nv_bfloat16* gates;
-  const __nv_bfloat16* o_cmp;
-  __nv_bfloat16* out;
+  const uint16_t* gates;  // 16-bit values of the activation type
+  const uint16_t* o_cmp;
+  uint16_t* out;
   float* lse;
   int* status;
   int B, Nq, Nk, Hq, Hk;
@@ -158,12 +168,13 @@ __device__ __forceinline__ KeyTile key_tile(const EngineParams& p, const int* se
   return kt;
 }
 
-// exp2 of 64 scores against max m, packed in place as 32 bf16 pairs (s[i] <- s[2i],
-// s[2i+1]); returns the fp32 row sum. Of every kPolyDen pairs the last kPolyNum
-// use the software exp2, the others ex2.approx.
+// exp2 of 64 scores against max m, packed in place as 32 pairs of the activation
+// type (s[i] <- s[2i], s[2i+1]); returns the fp32 row sum. Of every kPolyDen pairs
+// the last kPolyNum use the software exp2, the others ex2.approx.
 #ifndef MOSAIC_NACC
 #define MOSAIC_NACC 8
 #endif
+template <bool kF16>
 __device__ __forceinline__ float exp_pack_tile(uint32_t (&s)[64], float c, float m) {
   const uint64_t c2 = f2_pack(c, c);
   const uint64_t nm2 = f2_pack(-m, -m);
@@ -185,7 +196,7 @@ __device__ __forceinline__ float exp_pack_tile(uint32_t (&s)[64], float c, float
     acc[i % kAcc] = f2_add(acc[i % kAcc], e);
     float e0, e1;
     f2_unpack(e, e0, e1);
-    s[i] = pack_bf16x2(e0, e1);
+    s[i] = Act<kF16>::pack(e0, e1);
   }
 #pragma unroll
   for (int w = kAcc / 2; w > 0; w /= 2)
@@ -216,7 +227,8 @@ __device__ __forceinline__ void load_scores(uint32_t tS, uint32_t (&s)[64], int 
 // first tile of a branch, and any non-finite sum take the exact path: reload S,
 // take the row max, rescale this row's O accumulator (after the previous P*V has
 // landed, `o_done`) and l, and exponentiate again. P is written as 32 packed
-// bf16 pairs over the first 32 columns of the S buffer.
+// 16-bit pairs over the first 32 columns of the S buffer.
+template <bool kF16>
 __device__ __forceinline__ bool softmax_tile(uint32_t tS, uint32_t tO, int valid, bool first, float c,
                                              float& m_run, float& l_run, uint64_t* o_done, uint32_t o_parity,
                                              volatile int* abort_flag, int* status, int tslot) {
@@ -227,7 +239,7 @@ __device__ __forceinline__ bool softmax_tile(uint32_t tS, uint32_t tO, int valid
   float sum = 0.f;
   bool exact = first;
   if (!first) {
-    sum = exp_pack_tile(s, c, m_run);
+    sum = exp_pack_tile<kF16>(s, c, m_run);
     exact = !(sum <= kSumLimit);  // also catches NaN / inf
   }
   MOSAIC_TRACE_AT(tslot >= 0, 3000 + tslot * 4 + 1);
@@ -267,7 +279,7 @@ __device__ __forceinline__ bool softmax_tile(uint32_t tS, uint32_t tO, int valid
       if (!first) l_run *= alpha;
       m_run = m_new;
     }
-    const float sum2 = exp_pack_tile(s, c, m_run);  // rows not on the exact path recompute the same values
+    const float sum2 = exp_pack_tile<kF16>(s, c, m_run);  // rows not on the exact path recompute the same values
     if (exact) sum = sum2;
   }
   tmem_st32(tS, s);
@@ -283,7 +295,9 @@ __device__ __forceinline__ bool wait_noabort(uint64_t* bar, uint32_t parity, int
   return bounded_wait(bar, parity, &dummy, status);
 }
 
+template <bool kF16>
 __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_constant__ EngineParams p) {
+  using A = Act<kF16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = tiles;  // two buffers of 2 M-tiles
@@ -401,8 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
     // Warp 1 issues every MMA of M-tile 0 and warp 2 those of M-tile 1, so the two
     // issue chains overlap on the tensor core.
     const int m = warp - 1;
-    const uint32_t idesc_s = make_idesc_bf16(128, 64, false);
-    const uint32_t idesc_pv = make_idesc_bf16(128, 64, true);
+    const uint32_t idesc_s = make_idesc(128, 64, false, A::kMmaFmt);
+    const uint32_t idesc_pv = make_idesc(128, 64, true, A::kMmaFmt);
     const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sQa = smem_u32(sQ);
     // S_m(gt) = Q_m K(gt)^T into S buffer gt%2 of M-tile m
     auto issue_s = [&](uint64_t qdesc, int gt) {
@@ -437,12 +451,12 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
         const uint32_t col_o_off = t < w.T_loc ? 0u : 64u;
         const uint32_t acc0 = (t == 0 || t == w.T_loc) ? 0u : 1u;
         const uint64_t vdesc = sw128_desc(sVa + (gt % kStages) * kBoxBytes, 1024, 16384);
-        MOSAIC_TRACE_AT(traced_cta && it == 0 && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 0);
+        MOSAIC_TRACE_AT(traced_cta && it == MOSAIC_TRACE_IT && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 0);
         if (!warp_wait(&sm.p_full[m][gt & 1], (gt >> 1) & 1, abort_flag, p.status)) {
           ok = false;
           break;
         }
-        MOSAIC_TRACE_AT(traced_cta && it == 0 && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 1);
+        MOSAIC_TRACE_AT(traced_cta && it == MOSAIC_TRACE_IT && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 1);
         tc_fence_after();
         const uint32_t tO = tmem + col_ol(m) + col_o_off;
         const uint32_t tP = tmem + col_s(m, gt & 1);
@@ -459,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
           issue_s(qdesc, gt + 2);
         }
         tc_commit_elect(&sm.kv_empty[gt % kStages]);
-        MOSAIC_TRACE_AT(traced_cta && it == 0 && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 2);
+        MOSAIC_TRACE_AT(traced_cta && it == MOSAIC_TRACE_IT && lane == 0 && t < 64, 1024 + (m * 64 + t) * 3 + 2);
       }
       if (!ok) break;
       tc_commit_elect(&sm.q_empty[qbuf]);  // every S of this unit has been issued
@@ -497,9 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       } else if (live) {
         const size_t plane = static_cast<size_t>(p.B) * p.Nq * p.Hq;
         const size_t gi = (static_cast<size_t>(w.b) * p.Nq + n) * p.Hq + head;
-        const float w0 = __bfloat162float(p.gates[gi]);
-        const float w1 = __bfloat162float(p.gates[plane + gi]);
-        const float w2 = __bfloat162float(p.gates[2 * plane + gi]);
+        const float w0 = A::from_bits(p.gates[gi]);
+        const float w1 = A::from_bits(p.gates[plane + gi]);
+        const float w2 = A::from_bits(p.gates[2 * plane + gi]);
         if (p.combine == kCombineGated) {
           c0 = w0;
           c1 = w1;
@@ -524,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
           m_run = -INFINITY;
           l_run = 0.f;
         }
-        const bool rec = traced_cta && it == 0 && row == 0 && t < 64;
+        const bool rec = traced_cta && it == MOSAIC_TRACE_IT && row == 0 && t < 64;
         MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 0);
         if (!bounded_wait(&sm.s_full[wg][gt & 1], (gt >> 1) & 1, abort_flag, p.status)) {
           ok = false;
@@ -535,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
         const int valid = t < w.T_loc ? min(64, w.wend - (w.wstart + 64 * t)) : 64;
         const bool first = (t == 0) || (t == w.T_loc);
         const uint32_t tS = tmem + lane_off + col_s(wg, gt & 1);
-        ok = softmax_tile(tS, t < w.T_loc ? tOl : tOs, valid, first, p.scale_log2, m_run, l_run, &sm.o_done[wg],
+        ok = softmax_tile<kF16>(tS, t < w.T_loc ? tOl : tOs, valid, first, p.scale_log2, m_run, l_run, &sm.o_done[wg],
                           (gt - 1) & 1, abort_flag, p.status, rec ? wg * 64 + t : -1);
         MOSAIC_TRACE_AT(rec, (wg * 64 + t) * 5 + 4);
         tc_fence_before();
@@ -559,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
 #pragma unroll
       for (int i = 0; i < 8; ++i) cmpv[i] = cmp_row != nullptr ? __ldg(cmp_row + i) : make_uint4(0, 0, 0, 0);
 
-      MOSAIC_TRACE_AT(traced_cta && it == 0 && row == 0, 2002 + wg);
+      MOSAIC_TRACE_AT(traced_cta && it == MOSAIC_TRACE_IT && row == 0, 2002 + wg);
       if (!bounded_wait(&sm.o_final[wg], it & 1, abort_flag, p.status)) {
         ok = false;
         break;
@@ -593,10 +607,10 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
         if (cmp_row != nullptr) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(&cmpv[4 * half + i]);
+            const uint32_t* bv = reinterpret_cast<const uint32_t*>(&cmpv[4 * half + i]);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float2 f2v = __bfloat1622float2(bv[j]);
+              const float2 f2v = A::unpack(bv[j]);
               acc[8 * i + 2 * j] = fmaf(c1, f2v.x, acc[8 * i + 2 * j]);
               acc[8 * i + 2 * j + 1] = fmaf(c1, f2v.y, acc[8 * i + 2 * j + 1]);
             }
@@ -606,10 +620,10 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             uint4 v;
-            v.x = pack_bf16x2(acc[8 * i + 0], acc[8 * i + 1]);
-            v.y = pack_bf16x2(acc[8 * i + 2], acc[8 * i + 3]);
-            v.z = pack_bf16x2(acc[8 * i + 4], acc[8 * i + 5]);
-            v.w = pack_bf16x2(acc[8 * i + 6], acc[8 * i + 7]);
+            v.x = A::pack(acc[8 * i + 0], acc[8 * i + 1]);
+            v.y = A::pack(acc[8 * i + 2], acc[8 * i + 3]);
+            v.z = A::pack(acc[8 * i + 4], acc[8 * i + 5]);
+            v.w = A::pack(acc[8 * i + 6], acc[8 * i + 7]);
             dst[4 * half + i] = v;
           }
         }
@@ -617,6 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       // O has been read: the next unit's first P*V may overwrite it.
       tc_fence_before();
       mbar_arrive(&sm.o_empty[wg]);
+      MOSAIC_TRACE_AT(traced_cta && it == MOSAIC_TRACE_IT && row == 0, 2006 + wg);
       if (live && p.lse != nullptr && T_slc > 0)
         p.lse[(static_cast<size_t>(w.b) * p.Nq + n) * p.Hq + head] = m_slc + log2f(l_slc);
       g += w.T;
@@ -638,14 +653,14 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
 int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
   EngineParams p;
   memset(&p, 0, sizeof(p));
-  if (make_tmap_bf16_2d(&p.tm_q, a.q, static_cast<uint64_t>(a.B) * a.Nq, static_cast<uint64_t>(a.Hq) * 64) ||
-      make_tmap_bf16_2d(&p.tm_k, a.k, static_cast<uint64_t>(a.B) * a.Nk, static_cast<uint64_t>(a.Hk) * 64) ||
-      make_tmap_bf16_2d(&p.tm_v, a.v, static_cast<uint64_t>(a.B) * a.Nk, static_cast<uint64_t>(a.Hk) * 64))
+  if (make_tmap_2d(&p.tm_q, a.q, static_cast<uint64_t>(a.B) * a.Nq, static_cast<uint64_t>(a.Hq) * 64, a.f16) ||
+      make_tmap_2d(&p.tm_k, a.k, static_cast<uint64_t>(a.B) * a.Nk, static_cast<uint64_t>(a.Hk) * 64, a.f16) ||
+      make_tmap_2d(&p.tm_v, a.v, static_cast<uint64_t>(a.B) * a.Nk, static_cast<uint64_t>(a.Hk) * 64, a.f16))
     return MOSAIC_ERR_CUDA;
   p.block_idx = a.block_idx;
-  p.gates = static_cast<const __nv_bfloat16*>(a.gates);
-  p.o_cmp = static_cast<const __nv_bfloat16*>(a.o_cmp);
-  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.gates = static_cast<const uint16_t*>(a.gates);
+  p.o_cmp = static_cast<const uint16_t*>(a.o_cmp);
+  p.out = static_cast<uint16_t*>(a.out);
   p.lse = a.lse;
   p.status = a.status;
   p.B = a.B;
@@ -663,15 +678,16 @@ int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
   p.qtiles = (a.Nq + kQTile - 1) / kQTile;
   p.units = a.B * a.Hk * p.qtiles;
 
-  // The shared-memory opt-in is a per-device function attribute: set it once per device.
-  static bool attr_done[64] = {};
+  // The shared-memory opt-in is a per-device function attribute: set it once per
+  // device and instantiation.
+  static bool attr_done[2][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOSAIC_ERR_CUDA;
-  if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(bsa_engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+  if (!attr_done[a.f16][dev]) {
+    if (cudaFuncSetAttribute(a.f16 ? bsa_engine_kernel<true> : bsa_engine_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) != cudaSuccess)
       return MOSAIC_ERR_CUDA;
-    attr_done[dev] = true;
+    attr_done[a.f16][dev] = true;
   }
   // Persistent: one CTA per SM (TMEM and shared memory allow no more), each
   // walking work units blockIdx.x, blockIdx.x + gridDim.x, ...
@@ -680,7 +696,10 @@ int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
       cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return MOSAIC_ERR_CUDA;
   const int grid = p.units < sm_count[dev] ? p.units : sm_count[dev];
-  bsa_engine_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  if (a.f16)
+    bsa_engine_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(p);
+  else
+    bsa_engine_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 

@@ -13,7 +13,7 @@
 
 namespace mosaic {
 
-int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, bool f16) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
@@ -27,7 +27,8 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
   const cuuint64_t strides[1] = {cols * 2};
   const cuuint32_t box[2] = {64, 64};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+  const CUresult r = encode(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                            const_cast<void*>(base), dims, strides, box,
                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : 1;
@@ -80,6 +81,7 @@ constexpr int kMaxTopK = 128;    // topk.cu kMaxK
 constexpr int kMaxSelect = 1024;  // bsa_engine.cu kMaxSel
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool valid_dtype(int dtype) { return dtype == MOSAIC_DTYPE_BF16 || dtype == MOSAIC_DTYPE_F16; }
 inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 inline float default_scale(float s) { return s > 0.f ? s : 0.125f; }  // 64 ** -0.5
 
@@ -118,7 +120,7 @@ using namespace mosaic;
 
 extern "C" {
 
-int mosaic_abi_version(void) { return 1; }
+int mosaic_abi_version(void) { return 2; }
 
 int mosaic_selftest_wait_timeout(int* status, int* result, int timeout_us, void* stream) {
   if (status == nullptr || result == nullptr || timeout_us <= 0 || timeout_us > 10000000)
@@ -150,9 +152,11 @@ size_t mosaic_bsa_workspace_bytes(int batch, int seq_len, int num_q_heads, int n
 
 int mosaic_sparse_attn_fwd(const void* q, const void* k, const void* v, const int64_t* block_indices, void* out,
                            float* lse, int* status, int batch, int seq_len, int num_q_heads, int num_kv_heads,
-                           int head_dim, int block_size, int block_count, float softmax_scale, void* stream) {
+                           int head_dim, int block_size, int block_count, float softmax_scale, int dtype,
+                           void* stream) {
   int rc = check_heads(batch, seq_len, num_q_heads, num_kv_heads, head_dim);
   if (rc) return rc;
+  if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (batch == 0 || seq_len == 0) return MOSAIC_OK;
   if (!q || !k || !v || !out || !block_indices) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -170,6 +174,7 @@ int mosaic_sparse_attn_fwd(const void* q, const void* k, const void* v, const in
   a.win = 0; a.bs = block_size; a.K = block_count;
   a.combine = kCombineSel;
   a.softmax_scale = default_scale(softmax_scale);
+  a.f16 = dtype == MOSAIC_DTYPE_F16;
   return launch_engine(a, static_cast<cudaStream_t>(stream));
 }
 
@@ -177,9 +182,10 @@ int mosaic_bsa_attend_fwd(const void* q, const void* k, const void* v, const int
                           const void* gates, const void* o_cmp, void* out, int* status, int batch, int seq_len,
                           int num_q_heads, int num_kv_heads, int head_dim, int block_attn_size,
                           int sparse_block_size, int sparse_block_count, int combine, float softmax_scale,
-                          void* stream) {
+                          int dtype, void* stream) {
   int rc = check_heads(batch, seq_len, num_q_heads, num_kv_heads, head_dim);
   if (rc) return rc;
+  if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (batch == 0 || seq_len == 0) return MOSAIC_OK;
   if (combine < kCombineGated || combine > kCombineNoSlc) return MOSAIC_ERR_INVALID_ARGUMENT;
   const bool want_slc = combine != kCombineNoSlc;
@@ -207,14 +213,16 @@ int mosaic_bsa_attend_fwd(const void* q, const void* k, const void* v, const int
   a.win = block_attn_size; a.bs = sparse_block_size; a.K = want_slc ? sparse_block_count : 0;
   a.combine = combine;
   a.softmax_scale = default_scale(softmax_scale);
+  a.f16 = dtype == MOSAIC_DTYPE_F16;
   return launch_engine(a, static_cast<cudaStream_t>(stream));
 }
 
 int mosaic_block_attn_fwd(const void* q, const void* k, const void* v, void* out, int* status, int batch,
                           int seq_len, int num_q_heads, int num_kv_heads, int head_dim, int block_size,
-                          float softmax_scale, void* stream) {
+                          float softmax_scale, int dtype, void* stream) {
   int rc = check_heads(batch, seq_len, num_q_heads, num_kv_heads, head_dim);
   if (rc) return rc;
+  if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (batch == 0 || seq_len == 0) return MOSAIC_OK;
   if (!q || !k || !v || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -228,14 +236,16 @@ int mosaic_block_attn_fwd(const void* q, const void* k, const void* v, void* out
   a.win = block_size; a.bs = 64; a.K = 0;
   a.combine = kCombineLocal;
   a.softmax_scale = default_scale(softmax_scale);
+  a.f16 = dtype == MOSAIC_DTYPE_F16;
   return launch_engine(a, static_cast<cudaStream_t>(stream));
 }
 
 int mosaic_cmp_attn_fwd(const void* q_cmp, const void* k_cmp, const void* v_cmp, void* o_cmp, int* status,
                         int batch, int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
-                        float softmax_scale, void* stream) {
+                        float softmax_scale, int dtype, void* stream) {
   int rc = check_heads(batch, num_blocks, num_q_heads, num_kv_heads, head_dim);
   if (rc) return rc;
+  if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (batch == 0 || num_blocks == 0) return MOSAIC_OK;
   if (!q_cmp || !k_cmp || !v_cmp || !o_cmp) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(q_cmp) || !aligned16(k_cmp) || !aligned16(v_cmp) || !aligned16(o_cmp))
@@ -248,13 +258,16 @@ int mosaic_cmp_attn_fwd(const void* q_cmp, const void* k_cmp, const void* v_cmp,
   a.win = num_blocks; a.bs = 64; a.K = 0;
   a.combine = kCombineLocal;
   a.softmax_scale = default_scale(softmax_scale);
+  a.f16 = dtype == MOSAIC_DTYPE_F16;
   return launch_engine(a, static_cast<cudaStream_t>(stream));
 }
 
 int mosaic_block_pool(const void* q, const void* k, const void* v, const float* rope_cos, const float* rope_sin,
                       void* q_rot, void* k_rot, void* q_cmp, void* k_cmp, void* v_cmp, int batch, int seq_len,
-                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, void* stream) {
+                      int num_q_heads, int num_kv_heads, int head_dim, int block_size, int dtype,
+                      void* stream) {
   if (batch < 0 || seq_len < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
   if (block_size <= 0 || seq_len % block_size != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!k || !k_cmp || (q_cmp && !q) || (v_cmp && !v)) return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -270,12 +283,15 @@ int mosaic_block_pool(const void* q, const void* k, const void* v, const float* 
   a.q_rot = q_rot; a.k_rot = k_rot;
   a.q_cmp = q_cmp; a.k_cmp = k_cmp; a.v_cmp = v_cmp;
   a.B = batch; a.N = seq_len; a.Hq = num_q_heads; a.Hk = num_kv_heads; a.bs = block_size;
+  a.f16 = dtype == MOSAIC_DTYPE_F16;
   return launch_pool(a, static_cast<cudaStream_t>(stream));
 }
 
 int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indices, int batch, int num_blocks,
-                     int num_q_heads, int num_kv_heads, int head_dim, int block_count, void* stream) {
+                     int num_q_heads, int num_kv_heads, int head_dim, int block_count, int dtype,
+                     void* stream) {
   if (batch < 0 || num_blocks < 0 || num_q_heads <= 0 || num_kv_heads <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
   if (num_q_heads % num_kv_heads != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (num_q_heads / num_kv_heads > 8) return MOSAIC_ERR_UNSUPPORTED;
@@ -288,6 +304,7 @@ int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indice
   a.q_cmp = q_cmp; a.k_cmp = k_cmp; a.idx = block_indices;
   a.B = batch; a.nb = num_blocks; a.Hq = num_q_heads; a.Hk = num_kv_heads; a.K = block_count;
   a.status = nullptr;
+  a.f16 = dtype == MOSAIC_DTYPE_F16;
   a.overlap_previous = false;
   return launch_topk(a, static_cast<cudaStream_t>(stream));
 }
@@ -301,6 +318,8 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
   const bool rope = A.rope_cos != nullptr;
   int rc = check_heads(B, N, Hq, Hk, A.head_dim);
   if (rc) return rc;
+  if (!valid_dtype(A.dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  const bool f16 = A.dtype == MOSAIC_DTYPE_F16;
   if (B == 0 || N == 0) return MOSAIC_OK;
   if (!A.q || !A.k || !A.v || !A.out) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!local_only && !A.gates) return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -348,6 +367,7 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
     pl.q_cmp = q_cmp; pl.k_cmp = k_cmp;
     pl.v_cmp = want_cmp ? v_cmp : nullptr;
     pl.B = B; pl.N = N; pl.Hq = Hq; pl.Hk = Hk; pl.bs = bs > 0 ? bs : 64;
+    pl.f16 = f16;
     if ((rc = launch_pool(pl, st))) return rc;
     if (rope) {
       q = pl.q_rot;
@@ -360,7 +380,7 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
     std::memset(&e, 0, sizeof(e));
     e.q = q_cmp; e.k = k_cmp; e.v = v_cmp; e.out = o_cmp; e.status = A.status;
     e.B = B; e.Nq = nb; e.Nk = nb; e.Hq = Hq; e.Hk = Hk;
-    e.win = nb; e.bs = 64; e.K = 0; e.combine = kCombineLocal; e.softmax_scale = scale;
+    e.win = nb; e.bs = 64; e.K = 0; e.combine = kCombineLocal; e.softmax_scale = scale; e.f16 = f16;
     if ((rc = launch_engine(e, st))) return rc;
   }
   // (b) block scores + top-k
@@ -369,6 +389,7 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
     t.q_cmp = q_cmp; t.k_cmp = k_cmp; t.idx = idx;
     t.B = B; t.nb = nb; t.Hq = Hq; t.Hk = Hk; t.K = K;
     t.status = A.status;
+    t.f16 = f16;
     t.overlap_previous = want_cmp;  // runs beside the coarse attention (both only read the pooled tensors)
     if ((rc = launch_topk(t, st))) return rc;
   }
@@ -387,6 +408,7 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
   e.K = want_slc ? K : 0;
   e.combine = local_only ? kCombineLocal : (no_cmp ? kCombineNoCmp : (want_slc ? kCombineGated : kCombineNoSlc));
   e.softmax_scale = scale;
+  e.f16 = f16;
   return launch_engine(e, st);
 }
 

@@ -23,15 +23,16 @@ enum Combine : int {
 
 // One launch of the fused attention engine: for every (batch b, kv head h,
 // 64-query tile) it runs the local-window branch and/or the selected-block branch
-// for the G = 4 query heads of kv group h and writes the combined bf16 rows.
+// for the G = 4 query heads of kv group h and writes the combined rows. Every
+// 16-bit tensor below has the launch's activation type (bf16, or fp16 when f16).
 struct EngineLaunch {
-  const void* q;  // [B, Nq, Hq, 64] bf16
-  const void* k;  // [B, Nk, Hk, 64] bf16
-  const void* v;  // [B, Nk, Hk, 64] bf16
+  const void* q;  // [B, Nq, Hq, 64]
+  const void* k;  // [B, Nk, Hk, 64]
+  const void* v;  // [B, Nk, Hk, 64]
   const int64_t* block_idx;  // [B, Nq/bs, Hk, K] or null when K == 0
-  const void* gates;         // [3, B, Nq, Hq] bf16 or null
-  const void* o_cmp;         // [B, Nq/bs, Hq, 64] bf16 or null
-  void* out;                 // [B, Nq, Hq, 64] bf16
+  const void* gates;         // [3, B, Nq, Hq] or null
+  const void* o_cmp;         // [B, Nq/bs, Hq, 64] or null
+  void* out;                 // [B, Nq, Hq, 64]
   float* lse;                // [B, Nq, Hq] fp32 (selected branch, log2 units) or null
   int* status;               // device status word or null
   int B, Nq, Nk, Hq, Hk;
@@ -40,30 +41,33 @@ struct EngineLaunch {
   int K;    // selected blocks per query block; 0 = no selected branch
   int combine;
   float softmax_scale;
+  bool f16;  // activations are fp16 (else bf16)
 };
 
 // Mean-pool (optionally after 2D RoPE) of q, k, v over contiguous blocks of `bs` rows.
 struct PoolLaunch {
-  const void* q;  // [B, N, Hq, 64] bf16
-  const void* k;  // [B, N, Hk, 64] bf16
-  const void* v;  // [B, N, Hk, 64] bf16
+  const void* q;  // [B, N, Hq, 64]
+  const void* k;  // [B, N, Hk, 64]
+  const void* v;  // [B, N, Hk, 64]
   const float* rope_cos;  // [N, 32] fp32 or null (no rotation)
   const float* rope_sin;  // [N, 32] fp32 or null
-  void* q_rot;            // [B, N, Hq, 64] bf16 rotated copy (only when rope_cos != null)
-  void* k_rot;            // [B, N, Hk, 64] bf16 rotated copy (only when rope_cos != null)
-  void* q_cmp;            // [B, N/bs, Hq, 64] bf16 (may be null: skip q)
-  void* k_cmp;            // [B, N/bs, Hk, 64] bf16
-  void* v_cmp;            // [B, N/bs, Hk, 64] bf16 (may be null: skip v)
+  void* q_rot;            // [B, N, Hq, 64] rotated copy (only when rope_cos != null)
+  void* k_rot;            // [B, N, Hk, 64] rotated copy (only when rope_cos != null)
+  void* q_cmp;            // [B, N/bs, Hq, 64] (may be null: skip q)
+  void* k_cmp;            // [B, N/bs, Hk, 64]
+  void* v_cmp;            // [B, N/bs, Hk, 64] (may be null: skip v)
   int B, N, Hq, Hk, bs;
+  bool f16;  // every 16-bit tensor above is fp16 instead of bf16 (means rounded to fp16)
 };
 
 // Block scores + top-k selection (GQA group shared, strided head mean).
 struct TopkLaunch {
-  const void* q_cmp;  // [B, nb, Hq, 64] bf16
-  const void* k_cmp;  // [B, nb, Hk, 64] bf16
+  const void* q_cmp;  // [B, nb, Hq, 64]
+  const void* k_cmp;  // [B, nb, Hk, 64]
   int64_t* idx;       // [B, nb, Hk, K]
   int B, nb, Hq, Hk, K;
   int* status;  // device status word or null (timeouts of the tensor-core variant)
+  bool f16;     // q_cmp / k_cmp are fp16 and scores are rounded to fp16 (else bf16)
   // Launch with programmatic stream serialization, so that the kernel may start
   // while the previous kernel of the stream (which must not produce this
   // kernel's inputs) is still running.
@@ -182,9 +186,13 @@ int launch_topk(const TopkLaunch& a, cudaStream_t stream);
 bool topk_tc_supported(const TopkLaunch& a);
 int launch_topk_tc(const TopkLaunch& a, cudaStream_t stream);
 
-// Encodes a 2D bf16 tensor map over `rows` x `cols` elements (row pitch = cols),
-// 64x64 boxes, 128-byte swizzle. Returns 0 on success.
-int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
+// Encodes a 2D tensor map of 16-bit elements (bf16, or fp16 when f16) over
+// `rows` x `cols` elements (row pitch = cols), 64x64 boxes, 128-byte swizzle.
+// Returns 0 on success.
+int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, bool f16);
+inline int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+  return make_tmap_2d(map, base, rows, cols, false);
+}
 // 3D bf16 tensor map (d0 innermost, contiguous), strides of dims 1 and 2 in bytes,
 // 64 x 1 x 64 boxes, 128-byte swizzle: a box lands in shared memory like a 64 x 64 2D box.
 int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,

@@ -24,7 +24,10 @@
 //
 // Set-up: the first call on each device looks up the array's device address with
 // cudaGetSymbolAddress (with that device current) and caches it; later calls
-// reuse the cached address. Make that first call before any stream capture.
+// reuse the cached address. Make that first call before any stream capture. The
+// cache lives as long as the process: cudaDeviceReset destroys the context the
+// address belongs to, so a process that resets a device must not call this entry
+// point on that device afterwards.
 // Nothing here calls cudaMalloc, cudaFree or any allocating routine.
 #include <mutex>
 

@@ -2,23 +2,31 @@
 // Mosaic's 2D RoPE optionally applied to q and k on the way in.
 //
 // Reference: q_cmp/k_cmp/v_cmp = reduce(x, 'b (nb bs) h d -> b nb h d', 'mean')
-// (primitives.py:65-66,76): fp32 accumulation, one rounding to bf16. RoPE
-// (primitives.py:126-135): for pair p of a head, out[2p] = x[2p]*cos - x[2p+1]*sin,
-// out[2p+1] = x[2p+1]*cos + x[2p]*sin in fp32 (each product and the sum rounded
-// separately, as torch evaluates `x*cos + rotate_half(x)*sin`), then cast to bf16;
-// pooling then averages the rotated bf16 values, exactly as the reference pools
-// the rotated tensor.
+// (primitives.py:65-66,76): fp32 accumulation, one rounding to the activation type
+// (bf16, or fp16 under the reference's fp16 autocast). RoPE (primitives.py:126-135):
+// for pair p of a head, out[2p] = x[2p]*cos - x[2p+1]*sin, out[2p+1] = x[2p+1]*cos +
+// x[2p]*sin in fp32 (each product and the sum rounded separately, as torch evaluates
+// `x*cos + rotate_half(x)*sin`), then cast to the activation type; pooling then
+// averages the rotated values, exactly as the reference pools the rotated tensor.
 //
-// Layout: a block of bs rows of q is one contiguous bs x (Hq*128 B) slab (rows of
-// q are [Hq, 64] contiguous), so one CTA streams the q, k and v slabs of one block
-// with 16-byte vector loads: thread (chunk c, row group g) sums rows g, g+RG, ...
-// of the 16-byte column chunk c, then the RG partial sums meet in shared memory.
-// HBM-bound: every input byte is read exactly once.
+// Layout: a block of bs rows is a contiguous bs x (H*128 B) slab per tensor, and one
+// head of one row is 128 contiguous bytes. A work unit is one (batch, block, head of
+// q, k or v) and belongs to one warp: lane l owns the 16-byte chunk l % 8 of the head
+// and the rows l / 8, l / 8 + 4, ... of the block, issues all sixteen 16-byte loads
+// of a 64-row batch before it adds any (every lane keeps 256 bytes in flight, every
+// warp instruction touches four full 128-byte lines), and the four row groups meet
+// through two shuffles. No shared memory and no block barrier, so the grid is just
+// enough warps for every unit and the GPU's warp slots stay full of loads.
+// Rows past the end of a block (block sizes that are not multiples of 64) are
+// skipped. HBM-bound: every input byte is read exactly once.
 #include "kernels.h"
 #include "ptx.cuh"
 
 namespace mosaic {
 namespace {
+
+constexpr int kWarpsPerCta = 4;
+constexpr int kRowsPerBatch = 64;  // rows of a block per load batch (16 per lane)
 
 struct PoolParams {
   const uint4* q;
@@ -28,19 +36,20 @@ struct PoolParams {
   const float* sin;
   uint4* q_rot;
   uint4* k_rot;
-  __nv_bfloat16* q_cmp;
-  __nv_bfloat16* k_cmp;
-  __nv_bfloat16* v_cmp;
+  uint4* q_cmp;
+  uint4* k_cmp;
+  uint4* v_cmp;
   int B, N, Hq, Hk, bs, nb;
-  int cq, ck, cv;  // 16-byte chunks per row of q, k, v (0 when that tensor is skipped)
-  int rg;          // row groups summed in parallel per chunk
+  int nq, nv;  // q / v head slots per block (0 when that tensor is skipped)
+  int slots;   // nq + Hk + nv
+  long long units;
 };
 
-__device__ __forceinline__ float fmul_rn(float a, float b) { return __fmul_rn(a, b); }
-
-// Rotates the 8 bf16 values (4 RoPE pairs starting at pair index p0) of one chunk.
+// Rotates the 8 values (4 RoPE pairs starting at pair index p0) of one chunk.
+template <bool kF16>
 __device__ __forceinline__ uint4 rope_chunk(uint4 x, const float* cos_row, const float* sin_row, int p0) {
-  const __nv_bfloat162* xv = reinterpret_cast<const __nv_bfloat162*>(&x);
+  using A = Act<kF16>;
+  const uint32_t* xv = reinterpret_cast<const uint32_t*>(&x);
   const float4 c = *reinterpret_cast<const float4*>(cos_row + p0);
   const float4 s = *reinterpret_cast<const float4*>(sin_row + p0);
   const float cc[4] = {c.x, c.y, c.z, c.w};
@@ -49,95 +58,102 @@ __device__ __forceinline__ uint4 rope_chunk(uint4 x, const float* cos_row, const
   uint32_t* rv = reinterpret_cast<uint32_t*>(&r);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float2 f = __bfloat1622float2(xv[j]);
-    const float o0 = __fadd_rn(fmul_rn(f.x, cc[j]), fmul_rn(-f.y, ss[j]));
-    const float o1 = __fadd_rn(fmul_rn(f.y, cc[j]), fmul_rn(f.x, ss[j]));
-    rv[j] = pack_bf16x2(o0, o1);
+    const float2 f = A::unpack(xv[j]);
+    const float o0 = __fadd_rn(__fmul_rn(f.x, cc[j]), __fmul_rn(-f.y, ss[j]));
+    const float o1 = __fadd_rn(__fmul_rn(f.y, cc[j]), __fmul_rn(f.x, ss[j]));
+    rv[j] = A::pack(o0, o1);
   }
   return r;
 }
 
-template <bool kRope>
-__global__ void __launch_bounds__(512, 1) pool_kernel(const PoolParams p) {
-  extern __shared__ float part[];  // [rg][C][8]
-  const int C = p.cq + p.ck + p.cv;
-  const int blk = blockIdx.x, b = blockIdx.y;
-  const int c = threadIdx.x % C;
-  const int g = threadIdx.x / C;
-  if (g < p.rg) {
-    const uint4* src;
-    uint4* rot = nullptr;
-    int cpr, cc;  // chunks per row of this tensor, chunk within the row
-    if (c < p.cq) {
-      src = p.q; cpr = p.cq; cc = c; rot = p.q_rot;
-    } else if (c < p.cq + p.ck) {
-      src = p.k; cpr = p.ck; cc = c - p.cq; rot = p.k_rot;
-    } else {
-      src = p.v; cpr = p.cv; cc = c - p.cq - p.ck;
-    }
-    const bool rotate = kRope && c < p.cq + p.ck;
-    const int p0 = (cc & 7) * 4;  // first RoPE pair of this chunk within its head
-    float acc[8];
+template <bool kF16>
+__device__ __forceinline__ void add_chunk(float (&acc)[8], uint4 x) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(&x);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    const int row0 = blk * p.bs;
-    const size_t base = (static_cast<size_t>(b) * p.N + row0) * cpr + cc;
-    // 8 rows per step, all loads issued before any is used, so that each thread
-    // keeps 128 bytes in flight (the kernel is bound by HBM latency x bandwidth).
-    for (int r0 = g; r0 < p.bs; r0 += 8 * p.rg) {
-      uint4 x[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int r = r0 + u * p.rg;
-        x[u] = r < p.bs ? __ldg(src + base + static_cast<size_t>(r) * cpr) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int r = r0 + u * p.rg;
-        if (r >= p.bs) continue;
-        uint4 xv = x[u];
-        if (rotate) {
-          xv = rope_chunk(xv, p.cos + static_cast<size_t>(row0 + r) * 32, p.sin + static_cast<size_t>(row0 + r) * 32, p0);
-          rot[base + static_cast<size_t>(r) * cpr] = xv;
-        }
-        const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(xh[j]);
-          acc[2 * j] += f.x;
-          acc[2 * j + 1] += f.y;
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) part[(g * C + c) * 8 + i] = acc[i];
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = Act<kF16>::unpack(w[j]);
+    acc[2 * j] += f.x;
+    acc[2 * j + 1] += f.y;
   }
-  __syncthreads();
-  if (threadIdx.x < C) {
-    float s[8];
+}
+
+template <bool kF16, bool kRope>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) pool_kernel(const PoolParams p) {
+  using A = Act<kF16>;
+  const long long u = static_cast<long long>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  if (u >= p.units) return;
+  const int lane = threadIdx.x & 31;
+  const int c = lane & 7, rg = lane >> 3;
+  const int slot = static_cast<int>(u % p.slots);
+  const long long bb = u / p.slots;  // b * nb + blk
+  const int blk = static_cast<int>(bb % p.nb), b = static_cast<int>(bb / p.nb);
+
+  const uint4* src;
+  uint4* rot = nullptr;
+  uint4* dst;
+  int H, h;
+  if (slot < p.nq) {
+    src = p.q; rot = p.q_rot; dst = p.q_cmp; H = p.Hq; h = slot;
+  } else if (slot < p.nq + p.Hk) {
+    src = p.k; rot = p.k_rot; dst = p.k_cmp; H = p.Hk; h = slot - p.nq;
+  } else {
+    src = p.v; dst = p.v_cmp; H = p.Hk; h = slot - p.nq - p.Hk;
+  }
+  const bool rotate = kRope && slot < p.nq + p.Hk;
+  const int row0 = blk * p.bs;
+  // 16-byte chunk index of (b, row0, h, c); a row is H * 8 chunks
+  const size_t base = (static_cast<size_t>(b) * p.N + row0) * H * 8 + static_cast<size_t>(h) * 8 + c;
+  const size_t pitch = static_cast<size_t>(H) * 8;
+
+  float acc[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      s[i] = part[c * 8 + i];
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int r0 = 0; r0 < p.bs; r0 += kRowsPerBatch) {
+    uint4 x[kRowsPerBatch / 4];
 #pragma unroll
-      for (int gg = 1; gg < p.rg; ++gg) s[i] += part[(gg * C + c) * 8 + i];
+    for (int i = 0; i < kRowsPerBatch / 4; ++i) {
+      const int r = r0 + rg + 4 * i;
+      x[i] = r < p.bs ? __ldg(src + base + static_cast<size_t>(r) * pitch) : make_uint4(0, 0, 0, 0);
     }
-    __nv_bfloat16* dst;
-    int cpr, cc;
-    if (c < p.cq) {
-      dst = p.q_cmp; cpr = p.cq; cc = c;
-    } else if (c < p.cq + p.ck) {
-      dst = p.k_cmp; cpr = p.ck; cc = c - p.cq;
-    } else {
-      dst = p.v_cmp; cpr = p.cv; cc = c - p.cq - p.ck;
+#pragma unroll
+    for (int i = 0; i < kRowsPerBatch / 4; ++i) {
+      uint4 xv = x[i];
+      const int r = r0 + rg + 4 * i;
+      if (r >= p.bs) continue;
+      if (rotate) {
+        const size_t n = static_cast<size_t>(row0 + r);
+        xv = rope_chunk<kF16>(xv, p.cos + n * 32, p.sin + n * 32, c * 4);
+        rot[base + static_cast<size_t>(r) * pitch] = xv;
+      }
+      add_chunk<kF16>(acc, xv);
     }
+  }
+  // the four row groups (lanes c, c+8, c+16, c+24) meet in a fixed order
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 8);
+    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 16);
+  }
+  if (rg == 0 && dst != nullptr) {
     const float n = static_cast<float>(p.bs);
-    uint4 u;
-    u.x = pack_bf16x2(__fdiv_rn(s[0], n), __fdiv_rn(s[1], n));
-    u.y = pack_bf16x2(__fdiv_rn(s[2], n), __fdiv_rn(s[3], n));
-    u.z = pack_bf16x2(__fdiv_rn(s[4], n), __fdiv_rn(s[5], n));
-    u.w = pack_bf16x2(__fdiv_rn(s[6], n), __fdiv_rn(s[7], n));
-    reinterpret_cast<uint4*>(dst)[(static_cast<size_t>(b) * p.nb + blk) * cpr + cc] = u;
+    uint4 o;
+    o.x = A::pack(__fdiv_rn(acc[0], n), __fdiv_rn(acc[1], n));
+    o.y = A::pack(__fdiv_rn(acc[2], n), __fdiv_rn(acc[3], n));
+    o.z = A::pack(__fdiv_rn(acc[4], n), __fdiv_rn(acc[5], n));
+    o.w = A::pack(__fdiv_rn(acc[6], n), __fdiv_rn(acc[7], n));
+    dst[(static_cast<size_t>(b) * p.nb + blk) * pitch + static_cast<size_t>(h) * 8 + c] = o;
   }
+}
+
+template <bool kF16>
+int launch_typed(const PoolParams& p, bool rope, cudaStream_t stream) {
+  const long long ctas = (p.units + kWarpsPerCta - 1) / kWarpsPerCta;
+  if (ctas > 0x7fffffffLL) return MOSAIC_ERR_UNSUPPORTED;
+  if (rope)
+    pool_kernel<kF16, true><<<static_cast<unsigned>(ctas), kWarpsPerCta * 32, 0, stream>>>(p);
+  else
+    pool_kernel<kF16, false><<<static_cast<unsigned>(ctas), kWarpsPerCta * 32, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
 }  // namespace
@@ -151,39 +167,25 @@ int launch_pool(const PoolLaunch& a, cudaStream_t stream) {
   p.sin = a.rope_sin;
   p.q_rot = static_cast<uint4*>(a.q_rot);
   p.k_rot = static_cast<uint4*>(a.k_rot);
-  p.q_cmp = static_cast<__nv_bfloat16*>(a.q_cmp);
-  p.k_cmp = static_cast<__nv_bfloat16*>(a.k_cmp);
-  p.v_cmp = static_cast<__nv_bfloat16*>(a.v_cmp);
+  p.q_cmp = static_cast<uint4*>(a.q_cmp);
+  p.k_cmp = static_cast<uint4*>(a.k_cmp);
+  p.v_cmp = static_cast<uint4*>(a.v_cmp);
   p.B = a.B;
   p.N = a.N;
   p.Hq = a.Hq;
   p.Hk = a.Hk;
   p.bs = a.bs;
+  if (a.bs <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
   p.nb = a.N / a.bs;
   const bool rope = a.rope_cos != nullptr;
   // With RoPE the rotated q must be produced even when its pooled mean is not needed.
-  p.cq = (a.q_cmp != nullptr || rope) ? a.Hq * 8 : 0;
-  p.ck = a.Hk * 8;
-  p.cv = a.v_cmp != nullptr ? a.Hk * 8 : 0;
-  if (p.cq > 0 && a.q_cmp == nullptr) return MOSAIC_ERR_INVALID_ARGUMENT;
-  const int C = p.cq + p.ck + p.cv;
-  if (C > 512) return MOSAIC_ERR_UNSUPPORTED;
-  p.rg = 512 / C < 4 ? 512 / C : 4;
-  const int threads = ((C * p.rg + 31) / 32) * 32;
-  const size_t smem = static_cast<size_t>(p.rg) * C * 8 * sizeof(float);
-  dim3 grid(p.nb, a.B);
-  if (rope) {
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(pool_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return MOSAIC_ERR_CUDA;
-    pool_kernel<true><<<grid, threads, smem, stream>>>(p);
-  } else {
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(pool_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return MOSAIC_ERR_CUDA;
-    pool_kernel<false><<<grid, threads, smem, stream>>>(p);
-  }
-  return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  if (rope && a.q_cmp == nullptr) return MOSAIC_ERR_INVALID_ARGUMENT;
+  p.nq = (a.q_cmp != nullptr || rope) ? a.Hq : 0;
+  p.nv = a.v_cmp != nullptr ? a.Hk : 0;
+  p.slots = p.nq + a.Hk + p.nv;
+  p.units = static_cast<long long>(a.B) * p.nb * p.slots;
+  if (p.units == 0) return MOSAIC_OK;
+  return a.f16 ? launch_typed<true>(p, rope, stream) : launch_typed<false>(p, rope, stream);
 }
 
 }  // namespace mosaic

@@ -11,6 +11,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "../../include/mosaic_b200.h"
 
@@ -124,12 +125,16 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B and fp32 D (PTX ISA
-// "Instruction descriptor" table): D fmt bits [4,6), A fmt [7,10), B fmt [10,13),
-// B major bit 16, N>>3 at [17,23), M>>4 at [24,29).
-__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+// Instruction descriptor for kind::f16 with fp32 D (PTX ISA "Instruction
+// descriptor" table): D fmt bits [4,6), A fmt [7,10), B fmt [10,13) (0 = f16,
+// 1 = bf16; A and B always share the type), B major bit 16, N>>3 at [17,23),
+// M>>4 at [24,29).
+__host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool b_mn_major, uint32_t ab_fmt) {
+  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool b_mn_major) {
+  return make_idesc(M, N, b_mn_major, 1u);
 }
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand tile whose rows
@@ -207,6 +212,44 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+
+// The 16-bit activation type of a launch: Act<false> = bf16 (MOSAIC_DTYPE_BF16),
+// Act<true> = fp16 (MOSAIC_DTYPE_F16). Values are widened to fp32 for arithmetic
+// and rounded to nearest-even when stored; `round` is that store-and-reload, the
+// rounding point of a tensor op whose output has the activation type.
+template <bool kF16>
+struct Act;
+template <>
+struct Act<false> {
+  using T = __nv_bfloat16;
+  static constexpr uint32_t kMmaFmt = 1;  // kind::f16 operand format code
+  static __device__ __forceinline__ float2 unpack(uint32_t u) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return pack_bf16x2(lo, hi); }
+  static __device__ __forceinline__ float to_float(T x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ float from_bits(uint16_t b) { return __bfloat162float(__ushort_as_bfloat16(b)); }
+  static __device__ __forceinline__ T from_float(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ uint32_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+  static __device__ __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+};
+template <>
+struct Act<true> {
+  using T = __half;
+  static constexpr uint32_t kMmaFmt = 0;
+  static __device__ __forceinline__ float2 unpack(uint32_t u) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static __device__ __forceinline__ float to_float(T x) { return __half2float(x); }
+  static __device__ __forceinline__ float from_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+  static __device__ __forceinline__ T from_float(float x) { return __float2half_rn(x); }
+  static __device__ __forceinline__ uint32_t bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+  static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+};
 
 
 // ---------------------------------------------------------------- single-lane issue from a converged warp

@@ -2,15 +2,17 @@
 //
 // Reference attn_topk (primitives.py:35-51):
 //   k = k_cmp.repeat_interleave(G, dim=2)              -> q head j uses kv head j // G
-//   S_j = q_cmp[:, :, j] @ k[:, :, j]^T                (bf16 matmul: fp32 sum, bf16 result)
+//   S_j = q_cmp[:, :, j] @ k[:, :, j]^T                (matmul in the activation type, bf16
+//                                                       or fp16 under autocast: fp32 sum,
+//                                                       result rounded to that type)
 //   T_h = mean_g S_{g*Hk + h}                          ('b (g h) t k -> b h t k': a STRIDED
-//                                                       head group; fp32 sum, bf16 result)
+//                                                       head group; fp32 sum, rounded again)
 //   idx[b, i, h, :] = topk(T_h[i, :], K, largest)      (int64)
 // The strided group is what the reference computes even though the sparse kernel
 // then uses idx[..., h, :] for the contiguous heads h*G .. h*G+G-1 (ops.py:49);
 // this kernel reproduces it on purpose.
 //
-// Each score becomes the 32-bit key (order-preserving bf16 bits << 16) |
+// Each score becomes the 32-bit key (order-preserving 16-bit float bits << 16) |
 // (65535 - block): keys are unique, their order is score descending with ties to
 // the lower block index (torch.topk's usual order), and the top-K of a row is
 // exactly the K largest keys.
@@ -40,14 +42,14 @@ constexpr int kMaxK = 128;
 constexpr int kTcMinBlocks = 2048;
 
 struct TopkParams {
-  const __nv_bfloat16* q_cmp;
-  const __nv_bfloat16* k_cmp;
+  const uint16_t* q_cmp;  // bf16 or fp16 bits
+  const uint16_t* k_cmp;
   int64_t* idx;
   int B, nb, Hq, Hk, K, G;
 };
 
 struct TopkSmem {
-  __nv_bfloat16 qs[kMaxG][kRows][64];  // 16 KB
+  uint16_t qs[kMaxG][kRows][64];       // 16 KB
   uint32_t keys[kRows][kChunk];        // 64 KB
   uint32_t top[kRows][kMaxK];          // 8 KB  running top list per row (sorted descending)
   uint32_t buf[kWarps][kMaxK];         // 8 KB  per-warp selection buffers
@@ -63,21 +65,31 @@ __device__ __forceinline__ int perm_d(int kk) {
   return 16 * gc + 4 * ks + q;
 }
 
-__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
+// The score rounded to the activation type, as a key whose unsigned order is the
+// score order; bf16 and fp16 are both sign-magnitude, so one transform serves both.
+template <bool kF16>
 __device__ __forceinline__ uint32_t order_key(float t, int block) {
-  uint32_t u = __bfloat16_as_ushort(__float2bfloat16_rn(t));
+  uint32_t u = Act<kF16>::bits(t);
   if (u == 0x8000u) u = 0;  // -0 ties with +0, as in torch.topk
   const uint32_t ord = (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
   return (ord << 16) | (0xFFFFu - static_cast<uint32_t>(block));
 }
 
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+template <bool kF16>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (kF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
 }
 
 // A fragments of the 16 rows for head slot g (loaded once per chunk).
@@ -104,7 +116,7 @@ __device__ __forceinline__ void load_afrags(const TopkSmem& sm, AFrags<G>& f, in
 }
 
 // Scores of key group [kb0, kb0+8) for the CTA's 16 rows into keys[][col0..col0+8).
-template <int G>
+template <int G, bool kF16>
 __device__ __forceinline__ void score_group(const TopkParams& p, TopkSmem& sm, const AFrags<G>& f, int b, int h,
                                             int kb0, int col0, int lane) {
   const int gr = lane >> 2, gq = lane & 3;
@@ -127,7 +139,7 @@ __device__ __forceinline__ void score_group(const TopkParams& p, TopkSmem& sm, c
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
       if (G <= 4) {
-        mma_bf16_16816(d, f.a[G <= 4 ? g : 0][ks], w[2 * ks], w[2 * ks + 1]);
+        mma_16816<kF16>(d, f.a[G <= 4 ? g : 0][ks], w[2 * ks], w[2 * ks + 1]);
       } else {
         const int gr = lane >> 2, gc = gq * 2;
         uint32_t a[4];
@@ -135,11 +147,11 @@ __device__ __forceinline__ void score_group(const TopkParams& p, TopkSmem& sm, c
         a[1] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr + 8][ks * 16 + gc]);
         a[2] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr][ks * 16 + gc + 8]);
         a[3] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr + 8][ks * 16 + gc + 8]);
-        mma_bf16_16816(d, a, w[2 * ks], w[2 * ks + 1]);
+        mma_16816<kF16>(d, a, w[2 * ks], w[2 * ks + 1]);
       }
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) tacc[e] += round_bf16(d[e]);
+    for (int e = 0; e < 4; ++e) tacc[e] += Act<kF16>::round(d[e]);
   }
   const float fg = static_cast<float>(G);
   const int gc = gq * 2;
@@ -148,7 +160,7 @@ __device__ __forceinline__ void score_group(const TopkParams& p, TopkSmem& sm, c
     const int r = gr + (e >= 2 ? 8 : 0);
     const int c = gc + (e & 1);
     const int kb = kb0 + c;
-    sm.keys[r][col0 + c] = kb < p.nb ? order_key(__fdiv_rn(tacc[e], fg), kb) : 0u;
+    sm.keys[r][col0 + c] = kb < p.nb ? order_key<kF16>(__fdiv_rn(tacc[e], fg), kb) : 0u;
   }
 }
 
@@ -175,7 +187,7 @@ __device__ __forceinline__ uint32_t kth_largest(const uint32_t (&v)[NV], int K) 
   return lo;
 }
 
-template <int G>
+template <int G, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   TopkSmem& sm = *reinterpret_cast<TopkSmem*>(smem_raw);
@@ -188,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   for (int e = threadIdx.x; e < G * kRows * 64; e += kThreads) {
     const int g = e / (kRows * 64), r = (e / 64) % kRows, kk = e % 64;
     const int i = i0 + r;
-    __nv_bfloat16 val = __float2bfloat16(0.f);
+    uint16_t val = 0;  // +0 in both types
     if (i < p.nb) val = p.q_cmp[((static_cast<size_t>(b) * p.nb + i) * p.Hq + g * p.Hk + h) * 64 + perm_d(kk)];
     sm.qs[g][r][kk] = val;
   }
@@ -201,7 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     {
       AFrags<G> f;
       load_afrags<G>(sm, f, lane);
-      for (int grp = warp; grp * 8 < width; grp += kWarps) score_group<G>(p, sm, f, b, h, c0 + grp * 8, grp * 8, lane);
+      for (int grp = warp; grp * 8 < width; grp += kWarps)
+        score_group<G, kF16>(p, sm, f, b, h, c0 + grp * 8, grp * 8, lane);
     }
     __syncthreads();
 
@@ -250,14 +263,14 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   }
 }
 
-template <int G>
+template <int G, bool kF16>
 int launch_g(const TopkParams& p, cudaStream_t stream, bool overlap) {
   const size_t smem = sizeof(TopkSmem);
   static bool attr_done[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOSAIC_ERR_CUDA;
   if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(topk_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+    if (cudaFuncSetAttribute(topk_kernel<G, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return MOSAIC_ERR_CUDA;
     attr_done[dev] = true;
@@ -272,7 +285,7 @@ int launch_g(const TopkParams& p, cudaStream_t stream, bool overlap) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, topk_kernel<G>, p) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, topk_kernel<G, kF16>, p) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
 }  // namespace
@@ -282,8 +295,8 @@ int launch_topk(const TopkLaunch& a, cudaStream_t stream) {
   // kernel (topk_tc.cu) wins; below, this one's 16-row CTAs fill the GPU better.
   if (a.B > 0 && a.nb >= kTcMinBlocks && topk_tc_supported(a)) return launch_topk_tc(a, stream);
   TopkParams p;
-  p.q_cmp = static_cast<const __nv_bfloat16*>(a.q_cmp);
-  p.k_cmp = static_cast<const __nv_bfloat16*>(a.k_cmp);
+  p.q_cmp = static_cast<const uint16_t*>(a.q_cmp);
+  p.k_cmp = static_cast<const uint16_t*>(a.k_cmp);
   p.idx = a.idx;
   p.B = a.B;
   p.nb = a.nb;
@@ -292,11 +305,15 @@ int launch_topk(const TopkLaunch& a, cudaStream_t stream) {
   p.K = a.K;
   p.G = a.Hq / a.Hk;
   if (p.K > kMaxK || p.K > p.nb || p.nb > 65535) return MOSAIC_ERR_UNSUPPORTED;
-  switch (p.G) {
-    case 1: return launch_g<1>(p, stream, a.overlap_previous);
-    case 2: return launch_g<2>(p, stream, a.overlap_previous);
-    case 4: return launch_g<4>(p, stream, a.overlap_previous);
-    case 8: return launch_g<8>(p, stream, a.overlap_previous);
+  switch (p.G * 2 + (a.f16 ? 1 : 0)) {
+    case 2: return launch_g<1, false>(p, stream, a.overlap_previous);
+    case 3: return launch_g<1, true>(p, stream, a.overlap_previous);
+    case 4: return launch_g<2, false>(p, stream, a.overlap_previous);
+    case 5: return launch_g<2, true>(p, stream, a.overlap_previous);
+    case 8: return launch_g<4, false>(p, stream, a.overlap_previous);
+    case 9: return launch_g<4, true>(p, stream, a.overlap_previous);
+    case 16: return launch_g<8, false>(p, stream, a.overlap_previous);
+    case 17: return launch_g<8, true>(p, stream, a.overlap_previous);
     default: return MOSAIC_ERR_UNSUPPORTED;
   }
 }

@@ -3,10 +3,11 @@
 // 232 GFLOP at Nside 256).
 //
 // Same arithmetic as topk.cu and the reference attn_topk (primitives.py:35-51):
-// S_j = q_cmp[:, :, j] . k_cmp[:, :, j // G]^T in fp32, rounded to bf16; the mean
-// over the STRIDED head group j = g*Hk + h (fp32 sum of the rounded scores, divided
-// by G, rounded to bf16); the K largest per row with ties to the lower block index
-// (32-bit keys: order-preserving bf16 bits << 16 | 65535 - block).
+// S_j = q_cmp[:, :, j] . k_cmp[:, :, j // G]^T in fp32, rounded to the activation
+// type (bf16, or fp16 under the reference's fp16 autocast); the mean over the
+// STRIDED head group j = g*Hk + h (fp32 sum of the rounded scores, divided by G,
+// rounded again); the K largest per row with ties to the lower block index
+// (32-bit keys: order-preserving 16-bit float bits << 16 | 65535 - block).
 //
 // One CTA = 128 query blocks (one M = 128 MMA tile) of one (b, h). Keys stream in
 // tiles of 64 blocks: TMA brings the G kv-head rows of the tile, one elected lane
@@ -77,8 +78,9 @@ struct TopkTcSmem {
 constexpr size_t kTcSmemBytes =
     1024 + kMaxGTc * 2 * kBox + kStagesTc * kMaxGTc * kBox + sizeof(TopkTcSmem);
 
+template <bool kF16>
 __device__ __forceinline__ uint32_t order_key_tc(float t, int block) {
-  uint32_t u = __bfloat16_as_ushort(__float2bfloat16_rn(t));
+  uint32_t u = Act<kF16>::bits(t);
   if (u == 0x8000u) u = 0;  // -0 ties with +0, as in torch.topk
   const uint32_t ord = (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
   return (ord << 16) | (0xFFFFu - static_cast<uint32_t>(block));
@@ -107,7 +109,7 @@ __device__ __forceinline__ bool wait_noabort_tc(uint64_t* bar, uint32_t parity, 
   return bounded_wait(bar, parity, &dummy, status);
 }
 
-template <int KP, int G>
+template <int KP, int G, bool kF16>
 __global__ void __launch_bounds__(kThreadsTc, 1) topk_tc_kernel(const __grid_constant__ TopkTcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -181,7 +183,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) topk_tc_kernel(const __grid_con
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    const uint32_t idesc = make_idesc_bf16(128, kKeysTc, false);
+    const uint32_t idesc = make_idesc(128, kKeysTc, false, Act<kF16>::kMmaFmt);
     const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK);
     bool ok = warp_wait(&sm.q_full, 0, abort_flag, p.status);
     tc_fence_after();
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) topk_tc_kernel(const __grid_con
         if (g + 1 < G) tmem_ld32(tS + 64u * (g + 1), nxt);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float r = __bfloat162float(__float2bfloat16_rn(__uint_as_float(cur[j])));
+          const float r = Act<kF16>::round(__uint_as_float(cur[j]));
           tsum[j] = g == 0 ? r : tsum[j] + r;
         }
         if (g + 1 < G) {
@@ -271,7 +273,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) topk_tc_kernel(const __grid_con
       uint32_t mask = 0;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        keys[j] = order_key_tc(tsum[j] * kInvG, key0 + j);
+        keys[j] = order_key_tc<kF16>(tsum[j] * kInvG, key0 + j);
         const bool take = live && key0 + j < p.nb && keys[j] > thr;
         mask |= static_cast<uint32_t>(take) << j;
       }
@@ -320,13 +322,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) topk_tc_kernel(const __grid_con
   }
 }
 
-template <int KP, int G>
+template <int KP, int G, bool kF16>
 int launch_kp(const TopkTcParams& p, const TopkLaunch& a, cudaStream_t stream) {
   static bool attr_done[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOSAIC_ERR_CUDA;
   if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(topk_tc_kernel<KP, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(topk_tc_kernel<KP, G, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kTcSmemBytes)) != cudaSuccess)
       return MOSAIC_ERR_CUDA;
     attr_done[dev] = true;
@@ -341,18 +343,24 @@ int launch_kp(const TopkTcParams& p, const TopkLaunch& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.overlap_previous ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, topk_tc_kernel<KP, G>, p) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, topk_tc_kernel<KP, G, kF16>, p) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
-template <int G>
+template <int G, bool kF16>
 int launch_g(const TopkTcParams& p, const TopkLaunch& a, cudaStream_t stream) {
   switch ((a.K + 7) / 8) {
-    case 1: return launch_kp<8, G>(p, a, stream);
-    case 2: return launch_kp<16, G>(p, a, stream);
-    case 3: return launch_kp<24, G>(p, a, stream);
-    case 4: return launch_kp<32, G>(p, a, stream);
+    case 1: return launch_kp<8, G, kF16>(p, a, stream);
+    case 2: return launch_kp<16, G, kF16>(p, a, stream);
+    case 3: return launch_kp<24, G, kF16>(p, a, stream);
+    case 4: return launch_kp<32, G, kF16>(p, a, stream);
     default: return MOSAIC_ERR_UNSUPPORTED;
   }
+}
+
+template <bool kF16>
+int launch_typed(const TopkTcParams& p, const TopkLaunch& a, cudaStream_t stream) {
+  return p.G == 4 ? launch_g<4, kF16>(p, a, stream)
+                  : p.G == 2 ? launch_g<2, kF16>(p, a, stream) : launch_g<1, kF16>(p, a, stream);
 }
 
 }  // namespace
@@ -365,8 +373,8 @@ bool topk_tc_supported(const TopkLaunch& a) {
 int launch_topk_tc(const TopkLaunch& a, cudaStream_t stream) {
   TopkTcParams p;
   memset(&p, 0, sizeof(p));
-  if (make_tmap_bf16_2d(&p.tm_q, a.q_cmp, static_cast<uint64_t>(a.B) * a.nb, static_cast<uint64_t>(a.Hq) * 64) ||
-      make_tmap_bf16_2d(&p.tm_k, a.k_cmp, static_cast<uint64_t>(a.B) * a.nb, static_cast<uint64_t>(a.Hk) * 64))
+  if (make_tmap_2d(&p.tm_q, a.q_cmp, static_cast<uint64_t>(a.B) * a.nb, static_cast<uint64_t>(a.Hq) * 64, a.f16) ||
+      make_tmap_2d(&p.tm_k, a.k_cmp, static_cast<uint64_t>(a.B) * a.nb, static_cast<uint64_t>(a.Hk) * 64, a.f16))
     return MOSAIC_ERR_CUDA;
   p.idx = a.idx;
   p.status = a.status;
@@ -376,7 +384,7 @@ int launch_topk_tc(const TopkLaunch& a, cudaStream_t stream) {
   p.Hk = a.Hk;
   p.K = a.K;
   p.G = a.Hq / a.Hk;
-  return p.G == 4 ? launch_g<4>(p, a, stream) : p.G == 2 ? launch_g<2>(p, a, stream) : launch_g<1>(p, a, stream);
+  return a.f16 ? launch_typed<true>(p, a, stream) : launch_typed<false>(p, a, stream);
 }
 
 }  // namespace mosaic

@@ -4,9 +4,10 @@ Same call signature and semantics as ops.mosaic_sparse_attn (ops.py:557-566):
 q [B, N, Hq, D], k/v [B, N, Hk, D], block_indices int64 [B, N // block_size, Hk, K];
 query n of q head j attends to the K*block_size keys of blocks
 block_indices[b, n // block_size, j // (Hq // Hk), :] of kv head j // (Hq // Hk)
-with softmax scale `softmax_scale` (default D ** -0.5). Like the reference
-kernel (ops.py:92,115-116) the arithmetic is bf16 with fp32 accumulation
-whatever the input dtype; the result is returned in q's dtype (ops.py:538).
+with softmax scale `softmax_scale` (default D ** -0.5). The tensor-core operands
+are fp16 when q is fp16 (the reference's dtype under fp16 autocast) and bf16
+otherwise (like the reference kernel, which casts to bf16, ops.py:92,115-116),
+always with fp32 accumulation; the result is returned in q's dtype (ops.py:538).
 
 The work runs in `mosaic_sparse_attn_fwd` (and, for gradients,
 `mosaic_sparse_attn_bwd`) of libmosaic_b200.so on the current CUDA stream.
@@ -45,6 +46,21 @@ def _bf16(t):
     return t.contiguous()
 
 
+def act_dtype(t):
+    """The 16-bit type a forward call computes in: fp16 when `t` (q) is fp16, else bf16."""
+    return torch.float16 if t.dtype == torch.float16 else torch.bfloat16
+
+
+def dtype_code(dt):
+    """The C ABI's code (MOSAIC_DTYPE_*) for an activation type from act_dtype."""
+    return _lib.MOSAIC_DTYPE_F16 if dt == torch.float16 else _lib.MOSAIC_DTYPE_BF16
+
+
+def _act(t, dt):
+    t = t if t.dtype == dt else t.to(dt)
+    return t.contiguous()
+
+
 def _check_qkv(q, k, v):
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise ValueError("q, k, v must be [batch, seq_len, heads, head_dim]")
@@ -77,20 +93,23 @@ def _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse, sta
     if block_indices.dim() != 4 or tuple(block_indices.shape[:3]) != (B, N // block_size, Hk):
         raise ValueError(f"block_indices must be [B, N // block_size, Hk, K], got {tuple(block_indices.shape)}")
     lib = _lib.load()
-    qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
+    dt = act_dtype(q)
+    qb, kb, vb = _act(q, dt), _act(k, dt), _act(v, dt)
     idx = block_indices.to(torch.int64).contiguous()
-    out = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=q.device)
+    out = torch.empty(B, N, Hq, D, dtype=dt, device=q.device)
     lse = torch.empty(B, N, Hq, dtype=torch.float32, device=q.device) if want_lse else None
     with torch.cuda.device(q.device):
         rc = lib.mosaic_sparse_attn_fwd(
             _ptr(qb), _ptr(kb), _ptr(vb), _ptr(idx), _ptr(out), _ptr(lse), _ptr(status),
-            B, N, Hq, Hk, D, int(block_size), int(idx.shape[-1]), float(softmax_scale), _stream_ptr(q.device))
+            B, N, Hq, Hk, D, int(block_size), int(idx.shape[-1]), float(softmax_scale), dtype_code(dt),
+            _stream_ptr(q.device))
     _lib.check("mosaic_sparse_attn_fwd", rc)
     return out, lse
 
 
 def mosaic_attn_fwd(q, k, v, block_indices, block_size, softmax_scale, status=None):
-    """ops.mosaic_attn_fwd (ops.py:137-176): (output bf16, lse fp32 [B, N, Hq] in log2 units)."""
+    """ops.mosaic_attn_fwd (ops.py:137-176): (output in the activation type of q (fp16 or
+    bf16), lse fp32 [B, N, Hq] in log2 units)."""
     return _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=True, status=status)
 
 

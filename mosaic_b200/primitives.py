@@ -21,7 +21,7 @@ import ctypes
 import torch
 
 from . import _lib
-from .ops import _bf16, _check_qkv, _ptr, _require_cuda, _stream_ptr, mosaic_sparse_attn
+from .ops import _act, _check_qkv, _ptr, _require_cuda, _stream_ptr, act_dtype, dtype_code, mosaic_sparse_attn
 
 __all__ = ["mosaic_attn_func", "attn_topk", "block_attention", "block_pool", "cmp_attention", "bsa_attend",
            "mosaic_sparse_attn"]
@@ -29,7 +29,7 @@ __all__ = ["mosaic_attn_func", "attn_topk", "block_attention", "block_pool", "cm
 COMBINE_GATED, COMBINE_NO_CMP, COMBINE_NO_SLC = 0, 1, 2
 
 
-def _gates(weight_ba_cmp_slc, B, N, Hq):
+def _gates(weight_ba_cmp_slc, B, N, Hq, dt):
     w = weight_ba_cmp_slc
     if w.dim() == 5:
         if w.shape[-1] != 1:
@@ -37,7 +37,7 @@ def _gates(weight_ba_cmp_slc, B, N, Hq):
         w = w[..., 0]
     if tuple(w.shape) != (3, B, N, Hq):
         raise ValueError(f"weight_ba_cmp_slc must be [3, {B}, {N}, {Hq}, 1], got {tuple(weight_ba_cmp_slc.shape)}")
-    return _bf16(w)
+    return _act(w, dt)
 
 
 def mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_size, sparse_block_count,
@@ -51,6 +51,9 @@ def mosaic_attn_func(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_block_s
       o_slc = attention over the sparse_block_count blocks of highest pooled score.
     `block_attn_only` returns o_ba; `no_compression` drops o_cmp and renormalises
     (w0, w2); sparse_block_count == 0 drops o_slc and renormalises (w0, w1).
+    fp16 inputs (the reference's dtype under fp16 autocast) run natively in fp16,
+    with the pooled means and the top-k scores rounded to fp16 as the reference's
+    attn_topk does then; other dtypes run in bf16. The result has q's dtype.
     Under torch.compile the call becomes the opaque custom op
     torch.ops.mosaic_b200.attn_func (see torch_ops.py).
     """
@@ -74,11 +77,12 @@ def _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_
     Hk = k.shape[2]
     out_dtype = q.dtype
     lib = _lib.load()
-    qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
+    dt = act_dtype(q)
+    qb, kb, vb = _act(q, dt), _act(k, dt), _act(v, dt)
     gates = None
     if not block_attn_only:
         _require_cuda(weight_ba_cmp_slc)
-        gates = _gates(weight_ba_cmp_slc, B, N, Hq)
+        gates = _gates(weight_ba_cmp_slc, B, N, Hq, dt)
     cos = sin = None
     if rope_tables is not None:
         cos, sin = rope_tables
@@ -91,7 +95,7 @@ def _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_
     K = 0 if block_attn_only else int(sparse_block_count)
     if not block_attn_only and K > N // bs:
         raise ValueError(f"sparse_block_count {K} exceeds the number of blocks {N // bs}")
-    out = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=q.device)
+    out = torch.empty(B, N, Hq, D, dtype=dt, device=q.device)
     want_idx = return_block_indices and not block_attn_only and K > 0
     idx = torch.empty(B, N // bs, Hk, K, dtype=torch.int64, device=q.device) if want_idx else None
     ws_bytes = lib.mosaic_bsa_workspace_bytes(B, N, Hq, Hk, D, bs, K, int(cos is not None))
@@ -115,6 +119,7 @@ def _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_
     args.block_attn_only = int(bool(block_attn_only))
     args.no_compression = int(bool(no_compression))
     args.softmax_scale = float(D ** -0.5)
+    args.dtype = dtype_code(dt)
     with torch.cuda.device(q.device):
         rc = lib.mosaic_bsa_fwd(ctypes.byref(args), _stream_ptr(q.device))
     _lib.check("mosaic_bsa_fwd", rc)
@@ -124,7 +129,8 @@ def _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_
 
 @torch.no_grad()
 def attn_topk(q, k, block_count):
-    """Top-k block selection on pooled q/k (primitives.py:35-51): int64 [B, nb, Hk, K]."""
+    """Top-k block selection on pooled q/k (primitives.py:35-51): int64 [B, nb, Hk, K].
+    Scores are rounded to fp16 for fp16 inputs and to bf16 otherwise."""
     _require_cuda(q, k)
     B, nb, Hq, D = q.shape
     Hk = k.shape[2]
@@ -133,10 +139,11 @@ def attn_topk(q, k, block_count):
     if block_count > nb:
         raise ValueError(f"block_count {block_count} exceeds the number of blocks {nb}")
     lib = _lib.load()
-    qb, kb = _bf16(q), _bf16(k)
+    dt = act_dtype(q)
+    qb, kb = _act(q, dt), _act(k, dt)
     idx = torch.empty(B, nb, Hk, int(block_count), dtype=torch.int64, device=q.device)
     with torch.cuda.device(q.device):
-        rc = lib.mosaic_attn_topk(_ptr(qb), _ptr(kb), _ptr(idx), B, nb, Hq, Hk, D, int(block_count),
+        rc = lib.mosaic_attn_topk(_ptr(qb), _ptr(kb), _ptr(idx), B, nb, Hq, Hk, D, int(block_count), dtype_code(dt),
                                   _stream_ptr(q.device))
     _lib.check("mosaic_attn_topk", rc)
     return idx
@@ -151,11 +158,12 @@ def block_attention(q, k, v, block_size, status=None):
     if N % block_size != 0:
         raise ValueError(f"seq_len {N} is not a multiple of block_size {block_size}")
     lib = _lib.load()
-    qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
-    out = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=q.device)
+    dt = act_dtype(q)
+    qb, kb, vb = _act(q, dt), _act(k, dt), _act(v, dt)
+    out = torch.empty(B, N, Hq, D, dtype=dt, device=q.device)
     with torch.cuda.device(q.device):
         rc = lib.mosaic_block_attn_fwd(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(out), _ptr(status), B, N, Hq, Hk, D,
-                                       int(block_size), float(D ** -0.5), _stream_ptr(q.device))
+                                       int(block_size), float(D ** -0.5), dtype_code(dt), _stream_ptr(q.device))
     _lib.check("mosaic_block_attn_fwd", rc)
     return out.to(q.dtype)
 
@@ -172,11 +180,12 @@ def block_pool(q, k, v, block_size, rope_tables=None):
         raise ValueError(f"seq_len {N} is not a multiple of block_size {block_size}")
     nb = N // block_size
     lib = _lib.load()
-    qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
+    dt = act_dtype(q)
+    qb, kb, vb = _act(q, dt), _act(k, dt), _act(v, dt)
     dev = q.device
-    q_cmp = torch.empty(B, nb, Hq, D, dtype=torch.bfloat16, device=dev)
-    k_cmp = torch.empty(B, nb, Hk, D, dtype=torch.bfloat16, device=dev)
-    v_cmp = torch.empty(B, nb, Hk, D, dtype=torch.bfloat16, device=dev)
+    q_cmp = torch.empty(B, nb, Hq, D, dtype=dt, device=dev)
+    k_cmp = torch.empty(B, nb, Hk, D, dtype=dt, device=dev)
+    v_cmp = torch.empty(B, nb, Hk, D, dtype=dt, device=dev)
     cos = sin = q_rot = k_rot = None
     if rope_tables is not None:
         cos, sin = (t.float().contiguous() for t in rope_tables)
@@ -185,7 +194,7 @@ def block_pool(q, k, v, block_size, rope_tables=None):
     with torch.cuda.device(dev):
         rc = lib.mosaic_block_pool(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(cos), _ptr(sin), _ptr(q_rot), _ptr(k_rot),
                                    _ptr(q_cmp), _ptr(k_cmp), _ptr(v_cmp), B, N, Hq, Hk, D, int(block_size),
-                                   _stream_ptr(dev))
+                                   dtype_code(dt), _stream_ptr(dev))
     _lib.check("mosaic_block_pool", rc)
     if rope_tables is not None:
         return q_cmp, k_cmp, v_cmp, q_rot, k_rot
@@ -199,11 +208,12 @@ def cmp_attention(q_cmp, k_cmp, v_cmp, status=None):
     B, nb, Hq, D = q_cmp.shape
     Hk = k_cmp.shape[2]
     lib = _lib.load()
-    qb, kb, vb = _bf16(q_cmp), _bf16(k_cmp), _bf16(v_cmp)
-    out = torch.empty(B, nb, Hq, D, dtype=torch.bfloat16, device=q_cmp.device)
+    dt = act_dtype(q_cmp)
+    qb, kb, vb = _act(q_cmp, dt), _act(k_cmp, dt), _act(v_cmp, dt)
+    out = torch.empty(B, nb, Hq, D, dtype=dt, device=q_cmp.device)
     with torch.cuda.device(q_cmp.device):
         rc = lib.mosaic_cmp_attn_fwd(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(out), _ptr(status), B, nb, Hq, Hk, D,
-                                     float(D ** -0.5), _stream_ptr(q_cmp.device))
+                                     float(D ** -0.5), dtype_code(dt), _stream_ptr(q_cmp.device))
     _lib.check("mosaic_cmp_attn_fwd", rc)
     return out.to(q_cmp.dtype)
 
@@ -218,15 +228,16 @@ def bsa_attend(q, k, v, block_indices, weight_ba_cmp_slc, o_cmp, block_attn_size
     B, N, Hq, D = q.shape
     Hk = k.shape[2]
     lib = _lib.load()
-    qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
-    gates = _gates(weight_ba_cmp_slc, B, N, Hq)
+    dt = act_dtype(q)
+    qb, kb, vb = _act(q, dt), _act(k, dt), _act(v, dt)
+    gates = _gates(weight_ba_cmp_slc, B, N, Hq, dt)
     idx = block_indices.to(torch.int64).contiguous() if block_indices is not None else None
-    oc = _bf16(o_cmp) if o_cmp is not None else None
-    out = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=q.device)
+    oc = _act(o_cmp, dt) if o_cmp is not None else None
+    out = torch.empty(B, N, Hq, D, dtype=dt, device=q.device)
     with torch.cuda.device(q.device):
         rc = lib.mosaic_bsa_attend_fwd(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(idx), _ptr(gates), _ptr(oc), _ptr(out),
                                        _ptr(status), B, N, Hq, Hk, D, int(block_attn_size), int(sparse_block_size),
-                                       int(sparse_block_count), int(combine), float(D ** -0.5),
+                                       int(sparse_block_count), int(combine), float(D ** -0.5), dtype_code(dt),
                                        _stream_ptr(q.device))
     _lib.check("mosaic_bsa_attend_fwd", rc)
     return out.to(q.dtype)

@@ -81,11 +81,11 @@ FAKE = ctypes.c_void_p(0x10000)  # 16-byte aligned, never dereferenced: validati
 
 def _sparse(**kw):
     a = dict(q=FAKE, k=FAKE, v=FAKE, idx=FAKE, out=FAKE, lse=None, status=None, B=1, N=1024, Hq=8, Hk=2, D=64,
-             bs=64, K=4, scale=0.0)
+             bs=64, K=4, scale=0.0, dtype=_lib.MOSAIC_DTYPE_BF16)
     a.update(kw)
     return _lib.load().mosaic_sparse_attn_fwd(a["q"], a["k"], a["v"], a["idx"], a["out"], a["lse"], a["status"],
                                              a["B"], a["N"], a["Hq"], a["Hk"], a["D"], a["bs"], a["K"],
-                                             a["scale"], None)
+                                             a["scale"], a["dtype"], None)
 
 
 @pytest.mark.parametrize("kw,code", [
@@ -99,6 +99,7 @@ def _sparse(**kw):
     (dict(N=1000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),         # N % bs
     (dict(K=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(B=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
+    (dict(dtype=2), _lib.MOSAIC_ERR_INVALID_ARGUMENT),        # neither bf16 nor fp16
 ])
 def test_sparse_attn_rejects_bad_arguments(kw, code):
     assert _sparse(**kw) == code
@@ -129,6 +130,7 @@ def _bsa(**kw):
     (dict(workspace_bytes=16), _lib.MOSAIC_ERR_WORKSPACE),
     (dict(rope_cos=0x10000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),         # cos without sin
     (dict(head_dim=32), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(dtype=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
 ])
 def test_bsa_rejects_bad_arguments(kw, code):
     assert _bsa(**kw) == code
@@ -140,9 +142,11 @@ def test_bsa_null_args():
 
 def test_topk_rejects_bad_arguments():
     lib = _lib.load()
-    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 49, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
-    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 129, None) != _lib.MOSAIC_OK
-    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 0, None) == _lib.MOSAIC_OK
+    bf16, f16 = _lib.MOSAIC_DTYPE_BF16, _lib.MOSAIC_DTYPE_F16
+    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 49, bf16, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 129, f16, None) != _lib.MOSAIC_OK
+    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 0, f16, None) == _lib.MOSAIC_OK
+    assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 8, 7, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
 
 
 def _sparse_bwd(**kw):

@@ -52,11 +52,15 @@ def test_sparse_attention_matches_reference_triton_kernel(ref, cfg):
     assert (lse - r_lse).abs().max().item() < 3e-2
 
 
-@pytest.mark.parametrize("cfg", [(1, 3072, 4, 1, 1024, 64, 8), (1, 49152, 12, 3, 1024, 64, 24),
-                                 (2, 12288, 16, 4, 1024, 128, 12)])
+@pytest.mark.parametrize("cfg", [(1, 3072, 4, 1, 1024, 64, 8, torch.bfloat16),
+                                 (1, 49152, 12, 3, 1024, 64, 24, torch.bfloat16),
+                                 (2, 12288, 16, 4, 1024, 128, 12, torch.bfloat16),
+                                 # fp16, the reference rollout's dtype: its attn_topk then scores in fp16
+                                 (1, 3072, 4, 1, 1024, 64, 8, torch.float16),
+                                 (1, 49152, 12, 3, 1024, 64, 24, torch.float16)])
 def test_mosaic_attn_func_matches_reference_gpu_path(ref, cfg):
-    B, N, Hq, Hk, bas, bs, K = cfg
-    x = O.make_inputs(B, N, Hq, Hk, seed=N + bs, rope=True)
+    B, N, Hq, Hk, bas, bs, K, dtype = cfg
+    x = O.make_inputs(B, N, Hq, Hk, seed=N + bs, dtype=dtype, rope=True)
     q, k, v, w = (t.to(DEV) for t in (x["q"], x["k"], x["v"], x["w"]))
     r_out = ref.primitives.mosaic_attn_func(q, k, v, w, bas, bs, K, False)
     out, idx = M.mosaic_attn_func(q, k, v, w, bas, bs, K, False, return_block_indices=True)
@@ -66,4 +70,5 @@ def test_mosaic_attn_func_matches_reference_gpu_path(ref, cfg):
     same = (torch.sort(r_idx, -1).values == torch.sort(idx, -1).values).all(-1).all(-1)  # [B, nb]
     assert same.float().mean().item() > 0.9, "selections differ on more than a tenth of the query blocks"
     rows = same.repeat_interleave(bs, dim=1)  # [B, N]
+    assert out.dtype == r_out.dtype == dtype
     close(out[rows], r_out[rows])
