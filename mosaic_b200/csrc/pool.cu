@@ -12,11 +12,12 @@
 // Layout: a block of bs rows is a contiguous bs x (H*128 B) slab per tensor, and one
 // head of one row is 128 contiguous bytes. A work unit is one (batch, block, head of
 // q, k or v) and belongs to one warp: lane l owns the 16-byte chunk l % 8 of the head
-// and the rows l / 8, l / 8 + 4, ... of the block, issues all sixteen 16-byte loads
-// of a 64-row batch before it adds any (every lane keeps 256 bytes in flight, every
-// warp instruction touches four full 128-byte lines), and the four row groups meet
-// through two shuffles. No shared memory and no block barrier, so the grid is just
-// enough warps for every unit and the GPU's warp slots stay full of loads.
+// and the rows l / 8, l / 8 + 4, ... of the block, loads a 64-row batch as sixteen
+// 16-byte loads (every warp instruction touches four full 128-byte lines), and the
+// four row groups meet through two shuffles. The warps are persistent: while a warp
+// adds one batch, the sixteen loads of its next batch (the next unit's, at the end
+// of a block) are already in flight, so every lane keeps 256 bytes outstanding all
+// the time. No shared memory and no block barrier.
 // Rows past the end of a block (block sizes that are not multiples of 64) are
 // skipped. HBM-bound: every input byte is read exactly once.
 #include "kernels.h"
@@ -77,78 +78,131 @@ __device__ __forceinline__ void add_chunk(float (&acc)[8], uint4 x) {
   }
 }
 
-template <bool kF16, bool kRope>
-__global__ void __launch_bounds__(kWarpsPerCta * 32) pool_kernel(const PoolParams p) {
-  using A = Act<kF16>;
-  const long long u = static_cast<long long>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
-  if (u >= p.units) return;
-  const int lane = threadIdx.x & 31;
-  const int c = lane & 7, rg = lane >> 3;
+// One work unit of the warp: which tensor, head and block, and where its rows are.
+struct UnitRef {
+  const uint4* src;
+  uint4* rot;
+  uint4* dst;
+  size_t base, pitch, out;  // 16-byte chunk indices (of this lane's chunk c) and the row pitch
+  int row0;
+  bool rotate;
+};
+
+template <bool kRope>
+__device__ __forceinline__ UnitRef unit_ref(const PoolParams& p, long long u, int c) {
+  UnitRef r;
   const int slot = static_cast<int>(u % p.slots);
   const long long bb = u / p.slots;  // b * nb + blk
   const int blk = static_cast<int>(bb % p.nb), b = static_cast<int>(bb / p.nb);
-
-  const uint4* src;
-  uint4* rot = nullptr;
-  uint4* dst;
   int H, h;
+  r.rot = nullptr;
   if (slot < p.nq) {
-    src = p.q; rot = p.q_rot; dst = p.q_cmp; H = p.Hq; h = slot;
+    r.src = p.q; r.rot = p.q_rot; r.dst = p.q_cmp; H = p.Hq; h = slot;
   } else if (slot < p.nq + p.Hk) {
-    src = p.k; rot = p.k_rot; dst = p.k_cmp; H = p.Hk; h = slot - p.nq;
+    r.src = p.k; r.rot = p.k_rot; r.dst = p.k_cmp; H = p.Hk; h = slot - p.nq;
   } else {
-    src = p.v; dst = p.v_cmp; H = p.Hk; h = slot - p.nq - p.Hk;
+    r.src = p.v; r.dst = p.v_cmp; H = p.Hk; h = slot - p.nq - p.Hk;
   }
-  const bool rotate = kRope && slot < p.nq + p.Hk;
-  const int row0 = blk * p.bs;
-  // 16-byte chunk index of (b, row0, h, c); a row is H * 8 chunks
-  const size_t base = (static_cast<size_t>(b) * p.N + row0) * H * 8 + static_cast<size_t>(h) * 8 + c;
-  const size_t pitch = static_cast<size_t>(H) * 8;
+  r.rotate = kRope && slot < p.nq + p.Hk;
+  r.row0 = blk * p.bs;
+  r.pitch = static_cast<size_t>(H) * 8;
+  r.base = (static_cast<size_t>(b) * p.N + r.row0) * r.pitch + static_cast<size_t>(h) * 8 + c;
+  r.out = (static_cast<size_t>(b) * p.nb + blk) * r.pitch + static_cast<size_t>(h) * 8 + c;
+  return r;
+}
 
+// Issues the loads of rows r0 + rg + 4 i (i < 16) of a unit.
+__device__ __forceinline__ void load_batch(uint4 (&x)[kRowsPerBatch / 4], const UnitRef& r, int r0, int rg, int bs) {
+#pragma unroll
+  for (int i = 0; i < kRowsPerBatch / 4; ++i) {
+    const int row = r0 + rg + 4 * i;
+    x[i] = row < bs ? __ldg(r.src + r.base + static_cast<size_t>(row) * r.pitch) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Persistent warps: warp w of the grid takes units w, w + warps, ... and keeps the
+// next 64-row batch's sixteen 16-byte loads in flight while it adds the current one.
+template <bool kF16, bool kRope>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) pool_kernel(const PoolParams p) {
+  using A = Act<kF16>;
+  const long long warps = static_cast<long long>(gridDim.x) * kWarpsPerCta;
+  long long u = static_cast<long long>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  if (u >= p.units) return;
+  const int lane = threadIdx.x & 31;
+  const int c = lane & 7, rg = lane >> 3;
+  UnitRef cur = unit_ref<kRope>(p, u, c);
+  int r0 = 0;
+  uint4 x[kRowsPerBatch / 4], nx[kRowsPerBatch / 4];
+  load_batch(x, cur, 0, rg, p.bs);
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-  for (int r0 = 0; r0 < p.bs; r0 += kRowsPerBatch) {
-    uint4 x[kRowsPerBatch / 4];
-#pragma unroll
-    for (int i = 0; i < kRowsPerBatch / 4; ++i) {
-      const int r = r0 + rg + 4 * i;
-      x[i] = r < p.bs ? __ldg(src + base + static_cast<size_t>(r) * pitch) : make_uint4(0, 0, 0, 0);
+  while (true) {
+    // the batch after this one: the rest of this block, else the warp's next unit
+    long long nu = u;
+    int nr0 = r0 + kRowsPerBatch;
+    if (nr0 >= p.bs) {
+      nu = u + warps;
+      nr0 = 0;
     }
+    const bool more = nu < p.units;
+    UnitRef nxt = more ? unit_ref<kRope>(p, nu, c) : cur;
+    if (more) load_batch(nx, nxt, nr0, rg, p.bs);
 #pragma unroll
     for (int i = 0; i < kRowsPerBatch / 4; ++i) {
       uint4 xv = x[i];
       const int r = r0 + rg + 4 * i;
       if (r >= p.bs) continue;
-      if (rotate) {
-        const size_t n = static_cast<size_t>(row0 + r);
+      if (cur.rotate) {
+        const size_t n = static_cast<size_t>(cur.row0 + r);
         xv = rope_chunk<kF16>(xv, p.cos + n * 32, p.sin + n * 32, c * 4);
-        rot[base + static_cast<size_t>(r) * pitch] = xv;
+        cur.rot[cur.base + static_cast<size_t>(r) * cur.pitch] = xv;
       }
       add_chunk<kF16>(acc, xv);
     }
-  }
-  // the four row groups (lanes c, c+8, c+16, c+24) meet in a fixed order
+    if (nu != u || !more) {
+      // the unit is complete: the four row groups (lanes c, c+8, c+16, c+24) meet
+      // in a fixed order and lanes 0-7 write the 128-byte mean row
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 8);
-    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 16);
-  }
-  if (rg == 0 && dst != nullptr) {
-    const float n = static_cast<float>(p.bs);
-    uint4 o;
-    o.x = A::pack(__fdiv_rn(acc[0], n), __fdiv_rn(acc[1], n));
-    o.y = A::pack(__fdiv_rn(acc[2], n), __fdiv_rn(acc[3], n));
-    o.z = A::pack(__fdiv_rn(acc[4], n), __fdiv_rn(acc[5], n));
-    o.w = A::pack(__fdiv_rn(acc[6], n), __fdiv_rn(acc[7], n));
-    dst[(static_cast<size_t>(b) * p.nb + blk) * pitch + static_cast<size_t>(h) * 8 + c] = o;
+      for (int i = 0; i < 8; ++i) {
+        acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 8);
+        acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 16);
+      }
+      if (rg == 0 && cur.dst != nullptr) {
+        const float n = static_cast<float>(p.bs);
+        uint4 o;
+        o.x = A::pack(__fdiv_rn(acc[0], n), __fdiv_rn(acc[1], n));
+        o.y = A::pack(__fdiv_rn(acc[2], n), __fdiv_rn(acc[3], n));
+        o.z = A::pack(__fdiv_rn(acc[4], n), __fdiv_rn(acc[5], n));
+        o.w = A::pack(__fdiv_rn(acc[6], n), __fdiv_rn(acc[7], n));
+        cur.dst[cur.out] = o;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    }
+    if (!more) break;
+    u = nu;
+    r0 = nr0;
+    cur = nxt;
+#pragma unroll
+    for (int i = 0; i < kRowsPerBatch / 4; ++i) x[i] = nx[i];
   }
 }
 
 template <bool kF16>
 int launch_typed(const PoolParams& p, bool rope, cudaStream_t stream) {
-  const long long ctas = (p.units + kWarpsPerCta - 1) / kWarpsPerCta;
-  if (ctas > 0x7fffffffLL) return MOSAIC_ERR_UNSUPPORTED;
+  // Persistent grid: as many 4-warp CTAs as fit on the GPU at once (by registers),
+  // never more than there are units.
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  const void* fn = rope ? reinterpret_cast<const void*>(pool_kernel<kF16, true>)
+                        : reinterpret_cast<const void*>(pool_kernel<kF16, false>);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kWarpsPerCta * 32, 0) != cudaSuccess || per_sm < 1)
+    return MOSAIC_ERR_CUDA;
+  const long long need = (p.units + kWarpsPerCta - 1) / kWarpsPerCta;
+  const long long ctas = need < static_cast<long long>(sms) * per_sm ? need : static_cast<long long>(sms) * per_sm;
   if (rope)
     pool_kernel<kF16, true><<<static_cast<unsigned>(ctas), kWarpsPerCta * 32, 0, stream>>>(p);
   else

@@ -22,9 +22,11 @@
 //   A) scores of the chunk -> shared memory (mma.sync m16n8k16; each warp owns
 //      whole 8-key column groups for all G heads, so the strided-group mean needs
 //      no cross-warp reduction);
-//   B) warp r owns row r: it finds the K-th largest key among the chunk and its
-//      running top list by a binary search on the key value (warp reductions),
-//      keeps the keys >= that one, and sorts them descending.
+//   B) warp r owns row r: the keys of the chunk and its running top list reach a
+//      threshold (the K-th largest of the lanes' maxima) that every top-K key
+//      clears; the few that do are ranked against each other (K <= 32). Otherwise
+//      a binary search on the key value (warp reductions) finds the K-th largest,
+//      keeps the keys >= it and sorts them.
 // The work is tiny (0.9 GFLOP of scores at Nside 64); the kernel is latency-bound,
 // so the point of this layout is to keep many independent loads and warps in flight.
 #include "kernels.h"
@@ -95,17 +97,18 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 // A fragments of the 16 rows for head slot g (loaded once per chunk).
 // For G > 4 the fragments would not fit the register budget next to the B
 // fragments, so they are cached for G <= 4 only.
+constexpr int kCachedG = 4;
 template <int G>
 struct AFrags {
-  uint32_t a[G <= 4 ? G : 1][4][4];
+  uint32_t a[G <= kCachedG ? G : 1][4][4];
 };
 
 template <int G>
 __device__ __forceinline__ void load_afrags(const TopkSmem& sm, AFrags<G>& f, int lane) {
-  if (G > 4) return;
+  if (G > kCachedG) return;
   const int gr = lane >> 2, gc = (lane & 3) * 2;
 #pragma unroll
-  for (int g = 0; g < (G <= 4 ? G : 1); ++g)
+  for (int g = 0; g < (G <= kCachedG ? G : 1); ++g)
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
       f.a[g][ks][0] = *reinterpret_cast<const uint32_t*>(&sm.qs[g][gr][ks * 16 + gc]);
@@ -138,8 +141,8 @@ __device__ __forceinline__ void score_group(const TopkParams& p, TopkSmem& sm, c
     float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
-      if (G <= 4) {
-        mma_16816<kF16>(d, f.a[G <= 4 ? g : 0][ks], w[2 * ks], w[2 * ks + 1]);
+      if (G <= kCachedG) {
+        mma_16816<kF16>(d, f.a[G <= kCachedG ? g : 0][ks], w[2 * ks], w[2 * ks + 1]);
       } else {
         const int gr = lane >> 2, gc = gq * 2;
         uint32_t a[4];
@@ -187,6 +190,47 @@ __device__ __forceinline__ uint32_t kth_largest(const uint32_t (&v)[NV], int K) 
   return lo;
 }
 
+// Warp-wide exact top-K (K <= 32) of the distinct candidate keys in registers, written
+// to top[0..K) sorted descending; returns false (nothing written) when the shortcut
+// does not apply and the caller must take the binary search. Every key of the top K
+// is at least theta = the K-th largest of the 32 lanes' maxima (the K lanes with the
+// largest maxima hold at least K keys >= theta), and on score-like data only a few
+// dozen keys reach theta: they are compacted into buf and each one's rank is the
+// number of larger candidates. Costs ~4 instructions per candidate instead of the
+// search's 32 passes over all of them.
+template <int NV>
+__device__ __forceinline__ bool topk_by_threshold(const uint32_t (&v)[NV], int K, uint32_t* buf, uint32_t* top,
+                                                  int lane) {
+  constexpr int kCap = kMaxK;  // buf entries
+  if (K > 32) return false;
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) m = max(m, v[i]);
+  int above = 0;  // lanes whose maximum is larger than this lane's
+#pragma unroll
+  for (int j = 0; j < 32; ++j) above += __shfl_sync(0xffffffffu, m, j) > m ? 1 : 0;
+  const uint32_t theta = __reduce_min_sync(0xffffffffu, above < K ? m : 0xFFFFFFFFu);
+  int base = 0;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const bool keep = v[i] >= theta && v[i] != 0u;
+    const unsigned bal = __ballot_sync(0xffffffffu, keep);
+    const int at = base + __popc(bal & ((1u << lane) - 1u));
+    if (keep && at < kCap) buf[at] = v[i];
+    base += __popc(bal);
+  }
+  if (base > kCap || base < K) return false;  // warp-uniform
+  __syncwarp();
+  for (int e = lane; e < base; e += 32) {
+    const uint32_t x = buf[e];
+    int rank = 0;
+    for (int j = 0; j < base; ++j) rank += buf[j] > x ? 1 : 0;
+    if (rank < K) top[rank] = x;
+  }
+  __syncwarp();
+  return true;
+}
+
 template <int G, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -230,24 +274,26 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
       const int e = lane + 32 * i;
       v[i] = e < width ? row[e] : (e - width < count ? top[e - width] : 0u);
     }
-    const uint32_t kth = kth_largest<NV>(v, K);
-    // keep the keys >= kth (exactly K of them) in an unsorted buffer ...
     uint32_t* buf = sm.buf[warp];
-    int base = 0;
+    if (!topk_by_threshold<NV>(v, K, buf, top, lane)) {
+      const uint32_t kth = kth_largest<NV>(v, K);
+      // keep the keys >= kth (exactly K of them) in an unsorted buffer ...
+      int base = 0;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const bool keep = v[i] >= kth && v[i] != 0u;
-      const unsigned bal = __ballot_sync(0xffffffffu, keep);
-      if (keep) buf[base + __popc(bal & ((1u << lane) - 1u))] = v[i];
-      base += __popc(bal);
-    }
-    __syncwarp();
-    // ... and write them to the top list sorted descending (rank = number of larger keys)
-    for (int e = lane; e < K; e += 32) {
-      const uint32_t x = buf[e];
-      int rank = 0;
-      for (int j = 0; j < K; ++j) rank += buf[j] > x ? 1 : 0;
-      top[rank] = x;
+      for (int i = 0; i < NV; ++i) {
+        const bool keep = v[i] >= kth && v[i] != 0u;
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) buf[base + __popc(bal & ((1u << lane) - 1u))] = v[i];
+        base += __popc(bal);
+      }
+      __syncwarp();
+      // ... and write them to the top list sorted descending (rank = number of larger keys)
+      for (int e = lane; e < K; e += 32) {
+        const uint32_t x = buf[e];
+        int rank = 0;
+        for (int j = 0; j < K; ++j) rank += buf[j] > x ? 1 : 0;
+        top[rank] = x;
+      }
     }
     count = K;
     __syncthreads();
