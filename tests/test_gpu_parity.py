@@ -328,11 +328,15 @@ def test_sharp_softmax(q_gain):
     torch.cuda.synchronize()
     assert mops.check_status(status) == 0
     ref = O.mosaic_attn_func(q, x["k"], x["v"], x["w"], 1024, 64, 8, False, block_indices=idx.cpu())
-    # Sharp rows make outputs close to single v rows (|out| up to ~4), where storing the
-    # output in bf16 alone costs 2^-8 relative: the bound is relative to the output's
-    # largest magnitude, as for the layer tests.
+    # Known deviation from the absolute max-abs 2e-2: sharp rows make outputs close to
+    # single v rows (|out| up to ~6), where the bf16 rounding of P (applied in P*V but
+    # not in the row sum, as in the reference kernel) and of the output each cost up to
+    # 2^-9 of |out|. Measured on B200: max-abs 0.0205 / 0.0195 at q x4 / x8 (mean
+    # 6.4e-4 / 8.8e-4); the reference's own GPU path gives 0.028 / 0.049 on the same
+    # inputs (test_gpu_reference_kernel.py compares the two). The max bound is therefore
+    # relative to the output's largest magnitude; the mean bound stays absolute.
     m = ref.abs().max().item()
-    close(out, ref, max_abs=2e-2 * m, mean_abs=2e-3 * m)
+    close(out, ref, max_abs=2e-2 * m, mean_abs=2e-3)
 
 
 def test_score_spike_forces_exact_path():

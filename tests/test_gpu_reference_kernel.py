@@ -72,3 +72,25 @@ def test_mosaic_attn_func_matches_reference_gpu_path(ref, cfg):
     rows = same.repeat_interleave(bs, dim=1)  # [B, N]
     assert out.dtype == r_out.dtype == dtype
     close(out[rows], r_out[rows])
+
+
+@pytest.mark.parametrize("q_gain", [4.0, 8.0])
+def test_sharp_softmax_at_least_as_accurate_as_reference_gpu_path(ref, q_gain):
+    """Sharp rows (q scaled so outputs approach single v rows, |out| up to ~6): against the
+    fp32 oracle the reference's own GPU path (flash-attn + its Triton kernel) reaches
+    max-abs 0.028 / 0.049 at q x4 / x8 on these inputs, above the 2e-2 north-star bound;
+    ours must stay within the mean bound and no worse than the reference's maximum."""
+    B, N, Hq, Hk = 1, 3072, 8, 2
+    x = O.make_inputs(B, N, Hq, Hk, seed=23, rope=False)
+    q = (x["q"].float() * q_gain).bfloat16()
+    qd, kd, vd, wd = (t.to(DEV) for t in (q, x["k"], x["v"], x["w"]))
+    out, idx = M.mosaic_attn_func(qd, kd, vd, wd, 1024, 64, 8, False, return_block_indices=True)
+    r_out = ref.primitives.mosaic_attn_func(qd, kd, vd, wd, 1024, 64, 8, False)
+    qc, kc = O.pool_mean(q, 64), O.pool_mean(x["k"], 64)
+    r_idx = ref.primitives.attn_topk(qc.to(DEV), kc.to(DEV), 8).cpu()
+    d = (out.float().cpu() - O.mosaic_attn_func(q, x["k"], x["v"], x["w"], 1024, 64, 8, False,
+                                                block_indices=idx.cpu())).abs()
+    dr = (r_out.float().cpu() - O.mosaic_attn_func(q, x["k"], x["v"], x["w"], 1024, 64, 8, False,
+                                                   block_indices=r_idx)).abs()
+    assert d.mean().item() <= MEAN_ABS
+    assert d.max().item() <= dr.max().item(), (d.max().item(), dr.max().item())
