@@ -2,15 +2,17 @@
 
 The reference is an unpackaged Python project: `pip install --target baseline/_ref`
 refuses it (it has neither setup.py nor pyproject.toml). Its install here is
-therefore a verbatim copy of the three module files the attention path imports
-(ops.py with the Triton kernels, primitives.py, utils.py) into baseline/_ref,
-which git ignores and which travels with the source tree to the GPU box.
-`install(src_dir)` makes that copy; nothing of it is committed or edited.
+therefore a verbatim copy of the module files the attention path and the model
+import (ops.py with the Triton kernels, primitives.py, utils.py, mosaic.py with the
+U-Net) into baseline/_ref, which git ignores and which travels with the source tree
+to the GPU box. `install(src_dir)` makes that copy; nothing of it is committed or
+edited.
 
 `load()` imports the copies. Two bindings are set at load time, both outside the
 reference files:
   * `healpy` (absent from the image) is a stub module: only
-    utils.get_healpix_grid uses it, and the attention path never calls that;
+    utils.get_healpix_grid uses it; the attention path never calls that, and
+    `build_model` rebinds it to mosaic_b200.healpix's restatement;
   * the reference's Triton autotuner is bypassed: its config list includes
     q_tile_size = 128, which with 64-token blocks makes tiles_per_block zero and
     divides by it (ops.py:54-55), so every launch here goes to the kernel's JIT
@@ -30,7 +32,7 @@ import types
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_DIR = os.path.join(HERE, "_ref")
-FILES = ("ops.py", "primitives.py", "utils.py")
+FILES = ("ops.py", "primitives.py", "utils.py", "mosaic.py")
 
 
 def install(src_dir):
@@ -51,8 +53,8 @@ def available():
 class Reference:
     """The loaded reference modules plus the autotuner-free launch of its forward kernel."""
 
-    def __init__(self, ops, primitives, notes):
-        self.ops, self.primitives, self.notes = ops, primitives, notes
+    def __init__(self, ops, primitives, notes, mosaic=None):
+        self.ops, self.primitives, self.notes, self.mosaic = ops, primitives, notes, mosaic
         self.config = dict(q_tile_size=64, num_warps=4, num_stages=2)
 
     def sparse_attn_fwd(self, q, k, v, block_indices, block_size, softmax_scale=None, config=None):
@@ -93,14 +95,15 @@ def load(device=None):
     """Import the installed reference modules; returns a Reference (raises if absent)."""
     if not available():
         raise FileNotFoundError("baseline/_ref does not hold the reference modules")
-    saved = {name: sys.modules.get(name) for name in ("ops", "utils", "primitives", "healpy")}
+    saved = {name: sys.modules.get(name) for name in ("ops", "utils", "primitives", "mosaic", "healpy")}
     sys.modules.setdefault("healpy", types.ModuleType("healpy"))
     sys.path.insert(0, REF_DIR)
     try:
-        for name in ("ops", "utils", "primitives"):
+        for name in ("ops", "utils", "primitives", "mosaic"):
             sys.modules.pop(name, None)
         import ops as ref_ops  # noqa: E402  (the reference's ops.py)
         import primitives as ref_prim  # noqa: E402  (the reference's primitives.py)
+        import mosaic as ref_mosaic  # noqa: E402  (the reference's mosaic.py: the U-Net)
     finally:
         sys.path.remove(REF_DIR)
         for name, mod in saved.items():
@@ -108,7 +111,7 @@ def load(device=None):
                 sys.modules.pop(name, None)
             else:
                 sys.modules[name] = mod
-    ref = Reference(ref_ops, ref_prim, [])
+    ref = Reference(ref_ops, ref_prim, [], ref_mosaic)
     ref_prim.mosaic_sparse_attn = ref.mosaic_sparse_attn
     if device is not None:
         _check_flash_attn(ref, device)
@@ -142,3 +145,65 @@ def _check_flash_attn(ref, device):
         ref.primitives.flash_attn_func = _sdpa_gqa
         ref.notes.append(f"flash_attn_func unavailable here ({str(e).splitlines()[0][:100]}); "
                          "torch SDPA with its semantics stands in")
+
+
+# ----------------------------------------------------------------------------- the U-Net
+def era5_config(mosaic):
+    """The reference's `era5` model preset (inference.py:71-88 stage / bottleneck configs,
+    inference.py:290-306 model config): 3 stages (nside 64 / 32 / 16, dims 768 / 1024 /
+    1280, 12 / 16 / 20 heads, GQA 4, 128-token blocks, top-k 24 / 12 / 4, window 1024,
+    depths 4+2 / 4+2 / 2), 82 variables x 2 history states + 3 static, 24 neighbours,
+    noise 32, no affine RMSNorm."""
+    S, Bn = mosaic.StageConfig, mosaic.BottleneckConfig
+    stages = [S(nside=64, dim=768, num_heads=12, block_attn_size=1024, sparse_block_size=128, sparse_block_count=24,
+                encoder_depth=4, decoder_depth=2, mlp_ratio=4.0, gqa_ratio=4),
+              S(nside=32, dim=1024, num_heads=16, block_attn_size=1024, sparse_block_size=128,
+                sparse_block_count=12, encoder_depth=4, decoder_depth=2, mlp_ratio=4.0, gqa_ratio=4)]
+    bottleneck = Bn(nside=16, dim=1280, num_heads=20, block_attn_size=1024, sparse_block_size=128,
+                    sparse_block_count=4, depth=2, mlp_ratio=4.0, gqa_ratio=4)
+    return mosaic.ModelConfig(
+        dim=768, num_heads=12, variables=[f"var{i}" for i in range(82)],
+        static_variables=["geopotential_at_surface", "land_sea_mask", "soil_type"], k_neighbors=24,
+        qk_norm=False, rope=True, rope_theta=10000, sparse_every=1, qkv_compress_ratio=1, num_history_steps=2,
+        noise_dim=32, rmsnorm_elementwise_affine=False, cg_stage_cfgs=stages, bottleneck_cfg=bottleneck)
+
+
+GRID_LON, GRID_LAT = 240, 121  # the 1.5-degree lat-lon grid
+
+
+def build_model(ref, device, ours=True, dtype=None, seed=0):
+    """The reference's Transformer (mosaic.py:136-336) with the era5 preset and random
+    weights (torch.manual_seed(seed), the reference's own initialisers), its static
+    fields ~ N(0, 1) on the 240 x 121 grid, on `device` in eval mode.
+
+    ours=True rebinds, before construction, the names the model resolves at build time
+    to mosaic_b200's modules: primitives.MosaicAttention (looked up by MosaicBlock),
+    mosaic.CrossAttentionInterpolate, mosaic.HEALPixDownsample and
+    mosaic.HEALPixUpsample (as INTEGRATION.md describes); ours=False restores the
+    reference's own classes. Either way the HEALPix pixel centres come from
+    mosaic_b200.healpix (the reference's utils.get_healpix_grid needs healpy, which is
+    not installed here)."""
+    import torch
+    import mosaic_b200 as M
+    from mosaic_b200.healpix import get_healpix_grid
+
+    prim, mos = ref.primitives, ref.mosaic
+    if not hasattr(ref, "_orig"):
+        ref._orig = dict(MosaicAttention=prim.MosaicAttention, CrossAttentionInterpolate=mos.CrossAttentionInterpolate,
+                         HEALPixDownsample=mos.HEALPixDownsample, HEALPixUpsample=mos.HEALPixUpsample)
+    prim.MosaicAttention = M.MosaicAttention if ours else ref._orig["MosaicAttention"]
+    for name in ("CrossAttentionInterpolate", "HEALPixDownsample", "HEALPixUpsample"):
+        setattr(mos, name, getattr(M, name) if ours else ref._orig[name])
+    mos.get_healpix_grid = get_healpix_grid
+    prim.get_healpix_grid = get_healpix_grid
+    torch.manual_seed(seed)
+    model = mos.Transformer(era5_config(mos))
+    g = torch.Generator().manual_seed(seed + 1)
+    lon = torch.linspace(0, 360, GRID_LON + 1)[:-1]
+    lat = torch.linspace(-90, 90, GRID_LAT)
+    model.initialize_static_vars(torch.randn(GRID_LON, GRID_LAT, 3, generator=g), lon, lat)
+    model = model.to(device)
+    model.initialize_interpolation(lon.to(device), lat.to(device))
+    if dtype is not None:
+        model = model.to(dtype)
+    return model.eval()

@@ -42,6 +42,12 @@ fields), as step/s with the gather's share (--no-ensemble skips it); and, on one
 selected-block kernel, its flash-attn local branch, its whole mosaic_attn_func) timed
 on the same inputs beside ours, with the output differences (--no-reference-gpu).
 
+`unet_step` (S1 default run; --no-model skips it): one 24-member forward step of the
+whole U-Net — the reference's Transformer from baseline/_ref with mosaic_b200's modules
+rebound into it, random weights, bf16 — sharded by member over the ranks with the
+output fields all-gathered over NCCL in the step, eager and replayed from one CUDA
+graph, and on one GPU beside the same model with the reference's own modules.
+
 `--impl reference` times the reference algorithm on the host cores instead: the
 reference's CPU form is the oracle port (oracle/bsa_oracle.py; the reference itself
 needs CUDA for flash-attn and Triton), run on a bounded sample of the same workload
@@ -108,6 +114,7 @@ def parse():
     p.add_argument("--no-updown", action="store_true")
     p.add_argument("--no-ensemble", action="store_true")
     p.add_argument("--no-reference-gpu", action="store_true")
+    p.add_argument("--no-model", action="store_true")
     return p.parse_args()
 
 
@@ -840,6 +847,111 @@ def ensemble_leg(dev, rank, world, dist, stream, steps, warmup):
             "attention_tflops_per_gpu": flop * m / ((step_ms - gather_ms) / 1000) / 1e12}
 
 
+UNET_TFLOP_PER_MEMBER = 11.45  # FlopCounterMode on the reference model at the era5 preset, one member
+
+
+def model_leg(dev, rank, world, dist, stream, steps, warmup):
+    """One 24-member forward step of the whole Mosaic U-Net: the reference's own
+    Transformer (mosaic.py, era5 preset, random weights, from baseline/_ref) with
+    mosaic_b200's attention block, interpolation and resampling modules rebound into it
+    (INTEGRATION.md), bf16. Members are sharded over the ranks (num_noise_samples =
+    24 / N each, the model's own member batching, mosaic.py:300-308) and the output
+    fields [1, members, 240, 121, 82] are all-gathered over NCCL inside the timed step.
+    Also: the same step captured in one CUDA graph (forward only; replayed, then the
+    gather), and on one GPU the model with the reference's own modules (flash-attn, its
+    Triton kernel, torch ops) on the same weights and inputs, with the output difference."""
+    from baseline import reference as R
+
+    if not R.available():
+        return {"unavailable": "baseline/_ref is empty (the reference checkout was absent when build() ran)"}
+    from mosaic_b200 import ensemble as E
+
+    ref = R.load(dev)
+    lo, hi = E.member_range(MEMBERS, rank, world)
+    m = hi - lo
+    model = R.build_model(ref, dev, ours=True, dtype=torch.bfloat16, seed=0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(1, 1, 2, R.GRID_LON, R.GRID_LAT, 82, generator=g, device=dev).bfloat16()
+    dyt = torch.rand(1, 1, 2, generator=g, device=dev).bfloat16()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+
+    def gather(out):
+        return E.gather_members(out, MEMBERS, dim=1) if dist is not None else out
+
+    res = {"what": "one 24-member forward step of the whole Mosaic U-Net (the reference's Transformer, era5 "
+                   "preset, random weights, bf16) with mosaic_b200's attention, interpolation and resampling "
+                   "modules; members sharded over ranks, output fields all-gathered over NCCL in the step",
+           "members": MEMBERS, "members_per_rank": m, "steps": steps}
+    with torch.no_grad():
+        first = model(x, dyt, m)
+        for _ in range(warmup):
+            gather(model(x, dyt, m))
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(steps):
+            out = model(x, dyt, m)
+            evs[i][0].record(stream)
+            full = gather(out)
+            evs[i][1].record(stream)
+        b.record(stream)
+        torch.cuda.synchronize()
+        step_ms = a.elapsed_time(b) / steps
+        gather_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+        assert full.shape[1] == MEMBERS
+        # the forward captured in one CUDA graph (its noise generator registered, so every
+        # replay draws new noise), replayed, then the gather
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                model(x, dyt, m)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        graph.register_generator_state(model.noise_generator.generator)
+        with torch.cuda.graph(graph):
+            g_out = model(x, dyt, m)
+        for _ in range(warmup):
+            graph.replay()
+            gather(g_out)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        a.record(stream)
+        for _ in range(steps):
+            graph.replay()
+            gather(g_out)
+        b.record(stream)
+        torch.cuda.synchronize()
+        graph_ms = a.elapsed_time(b) / steps
+        del graph
+    if dist is not None:
+        t = torch.tensor([step_ms, gather_ms, graph_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, gather_ms, graph_ms = (float(v) for v in t.tolist())
+        dist.barrier()
+    res.update(step_ms=step_ms, step_per_s=1000.0 / step_ms, gather_ms=gather_ms, gather_share=gather_ms / step_ms,
+               graph_step_ms=graph_ms, graph_step_per_s=1000.0 / graph_ms,
+               tflop_per_step=UNET_TFLOP_PER_MEMBER * MEMBERS,
+               achieved_tflops_per_gpu=UNET_TFLOP_PER_MEMBER * m / (step_ms / 1000))
+    if world == 1:
+        ref_model = R.build_model(ref, dev, ours=False, dtype=torch.bfloat16, seed=0)
+        with torch.no_grad():
+            r_first = ref_model(x, dyt, m)  # same weights, same noise (both generators seeded 42, first draw)
+            d = (r_first.float() - first.float())
+            ref_ms = _timed(lambda: ref_model(x, dyt, m), stream, max(2, steps - 1), 1)
+        res.update(reference_modules_step_ms=ref_ms, speedup_vs_reference_modules=ref_ms / step_ms,
+                   rel_l2_vs_reference_modules=float(d.norm() / r_first.float().norm()),
+                   max_abs_vs_reference_modules=float(d.abs().max()),
+                   mean_abs_vs_reference_modules=float(d.abs().mean()), reference_notes=ref.notes)
+        del ref_model
+    del model
+    torch.cuda.empty_cache()
+    return res
+
+
 def b200_arm(args):
     from mosaic_b200 import _lib
     import mosaic_b200 as M
@@ -957,9 +1069,11 @@ def b200_arm(args):
         f16 = fp16_leg(c, sets, stream, max(3, min(args.steps, 50)), max(3, args.warmup))
         if "nside" in c:
             rope = rope_leg(c, sets, stream, max(3, min(args.steps, 50)), max(3, args.warmup))
-    ens = None
+    ens = unet = None
     if not args.no_ensemble and name == "S1":
         ens = ensemble_leg(dev, rank, world, dist, stream, steps=max(2, min(args.steps, 4)), warmup=1)
+    if not args.no_model and name == "S1":
+        unet = model_leg(dev, rank, world, dist, stream, steps=3, warmup=1)
     ref_gpu = None
     if not args.no_reference_gpu and rank == 0 and world == 1 and name in ("S1", "S1_bs128"):
         ref_gpu = reference_gpu_leg(c, sets[0], stream, reps=max(3, min(args.steps, 20)), warmup=2)
@@ -1035,6 +1149,8 @@ def b200_arm(args):
         line["rope_placement"] = rope
     if ens is not None:
         line["ensemble"] = ens
+    if unet is not None:
+        line["unet_step"] = unet
     if ref_gpu is not None:
         line["reference_gpu"] = ref_gpu
     if sdpa is not None:

@@ -264,23 +264,20 @@ MOSAIC_API int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, c
  * [out_dim, factor * in_dim] bf16 (proj_x.weight), pos_bias [n, out_dim] bf16 (the
  * static proj_pos(rel_pos)), norm_weight [out_dim] fp32 or NULL (no affine), eps the
  * RMSNorm epsilon. The projection output and the bias sum are rounded to bf16 as the
- * reference's bf16 layers do; the norm is fp32. ss_workspace: n_coarse * batch floats
- * (cleared here). in_dim a multiple of 64, out_dim a multiple of 128. */
+ * reference's bf16 layers do; the norm is fp32 over the stored bf16 row (a
+ * deterministic sum). in_dim a multiple of 64, out_dim a multiple of 128. */
 MOSAIC_API int mosaic_healpix_downsample(const void* x, const void* w_x, const void* pos_bias,
-                                         const float* norm_weight, void* out, float* ss_workspace, int* status,
-                                         int n_coarse, int factor, int batch, int in_dim, int out_dim, float eps,
-                                         void* stream);
+                                         const float* norm_weight, void* out, int* status, int n_coarse, int factor,
+                                         int batch, int in_dim, int out_dim, float eps, void* stream);
 
 /* HEALPixUpsample.forward (primitives.py:352-357) for x [n, batch, in_dim] bf16: out
  * [(n f), batch, out_dim] bf16 = RMSNorm(rearrange(x w_x^T + pos_bias[n],
  * 'n b (f d) -> (n f) b d') + shortcut) with w_x [factor * out_dim, in_dim] bf16,
  * pos_bias [n, factor * out_dim] bf16, shortcut [(n f), batch, out_dim] bf16 or NULL
- * (out may be the shortcut's buffer), norm_weight and eps as for the downsample.
- * ss_workspace: n_coarse * factor * batch floats (cleared here). */
+ * (out may be the shortcut's buffer), norm_weight and eps as for the downsample. */
 MOSAIC_API int mosaic_healpix_upsample(const void* x, const void* shortcut, const void* w_x, const void* pos_bias,
-                                       const float* norm_weight, void* out, float* ss_workspace, int* status,
-                                       int n_coarse, int factor, int batch, int in_dim, int out_dim, float eps,
-                                       void* stream);
+                                       const float* norm_weight, void* out, int* status, int n_coarse, int factor,
+                                       int batch, int in_dim, int out_dim, float eps, void* stream);
 
 #ifdef __cplusplus
 }

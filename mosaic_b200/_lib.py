@@ -62,8 +62,8 @@ SIGNATURES = {
     "mosaic_row_rms": ([_vp, _vp, _i, _i, _f, _vp], _i),
     "mosaic_interp_attend": ([_vp] * 6 + [_i] * 6 + [_f, _vp], _i),
     "mosaic_interp_attend_tiled": ([_vp] * 11 + [_i] * 8 + [_f, _vp], _i),
-    "mosaic_healpix_downsample": ([_vp] * 7 + [_i] * 5 + [_f, _vp], _i),
-    "mosaic_healpix_upsample": ([_vp] * 8 + [_i] * 5 + [_f, _vp], _i),
+    "mosaic_healpix_downsample": ([_vp] * 6 + [_i] * 5 + [_f, _vp], _i),
+    "mosaic_healpix_upsample": ([_vp] * 7 + [_i] * 5 + [_f, _vp], _i),
 }
 
 EXPECTED_ABI_VERSION = 2

@@ -132,10 +132,27 @@ class MosaicAttention(nn.Module):
         self.to_strategy_combine_mlp = None if block_attn_only else nn.Linear(dim, 3 * q_heads, bias=False)
 
     def _w_qkvg(self):
+        """cat(to_q, to_k, to_v[, gate]) weights in bf16, rebuilt only when a weight changes
+        (another tensor, or an in-place update, which bumps its version counter)."""
         ws = [self.to_q.weight, self.to_k.weight, self.to_v.weight]
         if self.to_strategy_combine_mlp is not None:
             ws.append(self.to_strategy_combine_mlp.weight)
-        return torch.cat([w.to(torch.bfloat16) for w in ws], dim=0)
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        if getattr(self, "_w_qkvg_key", None) != key:
+            self._w_qkvg_cache = torch.cat([w.detach().to(torch.bfloat16) for w in ws], dim=0)
+            self._w_qkvg_key = key
+        return self._w_qkvg_cache
+
+    def _check_rope_tables(self):
+        """q_rope and k_rope must hold the same tables (the projection epilogue applies one
+        pair to both); compared once per version of the tables, so that the forward is
+        free of host synchronisation afterwards (and can be captured in a CUDA graph)."""
+        ts = (self.q_rope.cos_freqs, self.q_rope.sin_freqs, self.k_rope.cos_freqs, self.k_rope.sin_freqs)
+        key = tuple((t.data_ptr(), t._version) for t in ts)
+        if getattr(self, "_rope_key", None) != key:
+            if not (torch.equal(ts[0], ts[2]) and torch.equal(ts[1], ts[3])):
+                raise ValueError("q_rope and k_rope must hold the same tables (both come from the same grid)")
+            self._rope_key = key
 
     def forward(self, x):
         if torch.is_grad_enabled() and (x.requires_grad or any(p_.requires_grad for p_ in self.parameters())):
@@ -145,9 +162,8 @@ class MosaicAttention(nn.Module):
         rope = self.q_rope is not None
         if rope and self.q_rope.cos_freqs is None:
             raise ValueError("RoPE tables not initialised (call q_rope/k_rope.initialize_rope)")
-        if rope and not (torch.equal(self.q_rope.cos_freqs, self.k_rope.cos_freqs)
-                         and torch.equal(self.q_rope.sin_freqs, self.k_rope.sin_freqs)):
-            raise ValueError("q_rope and k_rope must hold the same tables (both come from the same grid)")
+        if rope:
+            self._check_rope_tables()
         with_gates = not self.block_attn_only
         q, k, v, g = qkv_projection(
             x, self._w_qkvg(), self.q_heads, self.kv_heads,

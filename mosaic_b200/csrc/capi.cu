@@ -563,12 +563,12 @@ int mosaic_interp_attend_tiled(const void* kv, float* kw_workspace, const int* t
 }
 
 static int check_updown(const void* x, const void* w_x, const void* pos_bias, const float* norm_weight, void* out,
-                        float* ss_workspace, int n_coarse, int factor, int batch, int in_dim, int out_dim, float eps) {
+                        int n_coarse, int factor, int batch, int in_dim, int out_dim, float eps) {
   if (n_coarse < 0 || factor < 1 || batch < 0 || in_dim <= 0 || out_dim <= 0 || !(eps >= 0.f))
     return MOSAIC_ERR_INVALID_ARGUMENT;
   if (in_dim % 64 != 0 || out_dim % 128 != 0) return MOSAIC_ERR_UNSUPPORTED;
   if (n_coarse == 0 || batch == 0) return MOSAIC_OK;
-  if (!x || !w_x || !pos_bias || !out || !ss_workspace) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!x || !w_x || !pos_bias || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(x) || !aligned16(w_x) || !aligned16(pos_bias) || !aligned16(out) ||
       (norm_weight != nullptr && !aligned16(norm_weight)))
     return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -576,29 +576,27 @@ static int check_updown(const void* x, const void* w_x, const void* pos_bias, co
 }
 
 int mosaic_healpix_downsample(const void* x, const void* w_x, const void* pos_bias, const float* norm_weight,
-                              void* out, float* ss_workspace, int* status, int n_coarse, int factor, int batch,
-                              int in_dim, int out_dim, float eps, void* stream) {
-  const int rc = check_updown(x, w_x, pos_bias, norm_weight, out, ss_workspace, n_coarse, factor, batch, in_dim,
-                              out_dim, eps);
+                              void* out, int* status, int n_coarse, int factor, int batch, int in_dim, int out_dim,
+                              float eps, void* stream) {
+  const int rc = check_updown(x, w_x, pos_bias, norm_weight, out, n_coarse, factor, batch, in_dim, out_dim, eps);
   if (rc >= 0) return rc;
   UpDownLaunch l;
   std::memset(&l, 0, sizeof(l));
-  l.x = x; l.w = w_x; l.pos = pos_bias; l.norm_w = norm_weight; l.out = out; l.ss = ss_workspace;
+  l.x = x; l.w = w_x; l.pos = pos_bias; l.norm_w = norm_weight; l.out = out;
   l.status = status; l.n = n_coarse; l.F = factor; l.B = batch; l.c_in = in_dim; l.c_out = out_dim; l.eps = eps;
   return launch_healpix_down(l, static_cast<cudaStream_t>(stream));
 }
 
 int mosaic_healpix_upsample(const void* x, const void* shortcut, const void* w_x, const void* pos_bias,
-                            const float* norm_weight, void* out, float* ss_workspace, int* status, int n_coarse,
-                            int factor, int batch, int in_dim, int out_dim, float eps, void* stream) {
-  const int rc = check_updown(x, w_x, pos_bias, norm_weight, out, ss_workspace, n_coarse, factor, batch, in_dim,
-                              out_dim, eps);
+                            const float* norm_weight, void* out, int* status, int n_coarse, int factor, int batch,
+                            int in_dim, int out_dim, float eps, void* stream) {
+  const int rc = check_updown(x, w_x, pos_bias, norm_weight, out, n_coarse, factor, batch, in_dim, out_dim, eps);
   if (rc >= 0) return rc;
   if (shortcut != nullptr && !aligned16(shortcut)) return MOSAIC_ERR_INVALID_ARGUMENT;
   UpDownLaunch l;
   std::memset(&l, 0, sizeof(l));
   l.x = x; l.shortcut = shortcut; l.w = w_x; l.pos = pos_bias; l.norm_w = norm_weight; l.out = out;
-  l.ss = ss_workspace; l.status = status; l.n = n_coarse; l.F = factor; l.B = batch; l.c_in = in_dim;
+  l.status = status; l.n = n_coarse; l.F = factor; l.B = batch; l.c_in = in_dim;
   l.c_out = out_dim; l.eps = eps;
   return launch_healpix_up(l, static_cast<cudaStream_t>(stream));
 }

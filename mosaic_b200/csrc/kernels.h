@@ -164,7 +164,6 @@ struct UpDownLaunch {
   const void* pos;       // down: [n, c_out]; up: [n, F c_out] bf16 (proj_pos(rel_pos))
   const float* norm_w;   // [c_out] fp32 or null
   void* out;             // down: [n, B, c_out]; up: [(n f), B, c_out] bf16
-  float* ss;             // [output rows] fp32 scratch
   int* status;
   int n, F, B, c_in, c_out;
   float eps;

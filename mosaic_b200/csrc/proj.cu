@@ -22,13 +22,15 @@
 //                read straight from x [(n f), B, c] through a 3D tensor map (the
 //                rearrange '(n f) b c -> n b (f c)' is addressing); the epilogue rounds
 //                proj_x's output to bf16, adds the bf16 proj_pos(rel_pos) row of n,
-//                rounds, stores row (n, b) and adds its sum of squares to ss[n B + b].
+//                rounds and stores row (n, b).
 //   mode kUp:    HEALPixUpsample (primitives.py:352-357): A = x [n, B, c_in] rows (n, b),
 //                output column j = (f, d); the epilogue adds the bias row, then the
 //                shortcut, rounding after each add as the reference's bf16 ops do, and
 //                stores row ((n f), b) (the rearrange 'n b (f d) -> (n f) b d').
-//                RMSNorm then runs as rms_apply_kernel over the stored rows with the
-//                accumulated sums of squares (the norm spans several column tiles).
+//                RMSNorm then runs as rms_apply_kernel over the stored rows (the norm
+//                spans several column tiles): one warp per row sums the squares of the
+//                stored bf16 values in a fixed order, so the result is deterministic
+//                and equals RMSNorm of the bf16 tensor the reference normalises.
 //
 // Tiles of 128 rows x 256 columns, K in 64-wide stages (TMA, 128-byte swizzle, 4-stage
 // ring), fp32 accumulators double-buffered in TMEM so the epilogue of one tile runs
@@ -65,7 +67,6 @@ struct ProjParams {
   const float* rscale;     // kLinear: per-row factor or null
   const __nv_bfloat16* pos;       // kDown / kUp: [n, N] bias rows
   const __nv_bfloat16* shortcut;  // kUp: [(n f), B, out_dim] or null
-  float* ss;                      // kDown / kUp: sum of squares per stored row
   int F, out_dim, member, c_blocks;
   int a3d;                        // A is the 3D map (c, f, n) of kDown
   int* status;
@@ -142,11 +143,10 @@ __device__ __forceinline__ void load_chunk_res(uint32_t (&pw)[16], uint32_t (&sw
 }
 
 // 32 output columns of one row for kDown / kUp: y = bf16(bf16(acc) + pos) (+ shortcut,
-// rounded again) packed as bf16; returns the sum of y^2 (fp32) for the row's RMSNorm.
-__device__ __forceinline__ float pack_chunk_res(uint32_t (&packed)[16], const uint32_t (&acc)[32],
-                                                const uint32_t (&pw)[16], const uint32_t (&sw)[16], bool has_sc) {
+// rounded again) packed as bf16.
+__device__ __forceinline__ void pack_chunk_res(uint32_t (&packed)[16], const uint32_t (&acc)[32],
+                                               const uint32_t (&pw)[16], const uint32_t (&sw)[16], bool has_sc) {
   const bool sc = has_sc;
-  float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
@@ -156,21 +156,32 @@ __device__ __forceinline__ float pack_chunk_res(uint32_t (&packed)[16], const ui
       x0 = bf16_round(x0 + __uint_as_float(sw[i] << 16));
       x1 = bf16_round(x1 + __uint_as_float(sw[i] & 0xffff0000u));
     }
-    ss = fmaf(x0, x0, fmaf(x1, x1, ss));
     packed[i] = pack_bf16x2(x0, x1);
   }
-  return ss;
 }
 
-// RMSNorm of stored rows in place: y = bf16(y * rsqrt(ss / D + eps) (* w)), one warp per row.
-__global__ void __launch_bounds__(256) rms_apply_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ ss,
-                                                        const float* __restrict__ w, long long rows, int D,
-                                                        float eps) {
+// RMSNorm of stored rows in place: y = bf16(y * rsqrt(mean(y^2) + eps) (* w)), one warp per
+// row. The sum of squares is taken over the stored bf16 values, each lane over its
+// 16-byte chunks in order and the lanes by a fixed butterfly, so it is deterministic.
+__global__ void __launch_bounds__(256) rms_apply_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ w,
+                                                        long long rows, int D, float eps) {
   const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const float r = rsqrtf(__ldg(ss + row) / static_cast<float>(D) + eps);
   __nv_bfloat16* yr = y + row * D;
+  float ss = 0.f;
+  for (int c = lane * 8; c < D; c += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(yr + c);
+    const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = __uint_as_float(wd[i] << 16), b = __uint_as_float(wd[i] & 0xffff0000u);
+      ss = fmaf(a, a, fmaf(b, b, ss));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / static_cast<float>(D) + eps);
   for (int c = lane * 8; c < D; c += 256) {
     uint4 v = *reinterpret_cast<const uint4*>(yr + c);
     uint32_t wd[4] = {v.x, v.y, v.z, v.w};
@@ -356,7 +367,6 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           break;
         }
         tc_fence_after();
-        float ss_part = 0.f;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           if (k >= nch) break;
@@ -368,11 +378,9 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           tmem_ld_wait();
           reg_fence<32>(acc);
           uint32_t packed[16];
-          const float ss = pack_chunk_res(packed, acc, pw[k & 1], sw[k & 1], sc0 != nullptr);
-          if (live) ss_part += ss;
+          pack_chunk_res(packed, acc, pw[k & 1], sw[k & 1], sc0 != nullptr);
           warp_store_rows(stage, packed, live ? p.out + o0 + 32 * k : nullptr, lane);
         }
-        if (live && nch > 0) atomicAdd(p.ss + orow, ss_part);
         tc_fence_before();
         mbar_arrive(&sm.acc_empty[a]);
         continue;
@@ -590,19 +598,16 @@ int launch_linear(const LinearLaunch& a, cudaStream_t stream) {
   return launch_proj(p, stream);
 }
 
-int launch_rms_apply(void* y, const float* ss, const float* w, long long rows, int D, float eps,
-                     cudaStream_t stream) {
+int launch_rms_apply(void* y, const float* w, long long rows, int D, float eps, cudaStream_t stream) {
   if (rows == 0) return MOSAIC_OK;
   rms_apply_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
-      static_cast<__nv_bfloat16*>(y), ss, w, rows, D, eps);
+      static_cast<__nv_bfloat16*>(y), w, rows, D, eps);
   return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
 int launch_healpix_down(const UpDownLaunch& a, cudaStream_t stream) {
   const long long rows = static_cast<long long>(a.n) * a.B;
   if (rows == 0) return MOSAIC_OK;
-  if (cudaMemsetAsync(a.ss, 0, static_cast<size_t>(rows) * sizeof(float), stream) != cudaSuccess)
-    return MOSAIC_ERR_CUDA;
   for (int b = 0; b < a.B; ++b) {  // one GEMM per member: A = member b's children, read in place
     ProjParams p;
     memset(&p, 0, sizeof(p));
@@ -616,7 +621,6 @@ int launch_healpix_down(const UpDownLaunch& a, cudaStream_t stream) {
     p.c_blocks = a.c_in / kPBK;
     p.out = static_cast<__nv_bfloat16*>(a.out);
     p.pos = static_cast<const __nv_bfloat16*>(a.pos);
-    p.ss = a.ss;
     p.status = a.status;
     p.mode = kDown;
     p.M = a.n;
@@ -629,14 +633,12 @@ int launch_healpix_down(const UpDownLaunch& a, cudaStream_t stream) {
     const int rc = launch_proj(p, stream);
     if (rc != MOSAIC_OK) return rc;
   }
-  return launch_rms_apply(a.out, a.ss, a.norm_w, rows, a.c_out, a.eps, stream);
+  return launch_rms_apply(a.out, a.norm_w, rows, a.c_out, a.eps, stream);
 }
 
 int launch_healpix_up(const UpDownLaunch& a, cudaStream_t stream) {
   const long long rows = static_cast<long long>(a.n) * a.F * a.B;
   if (rows == 0) return MOSAIC_OK;
-  if (cudaMemsetAsync(a.ss, 0, static_cast<size_t>(rows) * sizeof(float), stream) != cudaSuccess)
-    return MOSAIC_ERR_CUDA;
   ProjParams p;
   memset(&p, 0, sizeof(p));
   if (make_tmap_bf16_2d(&p.tm_a, a.x, static_cast<uint64_t>(a.n) * a.B, static_cast<uint64_t>(a.c_in)) ||
@@ -645,7 +647,6 @@ int launch_healpix_up(const UpDownLaunch& a, cudaStream_t stream) {
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.pos = static_cast<const __nv_bfloat16*>(a.pos);
   p.shortcut = static_cast<const __nv_bfloat16*>(a.shortcut);
-  p.ss = a.ss;
   p.status = a.status;
   p.mode = kUp;
   p.M = a.n * a.B;
@@ -656,7 +657,7 @@ int launch_healpix_up(const UpDownLaunch& a, cudaStream_t stream) {
   p.out_dim = a.c_out;
   const int rc = launch_proj(p, stream);
   if (rc != MOSAIC_OK) return rc;
-  return launch_rms_apply(a.out, a.ss, a.norm_w, rows, a.c_out, a.eps, stream);
+  return launch_rms_apply(a.out, a.norm_w, rows, a.c_out, a.eps, stream);
 }
 
 int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream) {

@@ -266,14 +266,14 @@ def test_linear_and_rms_reject_bad_arguments():
 
 def _updown_call(kind, **kw):
     a = dict(x=ctypes.c_void_p(0x10000), sc=ctypes.c_void_p(0x20000), w=ctypes.c_void_p(0x30000),
-             pos=ctypes.c_void_p(0x40000), nw=None, out=ctypes.c_void_p(0x50000), ss=ctypes.c_void_p(0x60000),
+             pos=ctypes.c_void_p(0x40000), nw=None, out=ctypes.c_void_p(0x50000),
              n=192, F=4, B=1, c_in=768, c_out=1024, eps=1e-2)
     a.update(kw)
     lib = _lib.load()
     if kind == "down":
-        return lib.mosaic_healpix_downsample(a["x"], a["w"], a["pos"], a["nw"], a["out"], a["ss"], None, a["n"], a["F"],
+        return lib.mosaic_healpix_downsample(a["x"], a["w"], a["pos"], a["nw"], a["out"], None, a["n"], a["F"],
                                              a["B"], a["c_in"], a["c_out"], a["eps"], None)
-    return lib.mosaic_healpix_upsample(a["x"], a["sc"], a["w"], a["pos"], a["nw"], a["out"], a["ss"], None, a["n"],
+    return lib.mosaic_healpix_upsample(a["x"], a["sc"], a["w"], a["pos"], a["nw"], a["out"], None, a["n"],
                                        a["F"], a["B"], a["c_in"], a["c_out"], a["eps"], None)
 
 
@@ -284,7 +284,6 @@ def _updown_call(kind, **kw):
     (dict(n=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(F=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(eps=-1.0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
-    (dict(ss=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(pos=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(out=ctypes.c_void_p(0x50008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # misaligned
     (dict(n=0), _lib.MOSAIC_OK),                      # empty: nothing to do, no CUDA call

@@ -90,12 +90,11 @@ def test_upsample_without_shortcut_and_in_place():
     no_sc = U.healpix_upsample(xd, None, m.proj_x.weight, pos, 4, eps, m.norm.weight)
     close_rel(no_sc, O.healpix_upsample(x, torch.zeros_like(sc), w_x, w_pos, m.rel_pos.cpu(), eps, w_norm))
     ref = U.healpix_upsample(xd, scd, m.proj_x.weight, pos, 4, eps, m.norm.weight)
-    ss = torch.empty(sc.numel() // sc.shape[-1], dtype=torch.float32, device=DEV)
     buf = scd.clone()
     from mosaic_b200 import _lib
     from mosaic_b200.ops import _ptr, _stream_ptr
     rc = _lib.load().mosaic_healpix_upsample(_ptr(xd), _ptr(buf), _ptr(m.proj_x.weight), _ptr(pos),
-                                             _ptr(m.norm.weight.float().contiguous()), _ptr(buf), _ptr(ss), None,
+                                             _ptr(m.norm.weight.float().contiguous()), _ptr(buf), None,
                                              x.shape[0], 4, 2, 256, 128, float(eps), _stream_ptr(xd.device))
     assert rc == 0
     torch.cuda.synchronize()
