@@ -27,7 +27,11 @@ namespace mosaic {
 namespace {
 
 constexpr int kWarpsPerCta = 4;
-constexpr int kRowsPerBatch = 64;  // rows of a block per load batch (16 per lane)
+// Rows of a block per load batch: 64 (16 loads per lane), or 32 with RoPE, whose
+// rotation and rotated-copy stores need the registers (at 64 the RoPE kernel held
+// 8 warps per SM and ran at a quarter of the plain kernel's bandwidth).
+template <bool kRope>
+constexpr int rows_per_batch() { return kRope ? 32 : 64; }
 
 struct PoolParams {
   const uint4* q;
@@ -111,10 +115,11 @@ __device__ __forceinline__ UnitRef unit_ref(const PoolParams& p, long long u, in
   return r;
 }
 
-// Issues the loads of rows r0 + rg + 4 i (i < 16) of a unit.
-__device__ __forceinline__ void load_batch(uint4 (&x)[kRowsPerBatch / 4], const UnitRef& r, int r0, int rg, int bs) {
+// Issues the loads of rows r0 + rg + 4 i (i < NR / 4) of a unit.
+template <int NR>
+__device__ __forceinline__ void load_batch(uint4 (&x)[NR / 4], const UnitRef& r, int r0, int rg, int bs) {
 #pragma unroll
-  for (int i = 0; i < kRowsPerBatch / 4; ++i) {
+  for (int i = 0; i < NR / 4; ++i) {
     const int row = r0 + rg + 4 * i;
     x[i] = row < bs ? __ldg(r.src + r.base + static_cast<size_t>(row) * r.pitch) : make_uint4(0, 0, 0, 0);
   }
@@ -132,24 +137,25 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) pool_kernel(const PoolParam
   const int c = lane & 7, rg = lane >> 3;
   UnitRef cur = unit_ref<kRope>(p, u, c);
   int r0 = 0;
-  uint4 x[kRowsPerBatch / 4], nx[kRowsPerBatch / 4];
-  load_batch(x, cur, 0, rg, p.bs);
+  constexpr int NR = rows_per_batch<kRope>();
+  uint4 x[NR / 4], nx[NR / 4];
+  load_batch<NR>(x, cur, 0, rg, p.bs);
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   while (true) {
     // the batch after this one: the rest of this block, else the warp's next unit
     long long nu = u;
-    int nr0 = r0 + kRowsPerBatch;
+    int nr0 = r0 + NR;
     if (nr0 >= p.bs) {
       nu = u + warps;
       nr0 = 0;
     }
     const bool more = nu < p.units;
     UnitRef nxt = more ? unit_ref<kRope>(p, nu, c) : cur;
-    if (more) load_batch(nx, nxt, nr0, rg, p.bs);
+    if (more) load_batch<NR>(nx, nxt, nr0, rg, p.bs);
 #pragma unroll
-    for (int i = 0; i < kRowsPerBatch / 4; ++i) {
+    for (int i = 0; i < NR / 4; ++i) {
       uint4 xv = x[i];
       const int r = r0 + rg + 4 * i;
       if (r >= p.bs) continue;
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) pool_kernel(const PoolParam
     r0 = nr0;
     cur = nxt;
 #pragma unroll
-    for (int i = 0; i < kRowsPerBatch / 4; ++i) x[i] = nx[i];
+    for (int i = 0; i < NR / 4; ++i) x[i] = nx[i];
   }
 }
 
