@@ -115,6 +115,7 @@ def parse():
     p.add_argument("--no-ensemble", action="store_true")
     p.add_argument("--no-reference-gpu", action="store_true")
     p.add_argument("--no-model", action="store_true")
+    p.add_argument("--no-rollout", action="store_true")
     return p.parse_args()
 
 
@@ -952,6 +953,66 @@ def model_leg(dev, rank, world, dist, stream, steps, warmup):
     return res
 
 
+ROLLOUT_STEPS = 4
+
+
+def rollout_leg(dev, stream):
+    """The reference's autoregressive rollout (inference.py:330-390: 24 members, fp16
+    autocast over fp32 weights, state (de)normalised around each step) on its own U-Net
+    (era5 preset, random weights, synthetic normalisation statistics and initial
+    state), through mosaic_b200.rollout.unroll_direct: with mosaic_b200's modules and
+    steps 2.. replayed from one CUDA graph, the same eagerly, and the reference's
+    modules eagerly (the reference's loop). Device time of the whole rollout (CUDA
+    events on the launching stream), after one untimed 2-step rollout of each."""
+    import types
+
+    from baseline import reference as R
+    from mosaic_b200.rollout import unroll_direct
+
+    if not R.available():
+        return {"unavailable": "baseline/_ref is empty (the reference checkout was absent when build() ran)"}
+    ref = R.load(dev)
+    ours = R.build_model(ref, dev, ours=True, dtype=None, seed=0)
+    g = torch.Generator(device=dev).manual_seed(3)
+    ns = types.SimpleNamespace(state_mean=torch.randn(82, generator=g, device=dev) * 3,
+                               state_std=torch.rand(82, generator=g, device=dev) + 0.5)
+    x0 = ns.state_mean + ns.state_std * torch.randn(1, 2, R.GRID_LON, R.GRID_LAT, 82, generator=g, device=dev)
+    dyt = torch.rand(1, 2, generator=g, device=dev)
+    delta = torch.tensor([0.25, 1 / 365], device=dev)
+
+    def timed(model, graph, steps, warm=True):
+        if warm:
+            unroll_direct(model, x0, dyt, delta, ns, 2, MEMBERS, graph=graph)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        unroll_direct(model, x0, dyt, delta, ns, steps, MEMBERS, graph=graph)
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b)
+
+    T = ROLLOUT_STEPS
+    graph_ms = timed(ours, True, T)
+    graph_ms_more = timed(ours, True, T + 2, warm=False)
+    replay_ms = (graph_ms_more - graph_ms) / 2  # steady state: two more replays
+    eager_ms = timed(ours, False, T)
+    del ours
+    torch.cuda.empty_cache()
+    ref_model = R.build_model(ref, dev, ours=False, dtype=None, seed=0)
+    ref_ms = timed(ref_model, False, T)
+    del ref_model
+    torch.cuda.empty_cache()
+    return {"what": "unroll_direct (inference.py:330-390) of the reference's U-Net, 24 members, fp16 autocast "
+                    "over fp32 weights, synthetic state and normalisation statistics; ms_per_step is a graph "
+                    "replay in steady state ((rollout of T + 2 steps - rollout of T steps) / 2)",
+            "members": MEMBERS, "unroll_steps": T, "graph_replayed_steps": T - 2,
+            "rollout_ms": graph_ms, "rollout_ms_plus_2_steps": graph_ms_more, "ms_per_step": replay_ms,
+            "eager_rollout_ms": eager_ms, "eager_ms_per_step": eager_ms / T,
+            "reference_modules_rollout_ms": ref_ms, "reference_modules_ms_per_step": ref_ms / T,
+            "speedup_vs_reference_modules": (ref_ms / T) / replay_ms,
+            "capture_overhead_ms": graph_ms - 2 * eager_ms / T - (T - 2) * replay_ms}
+
+
 def b200_arm(args):
     from mosaic_b200 import _lib
     import mosaic_b200 as M
@@ -1074,6 +1135,9 @@ def b200_arm(args):
         ens = ensemble_leg(dev, rank, world, dist, stream, steps=max(2, min(args.steps, 4)), warmup=1)
     if not args.no_model and name == "S1":
         unet = model_leg(dev, rank, world, dist, stream, steps=3, warmup=1)
+    roll = None
+    if not args.no_model and not args.no_rollout and world == 1 and name == "S1":
+        roll = rollout_leg(dev, stream)
     ref_gpu = None
     if not args.no_reference_gpu and rank == 0 and world == 1 and name in ("S1", "S1_bs128"):
         ref_gpu = reference_gpu_leg(c, sets[0], stream, reps=max(3, min(args.steps, 20)), warmup=2)
@@ -1151,6 +1215,8 @@ def b200_arm(args):
         line["ensemble"] = ens
     if unet is not None:
         line["unet_step"] = unet
+    if roll is not None:
+        line["rollout"] = roll
     if ref_gpu is not None:
         line["reference_gpu"] = ref_gpu
     if sdpa is not None:

@@ -4,7 +4,12 @@
  * sizes and a cudaStream_t (passed as void*), launches asynchronously on that
  * stream, allocates nothing and synchronises nothing. Tensors are dense and
  * row-major in the reference's layouts ([batch, seq, heads, head_dim]); head_dim
- * is 64 and query heads per kv head (G) is 4. The attention entry points take a
+ * is 64. Any number of query heads per kv head (G = num_q_heads / num_kv_heads)
+ * is accepted by the attention and backward entry points; the top-k selection (and
+ * so mosaic_bsa_fwd outside block_attn_only) takes G = 1, 2, 4 or 8. The kernels
+ * work on groups of four query heads: G = 4 and 8 fill them, G = 1 and 2 leave
+ * three or two of the four head slots empty (computed on zeros, not written).
+ * The attention entry points take a
  * `dtype` (MOSAIC_DTYPE_BF16 or MOSAIC_DTYPE_F16) for all their 16-bit tensors; the
  * projection, interpolation, resampling and backward entry points are bf16.
  *
@@ -32,7 +37,7 @@ extern "C" {
 /* ---- return codes ---------------------------------------------------- */
 #define MOSAIC_OK 0
 #define MOSAIC_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, misaligned pointer */
-#define MOSAIC_ERR_UNSUPPORTED 2      /* a shape this build does not handle (head_dim != 64, G != 4, ...) */
+#define MOSAIC_ERR_UNSUPPORTED 2      /* a shape this build does not handle (head_dim != 64, top-k with G > 8, ...) */
 #define MOSAIC_ERR_WORKSPACE 3        /* workspace missing or smaller than mosaic_bsa_workspace_bytes() */
 #define MOSAIC_ERR_CUDA 4             /* a CUDA runtime / driver call failed (launch, tensor map) */
 

@@ -319,8 +319,27 @@ struct DqParams {
   int* status;
   int B, N, Hq, Hk, bs, K, nqb, nkb;
   float scale, scale_log2;
+  int ngroups;  // groups of four query heads per kv head: ceil(G / 4)
   int qtiles, units;
 };
+
+// A dq unit: (batch b, kv head h, head group grp, 64-query tile qt) with the query
+// heads h*G + 4*grp + 0..3 (slots past the group's last head are empty: their Q and
+// dO load as zeros and their dQ is not written).
+struct DqUnit {
+  int b, h, grp, qt;
+};
+
+__device__ __forceinline__ DqUnit decode_dq_unit(const DqParams& p, int u) {
+  DqUnit w;
+  w.qt = u % p.qtiles;
+  int rest = u / p.qtiles;
+  w.grp = rest % p.ngroups;
+  rest /= p.ngroups;
+  w.h = rest % p.Hk;
+  w.b = rest / p.Hk;
+  return w;
+}
 
 struct DqSmem {
   uint64_t kv_full[kStagesDq], kv_empty[kStagesDq];
@@ -387,8 +406,8 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
     int g = 0, nq = 0;  // K/V tiles and Q/dO stagings issued
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
-      const int qt = u % p.qtiles, rest = u / p.qtiles;
-      const int h = rest % p.Hk, b = rest / p.Hk;
+      const DqUnit un = decode_dq_unit(p, u);
+      const int qt = un.qt, h = un.h, b = un.b;
       const int qb = qt * 64 / p.bs;
       const int64_t* src = p.block_idx + ((static_cast<int64_t>(b) * p.nqb + qb) * p.Hk + h) * p.K;
       __syncwarp();
@@ -407,7 +426,9 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
       }
       mbar_arrive_expect_tx_elect(&sm.qs_full, 8 * kBox);
       for (int j = 0; j < 4; ++j) {
-        const int col = (h * G + j) * 64, row = b * p.N + qt * 64;
+        // an empty slot reads at column Hq * 64, outside the tensor: TMA fills zeros
+        const int jj = un.grp * 4 + j;
+        const int col = jj < G ? (h * G + jj) * 64 : p.Hq * 64, row = b * p.N + qt * 64;
         tma_load_2d_elect(sQ + j * kBox, &p.tm_q, &sm.qs_full, col, row);
         tma_load_2d_elect(sDO + j * kBox, &p.tm_do, &sm.qs_full, col, row);
       }
@@ -507,12 +528,15 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
     int g = 0, it = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
-      const int qt = u % p.qtiles, rest = u / p.qtiles;
-      const int h = rest % p.Hk, b = rest / p.Hk;
-      const int head = h * G + 2 * wg + (row >> 6);
+      const DqUnit un = decode_dq_unit(p, u);
+      const int qt = un.qt, h = un.h, b = un.b;
+      const int slot = un.grp * 4 + 2 * wg + (row >> 6);  // query head within the kv group
+      const bool live = slot < G;
+      const int head = h * G + min(slot, G - 1);
       const int n = qt * 64 + (row & 63);
       const size_t ri = (static_cast<size_t>(b) * p.N + n) * p.Hq + head;
-      const float lse_r = p.lse[ri], d_r = p.delta[ri];
+      // an empty slot's row has Q = dO = 0, so lse = D = 0 make its dS zero
+      const float lse_r = live ? p.lse[ri] : 0.f, d_r = live ? p.delta[ri] : 0.f;
       {
         // This row of Q and of dO, from the staging buffer (a 128-byte-swizzled TMA box:
         // 16-byte chunk c of box row r sits at chunk c ^ (r & 7)), into TMEM. Every MMA
@@ -593,7 +617,7 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dq_kernel(const __grid_constan
           w.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * p.scale, __uint_as_float(o[8 * i + 3]) * p.scale);
           w.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * p.scale, __uint_as_float(o[8 * i + 5]) * p.scale);
           w.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * p.scale, __uint_as_float(o[8 * i + 7]) * p.scale);
-          dst[4 * half + i] = w;
+          if (live) dst[4 * half + i] = w;
         }
       }
       g += T;
@@ -657,7 +681,10 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.Hq / p.Hk;
-  const int per_qb = (p.bs / 64) * (G / 2);  // chunks per q block: 64-query sub-tiles x head pairs
+  // chunks per q block: 64-query sub-tiles x head pairs (with an odd G the last pair
+  // has one head; its second half loads zeros and takes lse = D = 0, adding nothing)
+  const int HP = (G + 1) / 2;
+  const int per_qb = (p.bs / 64) * HP;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.kvt_full, 256);
@@ -697,7 +724,8 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
       int qb, mk;
       while (ok && walk.next(qb, mk)) {
         for (int cq = 0; cq < per_qb; ++cq, ++gc) {
-          const int hp = cq % (G / 2), qs = cq / (G / 2);
+          const int hp = cq % HP, qs = cq / HP;
+          const bool second = 2 * hp + 1 < G;
           const int st = gc % kStagesKv, r = gc / kStagesKv;
           if (r > 0 && !warp_wait(&sm.ch_empty[st], (r - 1) & 1, abort_flag, p.status)) {
             ok = false;
@@ -710,8 +738,9 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
           for (int j = 0; j < 4; ++j) {
             const int e = lane + 32 * j;
             const size_t ri = (static_cast<size_t>(kt.b) * p.N + nbase + (e & 63)) * p.Hq + head0 + (e >> 6);
-            lv[j] = p.lse[ri];
-            dv[j] = p.delta[ri];
+            const bool row_live = (e >> 6) == 0 || second;
+            lv[j] = row_live ? p.lse[ri] : 0.f;
+            dv[j] = row_live ? p.delta[ri] : 0.f;
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -723,9 +752,9 @@ __global__ void __launch_bounds__(kThreadsBwd, 1) dkv_kernel(const __grid_consta
           mbar_arrive_expect_tx_elect(&sm.ch_full[st], kChunkBytes);
           uint8_t* dst = sC + st * kChunkBytes;
           for (int v = 0; v < 2; ++v) {
-            tma_load_2d_elect(dst + v * kBox, &p.tm_q, &sm.ch_full[st], (head0 + v) * 64, kt.b * p.N + nbase);
-            tma_load_2d_elect(dst + (2 + v) * kBox, &p.tm_do, &sm.ch_full[st], (head0 + v) * 64,
-                              kt.b * p.N + nbase);
+            const int col = (v == 0 || second) ? (head0 + v) * 64 : p.Hq * 64;  // outside the tensor: zeros
+            tma_load_2d_elect(dst + v * kBox, &p.tm_q, &sm.ch_full[st], col, kt.b * p.N + nbase);
+            tma_load_2d_elect(dst + (2 + v) * kBox, &p.tm_do, &sm.ch_full[st], col, kt.b * p.N + nbase);
           }
         }
       }
@@ -1026,8 +1055,9 @@ int launch_sparse_bwd(const SparseBwdLaunch& a, cudaStream_t stream) {
     p.B = B; p.N = N; p.Hq = Hq; p.Hk = Hk; p.bs = bs; p.K = K;
     p.nqb = nkb; p.nkb = nkb;
     p.scale = scale; p.scale_log2 = scale_log2;
+    p.ngroups = (Hq / Hk + 3) / 4;
     p.qtiles = N / 64;
-    p.units = B * Hk * p.qtiles;
+    p.units = B * Hk * p.ngroups * p.qtiles;
     static bool done[64] = {};
     int rc = set_smem(dq_kernel, kDqSmemBytes, done);
     if (rc) return rc;

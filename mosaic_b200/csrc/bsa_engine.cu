@@ -1,11 +1,14 @@
 // Fused block-sparse attention engine for sm_100a (tcgen05 + TMEM + TMA).
 //
-// A work unit is one (batch b, kv head h, 64-query tile) with all G = 4 query heads
-// of that kv group; the grid is persistent (one CTA per SM) and CTA i walks units
-// i, i + grid, ... with Q double-buffered so that the next unit's Q loads while
-// the current one finishes. The four heads are packed into two M = 128 MMA tiles
-// ("M-tiles": rows 0-63 = head 4h+2m, rows 64-127 = head 4h+2m+1), so every K/V
-// tile that TMA brings into shared memory is used by 4 heads x 64 queries.
+// A work unit is one (batch b, kv head h, group of four query heads, 64-query tile):
+// query heads h*G + 4*grp + 0..3 of the G = Hq / Hk heads that share kv head h
+// (G = 8 makes two groups per kv head). The grid is persistent (one CTA per SM) and
+// CTA i walks units i, i + grid, ... with Q double-buffered so that the next unit's
+// Q loads while the current one finishes. The four head slots are packed into two
+// M = 128 MMA tiles ("M-tiles": rows 0-63 = slot 2m, rows 64-127 = slot 2m+1), so
+// every K/V tile that TMA brings into shared memory is used by 4 heads x 64 queries.
+// With G = 1 or 2 the slots past the last head of the group load zeros (an
+// out-of-range TMA column) and write nothing.
 // Keys stream in tiles of 64 (one TMA box each for K and V, 8-stage ring):
 //   * local branch   (primitives.block_attention, primitives.py:28-32): the
 //     window [w*win, (w+1)*win) that contains the query tile;
@@ -92,20 +95,33 @@ struct EngineParams {
   int win, bs, K, nqb, nkb;
   int combine;
   float scale_log2;
-  int qtiles;  // 64-query tiles per (batch, kv head)
-  int units;   // B * Hk * qtiles work units
+  int G;        // query heads per kv head
+  int ngroups;  // groups of four query heads per kv head: ceil(G / 4)
+  int qtiles;   // 64-query tiles per (batch, kv head)
+  int units;    // B * Hk * ngroups * qtiles work units
 };
 
-// One work unit: (batch b, kv head h, 64-query tile starting at n0) and its key tiles.
+// One work unit: (batch b, kv head h, head group grp, 64-query tile starting at n0)
+// and its key tiles.
 struct Unit {
-  int b, h, n0;
+  int b, h, grp, n0;
   int wstart, wend;  // local window
   int T_loc, T;      // local tiles, all tiles
 };
 
+// Q column (elements) of head slot j of a unit: slots past the group's last head
+// read at column Hq * 64, outside the tensor, which TMA fills with zeros.
+__device__ __forceinline__ int q_column(const Unit& w, int j, int G, int Hq) {
+  const int jj = w.grp * 4 + j;
+  return jj < G ? (w.h * G + jj) * 64 : Hq * 64;
+}
+
 __device__ __forceinline__ Unit decode_unit(const EngineParams& p, int u) {
   Unit w;
-  const int qt = u % p.qtiles, rest = u / p.qtiles;
+  const int qt = u % p.qtiles;
+  int rest = u / p.qtiles;
+  w.grp = rest % p.ngroups;
+  rest /= p.ngroups;
   w.h = rest % p.Hk;
   w.b = rest / p.Hk;
   w.n0 = qt * kQTile;
@@ -385,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       for (int m = 0; m < 2; ++m)
         for (int v = 0; v < 2; ++v)
           tma_load_2d_elect(sQ + (2 * qbuf + m) * kQTileBytes + v * kBoxBytes, &p.tm_q, &sm.q_full[qbuf],
-                            (w.h * G + 2 * m + v) * 64, w.b * p.Nq + w.n0);
+                            q_column(w, 2 * m + v, G, p.Hq), w.b * p.Nq + w.n0);
       for (int t = 0; t < w.T; ++t, ++g) {
         const int st = g % kStages, r = g / kStages;
         if (r > 0 && !warp_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) {
@@ -498,9 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
       const Unit w = decode_unit(p, u);
       const int T_slc = w.T - w.T_loc;
-      const int head = w.h * G + 2 * wg + (row >> 6);
+      const int slot = w.grp * 4 + 2 * wg + (row >> 6);  // query head within the kv group
+      const int head = w.h * G + min(slot, G - 1);
       const int n = w.n0 + (row & 63);
-      const bool live = n < p.Nq;
+      const bool live = n < p.Nq && slot < G;
 
       // Gates of this output row (the reference's weight_ba_cmp_slc[:, b, n, head]).
       float c0 = 0.f, c1 = 0.f, c2 = 0.f;
@@ -675,8 +692,10 @@ int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
   p.nkb = a.Nk / p.bs;
   p.combine = a.combine;
   p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+  p.G = a.Hq / a.Hk;
+  p.ngroups = (p.G + 3) / 4;
   p.qtiles = (a.Nq + kQTile - 1) / kQTile;
-  p.units = a.B * a.Hk * p.qtiles;
+  p.units = a.B * a.Hk * p.ngroups * p.qtiles;
 
   // The shared-memory opt-in is a per-device function attribute: set it once per
   // device and instantiation.

@@ -90,8 +90,14 @@ int check_heads(int B, int N, int Hq, int Hk, int D) {
   if (B < 0 || N < 0 || Hq <= 0 || Hk <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (D != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
   if (Hq % Hk != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
-  if (Hq / Hk != 4) return MOSAIC_ERR_UNSUPPORTED;
   return MOSAIC_OK;
+}
+
+// The top-k kernels are instantiated for 1, 2, 4 and 8 query heads per kv head; the
+// attention kernels take any ratio.
+bool topk_group_supported(int Hq, int Hk) {
+  const int G = Hq / Hk;
+  return G == 1 || G == 2 || G == 4 || G == 8;
 }
 
 struct Workspace {
@@ -134,7 +140,7 @@ const char* mosaic_error_string(int code) {
   switch (code) {
     case MOSAIC_OK: return "ok";
     case MOSAIC_ERR_INVALID_ARGUMENT: return "invalid argument (null/misaligned pointer, negative or inconsistent size)";
-    case MOSAIC_ERR_UNSUPPORTED: return "unsupported shape (needs head_dim 64, 4 query heads per kv head, block sizes multiple of 64)";
+    case MOSAIC_ERR_UNSUPPORTED: return "unsupported shape (needs head_dim 64, block sizes multiple of 64; top-k: 1, 2, 4 or 8 query heads per kv head)";
     case MOSAIC_ERR_WORKSPACE: return "workspace missing or smaller than mosaic_bsa_workspace_bytes()";
     case MOSAIC_ERR_CUDA: return "CUDA call failed (kernel launch or tensor-map encoding)";
     default: return "unknown mosaic_b200 error code";
@@ -294,7 +300,7 @@ int mosaic_attn_topk(const void* q_cmp, const void* k_cmp, int64_t* block_indice
   if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
   if (num_q_heads % num_kv_heads != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
-  if (num_q_heads / num_kv_heads > 8) return MOSAIC_ERR_UNSUPPORTED;
+  if (!topk_group_supported(num_q_heads, num_kv_heads)) return MOSAIC_ERR_UNSUPPORTED;
   if (!q_cmp || !k_cmp || !block_indices) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(q_cmp) || !aligned16(k_cmp)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (block_count < 0 || block_count > num_blocks) return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -338,6 +344,7 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
     if (K > nb) return MOSAIC_ERR_INVALID_ARGUMENT;
     if (no_cmp && K == 0) return MOSAIC_ERR_INVALID_ARGUMENT;
     if (K > kMaxTopK || nb > 65535) return MOSAIC_ERR_UNSUPPORTED;
+    if (!topk_group_supported(Hq, Hk)) return MOSAIC_ERR_UNSUPPORTED;
   }
   const Workspace ws = workspace_layout(B, N, Hq, Hk, bs > 0 ? bs : 64, local_only ? 0 : K, rope);
   const bool need_ws = !local_only || rope;

@@ -93,7 +93,6 @@ def _sparse(**kw):
     (dict(idx=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(k=ctypes.c_void_p(0x10008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # misaligned
     (dict(D=128), _lib.MOSAIC_ERR_UNSUPPORTED),
-    (dict(Hq=6, Hk=2), _lib.MOSAIC_ERR_UNSUPPORTED),          # G = 3
     (dict(Hq=7, Hk=2), _lib.MOSAIC_ERR_INVALID_ARGUMENT),     # not a multiple
     (dict(bs=32), _lib.MOSAIC_ERR_UNSUPPORTED),
     (dict(N=1000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),         # N % bs
@@ -130,6 +129,9 @@ def _bsa(**kw):
     (dict(workspace_bytes=16), _lib.MOSAIC_ERR_WORKSPACE),
     (dict(rope_cos=0x10000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),         # cos without sin
     (dict(head_dim=32), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(num_q_heads=3), _lib.MOSAIC_ERR_UNSUPPORTED),      # top-k with G = 3
+    (dict(num_q_heads=16), _lib.MOSAIC_ERR_UNSUPPORTED),     # top-k with G = 16
+    (dict(num_q_heads=6, num_kv_heads=4), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # not a multiple
     (dict(dtype=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
 ])
 def test_bsa_rejects_bad_arguments(kw, code):
@@ -147,6 +149,8 @@ def test_topk_rejects_bad_arguments():
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 129, f16, None) != _lib.MOSAIC_OK
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 0, f16, None) == _lib.MOSAIC_OK
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 8, 7, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+    for hq in (3, 6, 16):  # G outside 1, 2, 4, 8
+        assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, hq, 1, 64, 8, bf16, None) == _lib.MOSAIC_ERR_UNSUPPORTED
 
 
 def _sparse_bwd(**kw):
@@ -177,7 +181,7 @@ def test_sparse_bwd_workspace_size():
     (dict(dv=None), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(dk=ctypes.c_void_p(0x10008)), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # misaligned
     (dict(D=128), _lib.MOSAIC_ERR_UNSUPPORTED),
-    (dict(Hq=6, Hk=2), _lib.MOSAIC_ERR_UNSUPPORTED),
+    (dict(Hq=7, Hk=2), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(bs=32), _lib.MOSAIC_ERR_UNSUPPORTED),
     (dict(N=1000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
     (dict(K=0), _lib.MOSAIC_ERR_INVALID_ARGUMENT),

@@ -61,6 +61,10 @@ def gpu_bwd(q, k, v, go, idx, bs, scale=None):
     (1, 3072, 12, 3, 64, 16),
     (1, 2048, 4, 1, 256, 2),
     (1, 320, 4, 1, 64, 2),    # N % 128 == 64: the last 128-key tile has one segment
+    (1, 1024, 2, 2, 64, 4),   # 1 query head per kv head (an odd G: half-empty head pairs)
+    (1, 1024, 4, 2, 64, 3),   # 2
+    (1, 1024, 8, 1, 64, 4),   # 8: two head groups per kv head
+    (1, 768, 6, 2, 64, 4),    # 3
     (1, 512, 4, 1, 64, 8),    # every block selected by every query block
     (2, 640, 8, 2, 64, 1),
 ])

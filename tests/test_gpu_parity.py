@@ -97,7 +97,9 @@ def test_topk_matches_golden(name):
 
 
 # ----------------------------------------------------------------------------- coarse + local attention
-@pytest.mark.parametrize("cfg", [(1, 48, 4, 1), (1, 24, 20, 5), (2, 192, 16, 4), (1, 768, 12, 3), (1, 100, 8, 2)])
+@pytest.mark.parametrize("cfg", [(1, 48, 4, 1), (1, 24, 20, 5), (2, 192, 16, 4), (1, 768, 12, 3), (1, 100, 8, 2),
+                                 # 1, 2, 8 and 3 query heads per kv head
+                                 (1, 48, 3, 3), (1, 96, 4, 2), (1, 96, 16, 2), (1, 64, 6, 2)])
 def test_cmp_attention(cfg):
     B, nb, Hq, Hk = cfg
     x = O.make_inputs(B, nb, Hq, Hk, seed=5, rope=False)
@@ -106,7 +108,10 @@ def test_cmp_attention(cfg):
 
 
 @pytest.mark.parametrize("cfg", [(1, 3072, 4, 1, 1024), (2, 2048, 8, 2, 256), (1, 1024, 12, 3, 64),
-                                 (1, 768, 4, 1, 768), (1, 3840, 12, 3, 192)])
+                                 (1, 768, 4, 1, 768), (1, 3840, 12, 3, 192),
+                                 # 1, 2, 8 and 3 query heads per kv head
+                                 (1, 2048, 2, 2, 1024), (1, 2048, 4, 2, 512), (1, 2048, 8, 1, 512),
+                                 (1, 1024, 6, 2, 256)])
 def test_block_attention(cfg):
     B, N, Hq, Hk, bas = cfg
     x = O.make_inputs(B, N, Hq, Hk, seed=6, rope=False)
@@ -124,7 +129,10 @@ def random_indices(B, nb, Hk, K, seed, duplicates=False):
 
 
 @pytest.mark.parametrize("cfg", [(1, 768, 4, 1, 64, 4), (2, 1024, 8, 2, 128, 3), (1, 3072, 12, 3, 64, 24),
-                                 (1, 2048, 4, 1, 256, 2), (1, 1024, 4, 1, 64, 5), (1, 512, 4, 1, 64, 8)])
+                                 (1, 2048, 4, 1, 256, 2), (1, 1024, 4, 1, 64, 5), (1, 512, 4, 1, 64, 8),
+                                 # 1, 2, 8 and 3 query heads per kv head
+                                 (1, 1024, 2, 2, 64, 4), (2, 1024, 4, 2, 64, 6), (1, 1024, 16, 2, 128, 3),
+                                 (1, 768, 6, 2, 64, 4)])
 def test_sparse_attention(cfg):
     B, N, Hq, Hk, bs, K = cfg
     x = O.make_inputs(B, N, Hq, Hk, seed=7, rope=False)
@@ -206,6 +214,9 @@ def full_check(x, bas, bs, K, block_attn_only=False, no_compression=False, rope=
     (1, 3072, 20, 5, 1024, 64, 20),    # BN
     (2, 3072, 8, 2, 512, 128, 4),      # reference-preset block size 128
     (1, 12288, 16, 4, 1024, 64, 20),   # S2
+    (1, 3072, 3, 3, 1024, 64, 8),      # 1 query head per kv head
+    (1, 3072, 2, 1, 1024, 64, 8),      # 2
+    (1, 3072, 8, 1, 1024, 64, 8),      # 8
 ])
 def test_mosaic_attn_func(cfg):
     B, N, Hq, Hk, bas, bs, K = cfg

@@ -36,7 +36,9 @@ def close(got, want, max_abs=MAX_ABS, mean_abs=MEAN_ABS):
 
 
 @pytest.mark.parametrize("cfg", [(1, 3072, 4, 1, 64, 8), (1, 12288, 12, 3, 64, 24), (2, 4096, 8, 2, 128, 6),
-                                 (1, 49152, 12, 3, 128, 24)])
+                                 (1, 49152, 12, 3, 128, 24),
+                                 # 1, 2 and 8 query heads per kv head (the Triton kernel takes any)
+                                 (1, 3072, 2, 2, 64, 8), (1, 4096, 4, 2, 128, 6), (1, 3072, 8, 1, 64, 8)])
 def test_sparse_attention_matches_reference_triton_kernel(ref, cfg):
     B, N, Hq, Hk, bs, K = cfg
     g = torch.Generator(device=DEV).manual_seed(N + K)
@@ -57,7 +59,11 @@ def test_sparse_attention_matches_reference_triton_kernel(ref, cfg):
                                  (2, 12288, 16, 4, 1024, 128, 12, torch.bfloat16),
                                  # fp16, the reference rollout's dtype: its attn_topk then scores in fp16
                                  (1, 3072, 4, 1, 1024, 64, 8, torch.float16),
-                                 (1, 49152, 12, 3, 1024, 64, 24, torch.float16)])
+                                 (1, 49152, 12, 3, 1024, 64, 24, torch.float16),
+                                 # 1, 2 and 8 query heads per kv head
+                                 (1, 3072, 2, 2, 1024, 64, 8, torch.bfloat16),
+                                 (1, 3072, 2, 1, 1024, 64, 8, torch.bfloat16),
+                                 (1, 3072, 8, 1, 1024, 64, 8, torch.bfloat16)])
 def test_mosaic_attn_func_matches_reference_gpu_path(ref, cfg):
     B, N, Hq, Hk, bas, bs, K, dtype = cfg
     x = O.make_inputs(B, N, Hq, Hk, seed=N + bs, dtype=dtype, rope=True)
