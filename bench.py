@@ -980,37 +980,37 @@ def rollout_leg(dev, stream):
     dyt = torch.rand(1, 2, generator=g, device=dev)
     delta = torch.tensor([0.25, 1 / 365], device=dev)
 
-    def timed(model, graph, steps, warm=True):
-        if warm:
-            unroll_direct(model, x0, dyt, delta, ns, 2, MEMBERS, graph=graph)
+    def timed(model, graph, steps):
+        unroll_direct(model, x0, dyt, delta, ns, 2, MEMBERS, graph=graph)  # warm-up
         torch.cuda.synchronize()
+        ev = []
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        unroll_direct(model, x0, dyt, delta, ns, steps, MEMBERS, graph=graph)
+        unroll_direct(model, x0, dyt, delta, ns, steps, MEMBERS, graph=graph, step_events=ev)
         b.record(stream)
         torch.cuda.synchronize()
-        return a.elapsed_time(b)
+        per = {}
+        for t, kind, e0, e1 in ev:
+            per.setdefault(kind, []).append(e0.elapsed_time(e1))
+        return a.elapsed_time(b), {k: sum(v) / len(v) for k, v in per.items()}
 
     T = ROLLOUT_STEPS
-    graph_ms = timed(ours, True, T)
-    graph_ms_more = timed(ours, True, T + 2, warm=False)
-    replay_ms = (graph_ms_more - graph_ms) / 2  # steady state: two more replays
-    eager_ms = timed(ours, False, T)
+    graph_ms, g_steps = timed(ours, True, T)
+    eager_ms, e_steps = timed(ours, False, T)
     del ours
     torch.cuda.empty_cache()
     ref_model = R.build_model(ref, dev, ours=False, dtype=None, seed=0)
-    ref_ms = timed(ref_model, False, T)
+    ref_ms, r_steps = timed(ref_model, False, T)
     del ref_model
     torch.cuda.empty_cache()
     return {"what": "unroll_direct (inference.py:330-390) of the reference's U-Net, 24 members, fp16 autocast "
-                    "over fp32 weights, synthetic state and normalisation statistics; ms_per_step is a graph "
-                    "replay in steady state ((rollout of T + 2 steps - rollout of T steps) / 2)",
+                    "over fp32 weights, synthetic state and normalisation statistics; per-step times from CUDA "
+                    "events around each step",
             "members": MEMBERS, "unroll_steps": T, "graph_replayed_steps": T - 2,
-            "rollout_ms": graph_ms, "rollout_ms_plus_2_steps": graph_ms_more, "ms_per_step": replay_ms,
-            "eager_rollout_ms": eager_ms, "eager_ms_per_step": eager_ms / T,
-            "reference_modules_rollout_ms": ref_ms, "reference_modules_ms_per_step": ref_ms / T,
-            "speedup_vs_reference_modules": (ref_ms / T) / replay_ms,
-            "capture_overhead_ms": graph_ms - 2 * eager_ms / T - (T - 2) * replay_ms}
+            "rollout_ms": graph_ms, "ms_per_step": g_steps["graph"], "graph_eager_steps_ms": g_steps["eager"],
+            "eager_rollout_ms": eager_ms, "eager_ms_per_step": e_steps["eager"],
+            "reference_modules_rollout_ms": ref_ms, "reference_modules_ms_per_step": r_steps["eager"],
+            "speedup_vs_reference_modules": r_steps["eager"] / g_steps["graph"]}
 
 
 def b200_arm(args):

@@ -37,7 +37,7 @@ def _generators(model):
 
 @torch.no_grad()
 def unroll_direct(model, initial_unnorm_state, day_year_time, day_year_delta, norm_stats, num_unroll_steps,
-                  num_ensemble_members, dtype=torch.float16, graph=True, warmup_steps=1):
+                  num_ensemble_members, dtype=torch.float16, graph=True, warmup_steps=1, step_events=None):
     """Forecast `num_unroll_steps` steps of `num_ensemble_members` members
     (inference.py:330-390).
 
@@ -49,7 +49,11 @@ def unroll_direct(model, initial_unnorm_state, day_year_time, day_year_delta, no
     graph=False runs every step eagerly (the reference's loop, step for step);
     graph=True replays steps 1 + warmup_steps .. num_unroll_steps - 1 from one CUDA
     graph. Both give the same trajectory when the model draws no noise or its
-    generators are registered (graph replays advance them as eager calls do)."""
+    generators are registered (graph replays advance them as eager calls do).
+
+    step_events: a list to which (step, "eager" | "graph", start, end) is appended for
+    every step, start and end being CUDA events recorded around the step on the stream
+    that runs it (for timing; nothing is synchronised)."""
     if graph and initial_unnorm_state.device.type != "cuda":
         raise ValueError("unroll_direct(graph=True) runs on a CUDA device")
     B, H = initial_unnorm_state.shape[:2]
@@ -68,18 +72,35 @@ def unroll_direct(model, initial_unnorm_state, day_year_time, day_year_delta, no
             out = model(norm, dyt, num_ens)
         return out * std + mean
 
+    def mark(t, kind, stream=None):
+        if step_events is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return (t, kind, e)
+
+    def done(m, stream=None):
+        if m is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            step_events.append(m + (e,))
+
     def advance(dyt, num_ens):
         return dyt + day_year_delta.unsqueeze(0).unsqueeze(0).expand(B, num_ens, -1)
 
     # step 0: the ensemble is expanded here
     dyt = day_year_time.unsqueeze(1)
+    m = mark(0, "eager")
     traj[:, :, H] = step(traj[:, :1, :H], dyt, M)
     dyt = advance(dyt, M)
+    done(m)
     t = 1
     if not graph:
         for t in range(1, T):
+            m = mark(t, "eager")
             traj[:, :, H + t] = step(traj[:, :, t:t + H], dyt, 1)
             dyt = advance(dyt, M)
+            done(m)
         return traj
 
     # eager warm-up steps (real steps of the rollout) on a side stream
@@ -88,8 +109,10 @@ def unroll_direct(model, initial_unnorm_state, day_year_time, day_year_delta, no
     side.wait_stream(cur)
     with torch.cuda.stream(side):
         while t < T and t < 1 + warmup_steps:
+            m = mark(t, "eager", side)
             traj[:, :, H + t] = step(traj[:, :, t:t + H], dyt, 1, cache=False)
             dyt = advance(dyt, M)
+            done(m, side)
             t += 1
     cur.wait_stream(side)
     if t >= T:
@@ -106,7 +129,9 @@ def unroll_direct(model, initial_unnorm_state, day_year_time, day_year_delta, no
         s_dyt.add_(delta)
         s_state.copy_(torch.cat([s_state[:, :, 1:], s_next.unsqueeze(2).to(s_state.dtype)], dim=2))
     for t in range(t, T):
+        m = mark(t, "graph")
         g.replay()
         traj[:, :, H + t].copy_(s_next)
+        done(m)
     del g
     return traj

@@ -42,19 +42,22 @@ def setup():
     torch.cuda.empty_cache()
 
 
-def _run(model, setup, graph):
+def _run(model, setup, graph, step_events=None):
     from mosaic_b200.rollout import unroll_direct
 
     _, _, ns, x0, dyt, delta = setup
     model.noise_generator.generator = None  # re-seeded on the first draw
-    return unroll_direct(model, x0, dyt, delta, ns, T, M, graph=graph)
+    return unroll_direct(model, x0, dyt, delta, ns, T, M, graph=graph, step_events=step_events)
 
 
 def test_graph_rollout_matches_eager_rollout(setup):
     ours = setup[1]
     eager = _run(ours, setup, False)
-    graphed = _run(ours, setup, True)
+    ev = []
+    graphed = _run(ours, setup, True, ev)
     torch.cuda.synchronize()
+    assert [(t, kind) for t, kind, _, _ in ev] == [(0, "eager"), (1, "eager"), (2, "graph"), (3, "graph")]
+    assert all(e0.elapsed_time(e1) > 0 for _, _, e0, e1 in ev)
     assert graphed.shape == (1, M, 2 + T, R.GRID_LON, R.GRID_LAT, C)
     assert torch.isfinite(graphed).all()
     assert not torch.equal(graphed[:, 0, 2 + T - 1], graphed[:, 1, 2 + T - 1])  # members differ
