@@ -80,7 +80,7 @@ __device__ __forceinline__ void p_ds_quarter(uint32_t (&s)[32], uint32_t (&dp)[3
       const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nl[k]);
       uint64_t e;
       if ((i % kPolyDen) >= kPolyDen - kPolyNum) {
-        e = exp2_poly2(x);
+        e = exp2_poly2(x);  // x = s*c - lse <= 0 up to rounding: lse is the forward's log-sum of these keys
       } else {
         float x0, x1;
         f2_unpack(x, x0, x1);

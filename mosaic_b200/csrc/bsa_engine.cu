@@ -203,7 +203,7 @@ __device__ __forceinline__ float exp_pack_tile(uint32_t (&s)[64], float c, float
     const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nm2);
     uint64_t e;
     if ((i % kPolyDen) >= kPolyDen - kPolyNum) {
-      e = exp2_poly2(x);
+      e = exp2_poly2<true>(x);  // x = s*c - m_run is not bounded above (stale max)
     } else {
       float x0, x1;
       f2_unpack(x, x0, x1);

@@ -353,13 +353,18 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Software 2^x for x <= 0 on the FMA/ALU pipes, for two values at once.
+// Software 2^x on the FMA/ALU pipes, for two values at once.
 // Cody-Waite style reduction x = j + f with j = rint(x) (the 1.5*2^23 shifter
 // trick) and f in [-1/2, 1/2], then 2^f by a degree-3 polynomial whose
 // coefficients are a relative-error minimax fit computed for this library by the
 // Remez exchange algorithm (max relative error 7.5e-5, far below the 2^-9 of
 // the bf16 rounding that P undergoes next), and 2^j added into the exponent
-// field. x is clamped at -125 so that the exponent cannot underflow.
+// field. x is clamped at -125 so that the exponent cannot underflow and, with
+// kUpper, at 126 so that it cannot wrap past the top of the exponent field either
+// (without it a score more than 127 above the caller's shift would come back as a
+// tiny or negative number that no sum can flag; with it the result saturates near
+// 2^126, like MUFU's +inf).
+template <bool kUpper = false>
 __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
   constexpr float kC0 = 0.99992807f, kC1 = 0.69326099f, kC2 = 0.24261112f, kC3 = 0.05517167f;
@@ -367,6 +372,10 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
   f2_unpack(x2, x0, x1);
   x0 = fmaxf(x0, -125.0f);
   x1 = fmaxf(x1, -125.0f);
+  if (kUpper) {
+    x0 = fminf(x0, 126.0f);
+    x1 = fminf(x1, 126.0f);
+  }
   const uint64_t xc = f2_pack(x0, x1);
   const uint64_t t = f2_add(xc, f2_pack(kShift, kShift));        // low mantissa bits hold rint(x)
   const uint64_t j = f2_add(t, f2_pack(-kShift, -kShift));       // rint(x) as a float

@@ -365,3 +365,26 @@ def test_score_spike_forces_exact_path():
     torch.cuda.synchronize()
     assert mops.check_status(status) == 0
     close(out, O.block_attention(x["q"], k, x["v"], 1024))
+
+
+@pytest.mark.parametrize("column", [12, 2], ids=["polynomial-lane", "mufu-lane"])
+def test_score_far_above_running_max_in_every_lane(column):
+    """Every query gets a common component (q[..., 0] += 10) and one key per window,
+    in tile 5 at the given column, is 100 * e0, so its score is ~180 (base 2) above
+    the running max of the tiles before it: past the top of the exponent field. The
+    kernel splits its exponentials between MUFU lanes and a polynomial on the FMA
+    pipe (column 12 is a polynomial lane, column 2 a MUFU lane); both must saturate
+    so that the overflow shows in the tile sum and the exact path takes over."""
+    B, N, Hq, Hk = 1, 2048, 4, 1
+    x = O.make_inputs(B, N, Hq, Hk, seed=23, rope=False)
+    q, k = x["q"].float(), x["k"].float()
+    q[..., 0] += 10.0
+    spike = torch.arange(N) % 1024 == 5 * 64 + column
+    k[:, spike] = 0.0
+    k[:, spike, :, 0] = 100.0
+    q, k = q.bfloat16(), k.bfloat16()
+    status = mops.status_buffer(DEV)
+    out = M.block_attention(*cuda(q, k, x["v"]), 1024, status=status)
+    torch.cuda.synchronize()
+    assert mops.check_status(status) == 0
+    close(out, O.block_attention(q, k, x["v"], 1024))
