@@ -6,7 +6,7 @@
  * row-major in the reference's layouts ([batch, seq, heads, head_dim]); head_dim
  * is 64. Any number of query heads per kv head (G = num_q_heads / num_kv_heads)
  * is accepted by the attention and backward entry points; the top-k selection (and
- * so mosaic_bsa_fwd outside block_attn_only) takes G = 1, 2, 4 or 8. The kernels
+ * so mosaic_bsa_fwd outside block_attn_only) takes G = 1 to 8. The kernels
  * work on groups of four query heads: G = 4 and 8 fill them, G = 1 and 2 leave
  * three or two of the four head slots empty (computed on zeros, not written).
  * The attention entry points take a

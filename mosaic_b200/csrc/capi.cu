@@ -93,11 +93,11 @@ int check_heads(int B, int N, int Hq, int Hk, int D) {
   return MOSAIC_OK;
 }
 
-// The top-k kernels are instantiated for 1, 2, 4 and 8 query heads per kv head; the
-// attention kernels take any ratio.
+// The top-k kernels are instantiated for 1 to 8 query heads per kv head (every
+// preset has 4); the attention kernels take any ratio.
 bool topk_group_supported(int Hq, int Hk) {
   const int G = Hq / Hk;
-  return G == 1 || G == 2 || G == 4 || G == 8;
+  return G >= 1 && G <= 8;
 }
 
 struct Workspace {
@@ -140,7 +140,7 @@ const char* mosaic_error_string(int code) {
   switch (code) {
     case MOSAIC_OK: return "ok";
     case MOSAIC_ERR_INVALID_ARGUMENT: return "invalid argument (null/misaligned pointer, negative or inconsistent size)";
-    case MOSAIC_ERR_UNSUPPORTED: return "unsupported shape (needs head_dim 64, block sizes multiple of 64; top-k: 1, 2, 4 or 8 query heads per kv head)";
+    case MOSAIC_ERR_UNSUPPORTED: return "unsupported shape (needs head_dim 64, block sizes multiple of 64; top-k: 1 to 8 query heads per kv head)";
     case MOSAIC_ERR_WORKSPACE: return "workspace missing or smaller than mosaic_bsa_workspace_bytes()";
     case MOSAIC_ERR_CUDA: return "CUDA call failed (kernel launch or tensor-map encoding)";
     default: return "unknown mosaic_b200 error code";

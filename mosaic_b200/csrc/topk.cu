@@ -358,6 +358,14 @@ int launch_topk(const TopkLaunch& a, cudaStream_t stream) {
     case 5: return launch_g<2, true>(p, stream, a.overlap_previous);
     case 8: return launch_g<4, false>(p, stream, a.overlap_previous);
     case 9: return launch_g<4, true>(p, stream, a.overlap_previous);
+    case 6: return launch_g<3, false>(p, stream, a.overlap_previous);
+    case 7: return launch_g<3, true>(p, stream, a.overlap_previous);
+    case 10: return launch_g<5, false>(p, stream, a.overlap_previous);
+    case 11: return launch_g<5, true>(p, stream, a.overlap_previous);
+    case 12: return launch_g<6, false>(p, stream, a.overlap_previous);
+    case 13: return launch_g<6, true>(p, stream, a.overlap_previous);
+    case 14: return launch_g<7, false>(p, stream, a.overlap_previous);
+    case 15: return launch_g<7, true>(p, stream, a.overlap_previous);
     case 16: return launch_g<8, false>(p, stream, a.overlap_previous);
     case 17: return launch_g<8, true>(p, stream, a.overlap_previous);
     default: return MOSAIC_ERR_UNSUPPORTED;

@@ -129,8 +129,8 @@ def _bsa(**kw):
     (dict(workspace_bytes=16), _lib.MOSAIC_ERR_WORKSPACE),
     (dict(rope_cos=0x10000), _lib.MOSAIC_ERR_INVALID_ARGUMENT),         # cos without sin
     (dict(head_dim=32), _lib.MOSAIC_ERR_UNSUPPORTED),
-    (dict(num_q_heads=3), _lib.MOSAIC_ERR_UNSUPPORTED),      # top-k with G = 3
     (dict(num_q_heads=16), _lib.MOSAIC_ERR_UNSUPPORTED),     # top-k with G = 16
+    (dict(num_q_heads=27), _lib.MOSAIC_ERR_UNSUPPORTED),     # top-k with G = 9
     (dict(num_q_heads=6, num_kv_heads=4), _lib.MOSAIC_ERR_INVALID_ARGUMENT),  # not a multiple
     (dict(dtype=-1), _lib.MOSAIC_ERR_INVALID_ARGUMENT),
 ])
@@ -149,7 +149,7 @@ def test_topk_rejects_bad_arguments():
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 129, f16, None) != _lib.MOSAIC_OK
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 0, f16, None) == _lib.MOSAIC_OK
     assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, 4, 1, 64, 8, 7, None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
-    for hq in (3, 6, 16):  # G outside 1, 2, 4, 8
+    for hq in (9, 16):  # G outside 1 to 8
         assert lib.mosaic_attn_topk(FAKE, FAKE, FAKE, 1, 48, hq, 1, 64, 8, bf16, None) == _lib.MOSAIC_ERR_UNSUPPORTED
 
 

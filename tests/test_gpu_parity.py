@@ -63,7 +63,9 @@ def test_rope_pool_bit_exact(cfg):
 @pytest.mark.parametrize("cfg", [(1, 48, 4, 1, 8), (2, 192, 16, 4, 20), (1, 768, 12, 3, 24), (1, 1536, 8, 2, 64),
                                  # from 2048 blocks on the tensor-core kernel runs: partial key tiles and
                                  # row tiles, G = 4 / 2 / 1, best-list sizes 8 / 24 / 32
-                                 (1, 3072, 12, 3, 24), (1, 2600, 8, 4, 32), (2, 2100, 4, 4, 5), (1, 2049, 4, 1, 17)])
+                                 (1, 3072, 12, 3, 24), (1, 2600, 8, 4, 32), (2, 2100, 4, 4, 5), (1, 2049, 4, 1, 17),
+                                 # G = 3, 5, 6, 7 (the small-grid kernel at any size)
+                                 (1, 768, 9, 3, 24), (1, 192, 5, 1, 8), (2, 384, 12, 2, 16), (1, 2100, 7, 1, 12)])
 def test_topk_matches_oracle(cfg):
     B, nb, Hq, Hk, K = cfg
     g = torch.Generator().manual_seed(nb)
@@ -217,6 +219,8 @@ def full_check(x, bas, bs, K, block_attn_only=False, no_compression=False, rope=
     (1, 3072, 3, 3, 1024, 64, 8),      # 1 query head per kv head
     (1, 3072, 2, 1, 1024, 64, 8),      # 2
     (1, 3072, 8, 1, 1024, 64, 8),      # 8
+    (1, 3072, 9, 3, 1024, 64, 8),      # 3
+    (1, 3072, 12, 2, 1024, 64, 8),     # 6
 ])
 def test_mosaic_attn_func(cfg):
     B, N, Hq, Hk, bas, bs, K = cfg
