@@ -845,7 +845,9 @@ def ensemble_leg(dev, rank, world, dist, stream, steps, warmup):
             "step_per_s": 1000.0 / step_ms, "gather_ms": gather_ms, "gather_share": gather_ms / step_ms,
             "gathered_bytes_per_rank": MEMBERS * FIELD_NUMEL * 4,
             "attention_flop_per_member": flop,
-            "attention_tflops_per_gpu": flop * m / ((step_ms - gather_ms) / 1000) / 1e12}
+            "attention_tflops_per_gpu": flop * m / ((step_ms - gather_ms) / 1000) / 1e12,
+            "attention_frac_of_peak": flop * m / ((step_ms - gather_ms) / 1000) / 1e12 / peaks()[1],
+            "peak_source": peaks()[2] + " bf16_tflops (burst)"}
 
 
 UNET_TFLOP_PER_MEMBER = 11.45  # FlopCounterMode on the reference model at the era5 preset, one member
@@ -936,7 +938,8 @@ def model_leg(dev, rank, world, dist, stream, steps, warmup):
     res.update(step_ms=step_ms, step_per_s=1000.0 / step_ms, gather_ms=gather_ms, gather_share=gather_ms / step_ms,
                graph_step_ms=graph_ms, graph_step_per_s=1000.0 / graph_ms,
                tflop_per_step=UNET_TFLOP_PER_MEMBER * MEMBERS,
-               achieved_tflops_per_gpu=UNET_TFLOP_PER_MEMBER * m / (step_ms / 1000))
+               achieved_tflops_per_gpu=UNET_TFLOP_PER_MEMBER * m / (step_ms / 1000),
+               frac_of_peak=UNET_TFLOP_PER_MEMBER * m / (step_ms / 1000) / peaks()[1])
     if world == 1:
         ref_model = R.build_model(ref, dev, ours=False, dtype=torch.bfloat16, seed=0)
         with torch.no_grad():
