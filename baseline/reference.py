@@ -177,7 +177,9 @@ def build_model(ref, device, ours=True, dtype=None, seed=0):
     fields ~ N(0, 1) on the 240 x 121 grid, on `device` in eval mode.
 
     ours=True rebinds, before construction, the names the model resolves at build time
-    to mosaic_b200's modules: primitives.MosaicAttention (looked up by MosaicBlock),
+    to mosaic_b200's modules: the block class mosaic.py imports from primitives
+    (`_MosaicBlock`, whose attention is mosaic_b200.MosaicAttention and whose FFN is the
+    fused mosaic_b200.MosaicSwiGLU), primitives.MosaicAttention,
     mosaic.CrossAttentionInterpolate, mosaic.HEALPixDownsample and
     mosaic.HEALPixUpsample (as INTEGRATION.md describes); ours=False restores the
     reference's own classes. Either way the HEALPix pixel centres come from
@@ -190,8 +192,10 @@ def build_model(ref, device, ours=True, dtype=None, seed=0):
     prim, mos = ref.primitives, ref.mosaic
     if not hasattr(ref, "_orig"):
         ref._orig = dict(MosaicAttention=prim.MosaicAttention, CrossAttentionInterpolate=mos.CrossAttentionInterpolate,
-                         HEALPixDownsample=mos.HEALPixDownsample, HEALPixUpsample=mos.HEALPixUpsample)
+                         HEALPixDownsample=mos.HEALPixDownsample, HEALPixUpsample=mos.HEALPixUpsample,
+                         _MosaicBlock=mos._MosaicBlock)
     prim.MosaicAttention = M.MosaicAttention if ours else ref._orig["MosaicAttention"]
+    mos._MosaicBlock = M.MosaicBlock if ours else ref._orig["_MosaicBlock"]
     for name in ("CrossAttentionInterpolate", "HEALPixDownsample", "HEALPixUpsample"):
         setattr(mos, name, getattr(M, name) if ours else ref._orig[name])
     mos.get_healpix_grid = get_healpix_grid

@@ -286,7 +286,7 @@ def interp_leg(stream, steps, warmup, dim=768, heads=12, k=24):
         tiles = {key: (val.to(dev) if torch.is_tensor(val) else val) for key, val in I.build_tiles(nb, pt).items()}
         S_from, S_to = pf.shape[0], pt.shape[0]
         xs = [torch.randn(S_from, 1, dim, generator=g, device=dev).bfloat16() for _ in range(4)]
-        eps = torch.finfo(torch.bfloat16).eps
+        eps = torch.finfo(torch.float32).eps  # torch.nn.RMSNorm's eps=None default
 
         def fused(x, ev=None):
             if ev: ev[0].record(stream)
@@ -371,7 +371,7 @@ def updown_leg(stream, steps, warmup, dims=(768, 1024), nsides=(64, 32)):
         rows_in = n * Fk if kind == "down" else n
         xs = [torch.randn(rows_in, 1, c_in, generator=g, device=dev).bfloat16() for _ in range(4)]
         scs = [torch.randn(n * Fk, 1, c_out, generator=g, device=dev).bfloat16() for _ in range(4)]
-        eps = torch.finfo(torch.bfloat16).eps
+        eps = torch.finfo(torch.float32).eps  # torch.nn.RMSNorm's eps=None default
         rel = m.rel_pos.bfloat16()
 
         def fused(i):

@@ -218,6 +218,21 @@ MOSAIC_API int mosaic_attn_qkv_proj(const void* x, const void* w_qkvg, const flo
 MOSAIC_API int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* status, int seq_len,
                                     int batch, int dim, int num_q_heads, int head_dim, void* stream);
 
+/* mosaic_attn_out_proj followed by the residual add of MosaicBlock.forward
+ * (primitives.py:228, `x = x + self.attention(...)`): out [S, B, dim] = bf16(residual +
+ * bf16(to_o(attn))), residual [S, B, dim] bf16; out may be residual (in place). dim a
+ * multiple of 32. */
+MOSAIC_API int mosaic_attn_out_proj_residual(const void* attn, const void* w_o, const void* residual, void* out,
+                                             int* status, int seq_len, int batch, int dim, int num_q_heads,
+                                             int head_dim, void* stream);
+
+/* torch.nn.RMSNorm of bf16 rows (the norm1 / norm2 of MosaicBlock, primitives.py:225-226,
+ * with elementwise_affine weight or NULL): y = bf16(x * rsqrt(mean(x^2) + eps) * weight),
+ * fp32 arithmetic, the sum of squares in a fixed order. x, y [rows, dim] bf16 (y may be
+ * x), weight [dim] fp32 or NULL. dim a multiple of 8. */
+MOSAIC_API int mosaic_rms_norm(const void* x, const float* weight, void* y, int rows, int dim, float eps,
+                               void* stream);
+
 /* out [rows, out_features] = row_scale[r] * (a [rows, in_features] w^T) in bf16 (fp32
  * accumulation), row_scale optional (NULL = 1): a Linear layer without bias on the
  * tensor core. Serves CrossAttentionInterpolate's to_kv (primitives.py:275, with the
@@ -225,6 +240,27 @@ MOSAIC_API int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out
  * in_features a multiple of 64, out_features a multiple of 32. */
 MOSAIC_API int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
                              int in_features, int out_features, void* stream);
+
+/* out = residual + bf16(row_scale[r] * (a w^T)), rounded to bf16 once more: a Linear
+ * layer followed by a residual add, as `x = x + self.ffn(...)` in MosaicBlock.forward
+ * (primitives.py:229) with cSwiGLU's w2 (primitives.py:106) as the Linear. out may be
+ * residual itself (in place). Shapes and limits as mosaic_linear. */
+MOSAIC_API int mosaic_linear_residual(const void* a, const void* w, const void* residual, void* out,
+                                      const float* row_scale, int* status, int rows, int in_features,
+                                      int out_features, void* stream);
+
+/* First half of the conditional SwiGLU FFN of a Mosaic block (cSwiGLU.forward,
+ * primitives.py:102-106, with MosaicBlock's norm2, primitives.py:227, as row_scale):
+ * for x [rows, dim] bf16 with rows (s, b) of a sequence-first [S, batch, dim] tensor,
+ *   x1 = bf16(row_scale[r] * x w1^T), x3 = bf16(row_scale[r] * x w3^T)   (w13.chunk(2))
+ *   h [rows, hidden] = bf16(bf16(silu(bf16(x1 + noise[r % batch]))) * x3)
+ * with noise [batch, hidden] bf16 (noise_bias(z), NULL = none). w13 [2 hidden, dim]
+ * bf16 holds the rows of cSwiGLU.w13.weight interleaved in blocks of 128: rows
+ * [256 i, 256 i + 128) = w1 rows [128 i, 128 i + 128) and rows [256 i + 128, 256 i + 256)
+ * = the w3 rows of the same hidden units (w3 row j = w13 row hidden + j). dim a
+ * multiple of 64, hidden a multiple of 128, rows a multiple of batch. */
+MOSAIC_API int mosaic_ffn_swiglu(const void* x, const void* w13, const float* row_scale, const void* noise, void* h,
+                                 int* status, int rows, int dim, int hidden, int batch, void* stream);
 
 /* rinv[r] = 1 / sqrt(mean_d x[r, d]^2 + eps) for x [rows, dim] bf16: the row factor of
  * torch.nn.RMSNorm without an affine weight (the kv_norm of CrossAttentionInterpolate,

@@ -9,6 +9,9 @@ Public API (same signatures as the reference's ops.py / primitives.py):
     MosaicAttention(config, block_attn_only, no_compression=False)   # primitives.py:139-209
         (the whole attention block: fused projections + RoPE + gates, attention, to_o)
     CrossAttentionInterpolate(config)                                 # primitives.py:228-284
+    MosaicBlock(config, block_attn_only, no_compression=False)        # primitives.py:212-229
+        (attention block + fused FFN: norm2, w13 with noise / SiLU / product, w2 + residual)
+    MosaicSwiGLU(dim, hidden_dim, noise_dim)                          # primitives.py:92-106
 plus get_healpix_grid / rope_tables for the RoPE tables, `ensemble` for
 member-sharded multi-GPU runs and `streaming.StreamedAttention` for host-resident
 batches with their PCIe copies overlapped with the attention.
@@ -18,6 +21,8 @@ from .attention import MosaicAttention
 from . import interp
 from .interp import CrossAttentionInterpolate
 from . import updown
+from . import ffn
+from .ffn import MosaicBlock, MosaicSwiGLU
 from .updown import HEALPixDownsample, HEALPixUpsample
 from .healpix import get_healpix_grid, healpix_rope_tables, pix2ang_nest, rope_tables
 from .ops import mosaic_attn_bwd, mosaic_attn_fwd, mosaic_sparse_attn, mosaic_sparse_attn_with_lse
@@ -25,5 +30,5 @@ from .primitives import attn_topk, block_attention, block_pool, cmp_attention, m
 
 __all__ = [
     "mosaic_sparse_attn", "mosaic_sparse_attn_with_lse", "mosaic_attn_fwd", "mosaic_attn_bwd", "mosaic_attn_func", "attn_topk", "block_attention",
-    "block_pool", "cmp_attention", "MosaicAttention", "CrossAttentionInterpolate", "HEALPixDownsample", "HEALPixUpsample", "get_healpix_grid", "healpix_rope_tables", "pix2ang_nest", "rope_tables",
+    "block_pool", "cmp_attention", "MosaicAttention", "CrossAttentionInterpolate", "MosaicBlock", "MosaicSwiGLU", "HEALPixDownsample", "HEALPixUpsample", "get_healpix_grid", "healpix_rope_tables", "pix2ang_nest", "rope_tables",
 ]

@@ -88,9 +88,10 @@ def qkv_projection(x, w_qkvg, num_q_heads, num_kv_heads, rope_cos=None, rope_sin
     return q, k, v, g
 
 
-def out_projection(attn, w_o, status=None):
+def out_projection(attn, w_o, status=None, residual=None):
     """rearrange(attn, 'b s h d -> s b (h d)') @ w_o^T through mosaic_attn_out_proj:
-    attn [B, S, Hq, 64] -> [S, B, dim] bf16."""
+    attn [B, S, Hq, 64] -> [S, B, dim] bf16; with `residual` [S, B, dim] bf16 the result
+    is residual + that, rounded again (mosaic_attn_out_proj_residual)."""
     _require_cuda(attn, w_o)
     B, S, Hq, D = attn.shape
     dim = w_o.shape[0]
@@ -100,9 +101,16 @@ def out_projection(attn, w_o, status=None):
     out = torch.empty(S, B, dim, dtype=torch.bfloat16, device=attn.device)
     lib = _lib.load()
     with torch.cuda.device(attn.device):
-        rc = lib.mosaic_attn_out_proj(_ptr(ab), _ptr(wb), _ptr(out), _ptr(status), S, B, dim, Hq, D,
-                                      _stream_ptr(attn.device))
-    _lib.check("mosaic_attn_out_proj", rc)
+        if residual is None:
+            rc = lib.mosaic_attn_out_proj(_ptr(ab), _ptr(wb), _ptr(out), _ptr(status), S, B, dim, Hq, D,
+                                          _stream_ptr(attn.device))
+        else:
+            rb = _bf16c(residual)
+            if tuple(rb.shape) != (S, B, dim):
+                raise ValueError(f"residual must be [{S}, {B}, {dim}], got {tuple(rb.shape)}")
+            rc = lib.mosaic_attn_out_proj_residual(_ptr(ab), _ptr(wb), _ptr(rb), _ptr(out), _ptr(status), S, B, dim,
+                                                   Hq, D, _stream_ptr(attn.device))
+    _lib.check("mosaic_attn_out_proj" if residual is None else "mosaic_attn_out_proj_residual", rc)
     return out
 
 
@@ -154,7 +162,10 @@ class MosaicAttention(nn.Module):
                 raise ValueError("q_rope and k_rope must hold the same tables (both come from the same grid)")
             self._rope_key = key
 
-    def forward(self, x):
+    def forward(self, x, residual=None):
+        """The block's attention on x [S, B, dim]; with `residual` (a bf16 [S, B, dim]
+        tensor, mosaic_b200.MosaicBlock passes the stream before norm1) it returns
+        residual + attention(x), the add done in the output projection's epilogue."""
         if torch.is_grad_enabled() and (x.requires_grad or any(p_.requires_grad for p_ in self.parameters())):
             raise NotImplementedError(
                 "mosaic_b200.MosaicAttention serves inference (the fused projections have no backward); "
@@ -170,4 +181,6 @@ class MosaicAttention(nn.Module):
             self.q_rope.cos_freqs if rope else None, self.q_rope.sin_freqs if rope else None, with_gates)
         out = mosaic_attn_func(q, k, v, g, self.block_attn_size, self.sparse_block_size, self.sparse_block_count,
                                self.block_attn_only, self.no_compression)
+        if residual is not None:
+            return out_projection(out, self.to_o.weight, residual=residual)
         return out_projection(out, self.to_o.weight).to(x.dtype)

@@ -497,6 +497,30 @@ int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* stat
   return launch_out_proj(a, static_cast<cudaStream_t>(stream));
 }
 
+int mosaic_attn_out_proj_residual(const void* attn, const void* w_o, const void* residual, void* out, int* status,
+                                  int seq_len, int batch, int dim, int num_q_heads, int head_dim, void* stream) {
+  if (seq_len < 0 || batch < 0 || dim <= 0 || num_q_heads <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
+  if (dim % 32 != 0) return MOSAIC_ERR_UNSUPPORTED;  // whole 32-column chunks of residual and output rows
+  if (seq_len == 0 || batch == 0) return MOSAIC_OK;
+  if (!attn || !w_o || !residual || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(attn) || !aligned16(w_o) || !aligned16(residual) || !aligned16(out))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  OutProjLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  a.attn = attn; a.w = w_o; a.out = out; a.residual = residual; a.status = status;
+  a.S = seq_len; a.B = batch; a.dim = dim; a.Hq = num_q_heads;
+  return launch_out_proj(a, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_rms_norm(const void* x, const float* weight, void* y, int rows, int dim, float eps, void* stream) {
+  if (rows < 0 || dim <= 0 || !(eps >= 0.f)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dim % 8 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (rows == 0) return MOSAIC_OK;
+  if (!x || !y || !aligned16(x) || !aligned16(y) || (weight && !aligned16(weight))) return MOSAIC_ERR_INVALID_ARGUMENT;
+  return launch_rms_norm(x, y, weight, rows, dim, eps, static_cast<cudaStream_t>(stream));
+}
+
 int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
                   int in_features, int out_features, void* stream) {
   if (rows < 0 || in_features <= 0 || out_features <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
@@ -510,6 +534,36 @@ int mosaic_linear(const void* a, const void* w, void* out, const float* row_scal
   l.a = a; l.w = w; l.out = out; l.rscale = row_scale; l.status = status;
   l.M = rows; l.K = in_features; l.N = out_features;
   return launch_linear(l, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_linear_residual(const void* a, const void* w, const void* residual, void* out, const float* row_scale,
+                           int* status, int rows, int in_features, int out_features, void* stream) {
+  if (rows < 0 || in_features <= 0 || out_features <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (in_features % 64 != 0 || out_features % 32 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (rows == 0) return MOSAIC_OK;
+  if (!a || !w || !residual || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(residual) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  LinearLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.a = a; l.w = w; l.out = out; l.rscale = row_scale; l.residual = residual; l.status = status;
+  l.M = rows; l.K = in_features; l.N = out_features;
+  return launch_linear(l, static_cast<cudaStream_t>(stream));
+}
+
+int mosaic_ffn_swiglu(const void* x, const void* w13, const float* row_scale, const void* noise, void* h, int* status,
+                      int rows, int dim, int hidden, int batch, void* stream) {
+  if (rows < 0 || dim <= 0 || hidden <= 0 || batch <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (rows % batch != 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dim % 64 != 0 || hidden % 128 != 0) return MOSAIC_ERR_UNSUPPORTED;
+  if (rows == 0) return MOSAIC_OK;
+  if (!x || !w13 || !h) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(w13) || !aligned16(h) || (noise && !aligned16(noise)))
+    return MOSAIC_ERR_INVALID_ARGUMENT;
+  SwigluLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.x = x; l.w13 = w13; l.rscale = row_scale; l.noise = noise; l.h = h; l.status = status;
+  l.M = rows; l.dim = dim; l.hidden = hidden; l.B = batch;
+  return launch_swiglu(l, static_cast<cudaStream_t>(stream));
 }
 
 int mosaic_row_rms(const void* x, float* rinv, int rows, int dim, float eps, void* stream) {

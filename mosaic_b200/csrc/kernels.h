@@ -115,19 +115,34 @@ struct QkvProjLaunch {
   int S, B, dim, Hq, Hk;
 };
 struct OutProjLaunch {
-  const void* attn;  // [B, S, Hq*64] bf16
-  const void* w;     // [dim, Hq*64] bf16 (to_o.weight)
-  void* out;         // [S, B, dim] bf16
+  const void* attn;      // [B, S, Hq*64] bf16
+  const void* w;         // [dim, Hq*64] bf16 (to_o.weight)
+  void* out;             // [S, B, dim] bf16
+  const void* residual;  // [S, B, dim] bf16 added to the rounded output (may alias out) or null
   int* status;
   int S, B, dim, Hq;
 };
 struct LinearLaunch {
-  const void* a;        // [M, K] bf16
-  const void* w;        // [N, K] bf16
-  void* out;            // [M, N] bf16
-  const float* rscale;  // [M] fp32 row factors or null
+  const void* a;         // [M, K] bf16
+  const void* w;         // [N, K] bf16
+  void* out;             // [M, N] bf16
+  const float* rscale;   // [M] fp32 row factors or null
+  const void* residual;  // [M, N] bf16 added to the rounded output (may alias out) or null
   int* status;
   int M, K, N;
+};
+// First half of the conditional SwiGLU FFN (proj.cu, mode kSwiGLU):
+// h = bf16(bf16(silu(bf16(x1 + noise[b]))) * x3) with x1, x3 = bf16(rscale * (x w1^T)),
+// bf16(rscale * (x w3^T)).
+struct SwigluLaunch {
+  const void* x;         // [M, dim] bf16: rows (s, b) of x [S, B, dim]
+  const void* w13;       // [2 hidden, dim] bf16, rows interleaved in blocks of 128: w1 rows
+                         // [128 i, 128 i + 128) then the w3 rows of the same hidden units
+  const float* rscale;   // [M] fp32 row factors (the RMSNorm in front) or null
+  const void* noise;     // [B, hidden] bf16 (the block's noise_bias(z)) or null
+  void* h;               // [M, hidden] bf16
+  int* status;
+  int M, dim, hidden, B;
 };
 // Cross-attention interpolation (interp.cu).
 struct InterpLaunch {
@@ -174,9 +189,12 @@ int launch_qkv_proj(const QkvProjLaunch& a, cudaStream_t stream);
 int launch_interp_tiled(const InterpTiledLaunch& a, cudaStream_t stream);
 size_t tiled_interp_smem_bytes(int max_union, int H, int k);
 int launch_linear(const LinearLaunch& a, cudaStream_t stream);
+int launch_swiglu(const SwigluLaunch& a, cudaStream_t stream);
 int launch_interp_attend(const InterpLaunch& a, cudaStream_t stream);
 int launch_row_rms(const void* x, float* rinv, long long rows, int dim, float eps, cudaStream_t stream);
 int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream);
+// y = bf16(x * rsqrt(mean(x^2) + eps) (* w)) per row of x [rows, D] bf16 (y may be x).
+int launch_rms_norm(const void* x, void* y, const float* w, long long rows, int D, float eps, cudaStream_t stream);
 
 int launch_engine(const EngineLaunch& a, cudaStream_t stream);
 int launch_pool(const PoolLaunch& a, cudaStream_t stream);

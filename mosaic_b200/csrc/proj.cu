@@ -31,6 +31,15 @@
 //                spans several column tiles): one warp per row sums the squares of the
 //                stored bf16 values in a fixed order, so the result is deterministic
 //                and equals RMSNorm of the bf16 tensor the reference normalises.
+//   mode kSwiGLU: the first half of the conditional SwiGLU FFN (cSwiGLU.forward,
+//                primitives.py:102-106) with the RMSNorm in front of it
+//                (MosaicBlock.norm2, primitives.py:227) folded in as a row factor: the
+//                host interleaves w13's rows in blocks of 128 (w1 rows j..j+127, then
+//                the w3 rows of the same hidden units), so one 256-column tile holds
+//                x1 and x3 of 128 hidden units and the epilogue forms
+//                bf16(silu(bf16(x1 + noise[b])) * x3) with every tensor op's bf16
+//                rounding; the chunk(2) views and the elementwise passes over them
+//                never exist. kLinear with a residual then gives x + w2(h).
 //
 // Tiles of 128 rows x 256 columns, K in 64-wide stages (TMA, 128-byte swizzle, 4-stage
 // ring), fp32 accumulators double-buffered in TMEM so the epilogue of one tile runs
@@ -53,7 +62,7 @@ constexpr int kPABytes = kPBM * kPBK * 2;   // 16 KB
 constexpr int kPBBytes = kPBN * kPBK * 2;   // 32 KB
 constexpr int kPStageBytes = kPABytes + kPBBytes;
 
-enum ProjMode : int { kQkv = 0, kPlain = 1, kLinear = 2, kDown = 3, kUp = 4 };
+enum ProjMode : int { kQkv = 0, kPlain = 1, kLinear = 2, kDown = 3, kUp = 4, kSwiGLU = 5 };
 
 struct ProjParams {
   CUtensorMap tm_a, tm_w;
@@ -66,7 +75,9 @@ struct ProjParams {
   __nv_bfloat16* out;      // kPlain, kLinear
   const float* rscale;     // kLinear: per-row factor or null
   const __nv_bfloat16* pos;       // kDown / kUp: [n, N] bias rows
-  const __nv_bfloat16* shortcut;  // kUp: [(n f), B, out_dim] or null
+  const __nv_bfloat16* shortcut;  // kUp: [(n f), B, out_dim]; kLinear: residual [M, N]; or null
+  const __nv_bfloat16* noise;     // kSwiGLU: [B, hidden] or null
+  int hidden;                     // kSwiGLU: output columns (N / 2)
   int F, out_dim, member, c_blocks;
   int a3d;                        // A is the 3D map (c, f, n) of kDown
   int* status;
@@ -160,18 +171,59 @@ __device__ __forceinline__ void pack_chunk_res(uint32_t (&packed)[16], const uin
   }
 }
 
-// RMSNorm of stored rows in place: y = bf16(y * rsqrt(mean(y^2) + eps) (* w)), one warp per
-// row. The sum of squares is taken over the stored bf16 values, each lane over its
-// 16-byte chunks in order and the lanes by a fixed butterfly, so it is deterministic.
-__global__ void __launch_bounds__(256) rms_apply_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ w,
-                                                        long long rows, int D, float eps) {
+// 16 words (32 bf16 values) of a row segment, zero when src is null. Plain (coherent)
+// loads: a kLinear residual may be the output tensor itself.
+__device__ __forceinline__ void load_words16(uint32_t (&w)[16], const __nv_bfloat16* src) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 t = src != nullptr ? reinterpret_cast<const uint4*>(src)[i] : make_uint4(0, 0, 0, 0);
+    w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+  }
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// torch's SiLU in fp32 (x / (1 + exp(-x)), the op math of a bf16 tensor), rounded.
+__device__ __forceinline__ float silu_bf16(float t) { return bf16_round(t / (1.0f + expf(-t))); }
+
+// 32 hidden units of one row for kSwiGLU from the x1 and x3 accumulators:
+// bf16(bf16(silu(bf16(bf16(rs a1) + noise))) * bf16(rs a3)).
+__device__ __forceinline__ void pack_chunk_swiglu(uint32_t (&packed)[16], const uint32_t (&a1)[32],
+                                                  const uint32_t (&a3)[32], const uint32_t (&nw)[16], float rs) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float x1a = bf16_round(__uint_as_float(a1[2 * i]) * rs), x1b = bf16_round(__uint_as_float(a1[2 * i + 1]) * rs);
+    const float x3a = bf16_round(__uint_as_float(a3[2 * i]) * rs), x3b = bf16_round(__uint_as_float(a3[2 * i + 1]) * rs);
+    const float ta = bf16_round(x1a + bf16_lo(nw[i])), tb = bf16_round(x1b + bf16_hi(nw[i]));
+    packed[i] = pack_bf16x2(silu_bf16(ta) * x3a, silu_bf16(tb) * x3b);
+  }
+}
+
+// 32 output columns of one row for kLinear with a residual: bf16(bf16(rs acc) + res).
+__device__ __forceinline__ void pack_chunk_residual(uint32_t (&packed)[16], const uint32_t (&acc)[32],
+                                                    const uint32_t (&rw)[16], float rs) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    packed[i] = pack_bf16x2(bf16_round(__uint_as_float(acc[2 * i]) * rs) + bf16_lo(rw[i]),
+                            bf16_round(__uint_as_float(acc[2 * i + 1]) * rs) + bf16_hi(rw[i]));
+}
+
+// RMSNorm of bf16 rows: y = bf16(x * rsqrt(mean(x^2) + eps) (* w)), one warp per row,
+// in place when y == x (the resampling layers) or into another tensor (the norms of a
+// Mosaic block, torch.nn.RMSNorm with the same fp32 arithmetic). The sum of squares is
+// taken over the bf16 values, each lane over its 16-byte chunks in order and the lanes
+// by a fixed butterfly, so it is deterministic.
+__global__ void __launch_bounds__(256) rms_apply_kernel(const __nv_bfloat16* x, __nv_bfloat16* y,
+                                                        const float* __restrict__ w, long long rows, int D, float eps) {
   const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
+  const __nv_bfloat16* xr = x + row * D;
   __nv_bfloat16* yr = y + row * D;
   float ss = 0.f;
   for (int c = lane * 8; c < D; c += 256) {
-    const uint4 v = *reinterpret_cast<const uint4*>(yr + c);
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
     const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -183,7 +235,7 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(__nv_bfloat16* __restric
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float r = rsqrtf(ss / static_cast<float>(D) + eps);
   for (int c = lane * 8; c < D; c += 256) {
-    uint4 v = *reinterpret_cast<const uint4*>(yr + c);
+    uint4 v = *reinterpret_cast<const uint4*>(xr + c);
     uint32_t wd[4] = {v.x, v.y, v.z, v.w};
     float wt[8];
     if (w != nullptr) {
@@ -346,6 +398,39 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
       const int m = mt * kPBM + row;
       const bool live = m < p.M;
       const uint32_t tacc = tmem + lane_off + 256u * a;
+      if constexpr (kMode == kSwiGLU) {
+        // Tile nt holds x1 of hidden units [128 nt, 128 nt + 128) in columns 0-127 and x3
+        // of the same units in columns 128-255; warpgroup `half` forms units
+        // j0 + [0, 64), two chunks of 32. Rows are (s, b): member b = m % B.
+        const int j0 = nt * 128 + 64 * half;
+        const float rs = live && p.rscale != nullptr ? __ldg(p.rscale + m) : 1.0f;
+        const __nv_bfloat16* nrow =
+            live && p.noise != nullptr ? p.noise + static_cast<size_t>(m % p.B) * p.hidden + j0 : nullptr;
+        uint32_t nw[2][16];
+        load_words16(nw[0], nrow);
+        load_words16(nw[1], nrow != nullptr ? nrow + 32 : nullptr);
+        if (!bounded_wait(&sm.acc_full[a], (it >> 1) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          uint32_t a1[32], a3[32];
+          tmem_ld32(tacc + 64 * half + 32 * k, a1);
+          tmem_ld32(tacc + 128 + 64 * half + 32 * k, a3);
+          tmem_ld_wait();
+          reg_fence<32>(a1);
+          reg_fence<32>(a3);
+          uint32_t packed[16];
+          pack_chunk_swiglu(packed, a1, a3, nw[k], rs);
+          warp_store_rows(stage, packed, live ? p.out + static_cast<size_t>(m) * p.hidden + j0 + 32 * k : nullptr,
+                          lane);
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.acc_empty[a]);
+        continue;
+      }
       if constexpr (kMode == kDown || kMode == kUp) {
         // The warpgroup's (up to) 4 chunks of 32 columns lie in one child block f
         // (out_dim % 128 == 0), so the output row and the bias row are fixed for the
@@ -406,22 +491,36 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
         if (kMode == kQkv && c0 == gbase + 32) continue;  // second gate chunk: taken with the first
         uint32_t acc[32];
         if (kMode == kPlain) {
+          // A rows are (b, s) (attention output), out rows (s, b)
+          const int b = m / p.S, s = m % p.S;
+          const size_t o = (static_cast<size_t>(s) * p.B + b) * p.N + c0;
+          uint32_t rw[16];
+          if (p.shortcut != nullptr) load_words16(rw, live ? p.shortcut + o : nullptr);
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
-          // A rows are (b, s) (attention output), out rows (s, b)
-          const int b = m / p.S, s = m % p.S;
           uint32_t packed[16];
-          pack_chunk(packed, acc);
-          warp_store_rows(stage, packed, live ? p.out + (static_cast<size_t>(s) * p.B + b) * p.N + c0 : nullptr, lane);
+          if (p.shortcut != nullptr)
+            pack_chunk_residual(packed, acc, rw, 1.0f);
+          else
+            pack_chunk(packed, acc);
+          warp_store_rows(stage, packed, live ? p.out + o : nullptr, lane);
           continue;
         }
         if (kMode == kLinear) {
+          const float rs = live && p.rscale != nullptr ? __ldg(p.rscale + m) : 1.0f;
+          uint32_t rw[16];
+          if (p.shortcut != nullptr) load_words16(rw, live ? p.shortcut + static_cast<size_t>(m) * p.N + c0 : nullptr);
           tmem_ld32(tacc + 32 * ci, acc);
           tmem_ld_wait();
           reg_fence<32>(acc);
           uint32_t packed[16];
-          pack_chunk(packed, acc, live && p.rscale != nullptr ? __ldg(p.rscale + m) : 1.0f);
+          if (p.shortcut != nullptr)
+            pack_chunk_residual(packed, acc, rw, rs);
+          else
+            pack_chunk(packed, acc, rs);
+          // with a residual the output may alias it: every lane of the warp has read its
+          // residual words before warp_store_rows writes any row
           warp_store_rows(stage, packed, live ? p.out + static_cast<size_t>(m) * p.N + c0 : nullptr, lane);
           continue;
         }
@@ -534,6 +633,7 @@ int launch_proj(ProjParams& p, cudaStream_t stream) {
     case kLinear: rc = set_proj_smem<kLinear>(dev); break;
     case kDown: rc = set_proj_smem<kDown>(dev); break;
     case kUp: rc = set_proj_smem<kUp>(dev); break;
+    case kSwiGLU: rc = set_proj_smem<kSwiGLU>(dev); break;
   }
   if (rc != MOSAIC_OK) return rc;
   const int sms = sm_count_p();
@@ -550,6 +650,7 @@ int launch_proj(ProjParams& p, cudaStream_t stream) {
       case kLinear: launch_proj_mode<kLinear>(p, grid, stream); break;
       case kDown: launch_proj_mode<kDown>(p, grid, stream); break;
       case kUp: launch_proj_mode<kUp>(p, grid, stream); break;
+      case kSwiGLU: launch_proj_mode<kSwiGLU>(p, grid, stream); break;
     }
   }
   return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
@@ -590,6 +691,7 @@ int launch_linear(const LinearLaunch& a, cudaStream_t stream) {
     return MOSAIC_ERR_CUDA;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.rscale = a.rscale;
+  p.shortcut = static_cast<const __nv_bfloat16*>(a.residual);
   p.status = a.status;
   p.mode = kLinear;
   p.M = a.M;
@@ -598,10 +700,33 @@ int launch_linear(const LinearLaunch& a, cudaStream_t stream) {
   return launch_proj(p, stream);
 }
 
+int launch_swiglu(const SwigluLaunch& a, cudaStream_t stream) {
+  ProjParams p;
+  memset(&p, 0, sizeof(p));
+  if (make_tmap_bf16_2d(&p.tm_a, a.x, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.dim)) ||
+      make_tmap_bf16_2d(&p.tm_w, a.w13, static_cast<uint64_t>(2) * a.hidden, static_cast<uint64_t>(a.dim)))
+    return MOSAIC_ERR_CUDA;
+  p.out = static_cast<__nv_bfloat16*>(a.h);
+  p.rscale = a.rscale;
+  p.noise = static_cast<const __nv_bfloat16*>(a.noise);
+  p.status = a.status;
+  p.mode = kSwiGLU;
+  p.M = a.M;
+  p.K = a.dim;
+  p.N = 2 * a.hidden;
+  p.hidden = a.hidden;
+  p.B = a.B;
+  return launch_proj(p, stream);
+}
+
 int launch_rms_apply(void* y, const float* w, long long rows, int D, float eps, cudaStream_t stream) {
+  return launch_rms_norm(y, y, w, rows, D, eps, stream);
+}
+
+int launch_rms_norm(const void* x, void* y, const float* w, long long rows, int D, float eps, cudaStream_t stream) {
   if (rows == 0) return MOSAIC_OK;
   rms_apply_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
-      static_cast<__nv_bfloat16*>(y), w, rows, D, eps);
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), w, rows, D, eps);
   return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
@@ -668,6 +793,7 @@ int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream) {
       make_tmap_bf16_2d(&p.tm_w, a.w, static_cast<uint64_t>(a.dim), static_cast<uint64_t>(kdim)))
     return MOSAIC_ERR_CUDA;
   p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.shortcut = static_cast<const __nv_bfloat16*>(a.residual);
   p.status = a.status;
   p.mode = kPlain;
   p.M = a.S * a.B;

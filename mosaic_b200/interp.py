@@ -25,7 +25,7 @@ import torch.nn as nn
 from . import _lib
 from .ops import _ptr, _require_cuda, _stream_ptr
 
-__all__ = ["CrossAttentionInterpolate", "rad_to_xyz", "knn_neighbors", "linear", "row_rms", "interp_attend",
+__all__ = ["CrossAttentionInterpolate", "rad_to_xyz", "knn_neighbors", "linear", "norm_eps", "row_rms", "interp_attend",
            "build_tiles", "interp_attend_tiled"]
 
 TILE_MAX_UNION = 80  # source points per tile (a multiple of 16: the tensor-core k step)
@@ -70,6 +70,14 @@ def linear(a, w, row_scale=None, status=None):
                                        _stream_ptr(a.device))
     _lib.check("mosaic_linear", rc)
     return out.reshape(*lead, n_out)
+
+
+def norm_eps(norm):
+    """The epsilon torch.nn.RMSNorm `norm` applies: its own eps, or when that is None the
+    epsilon of the op's math type, which is fp32 for bf16, fp16 and fp32 inputs alike
+    (torch upcasts half-precision inputs and takes numeric_limits<float>::epsilon), not
+    the input dtype's epsilon."""
+    return norm.eps if norm.eps is not None else torch.finfo(torch.float32).eps
 
 
 def row_rms(x, eps):
@@ -295,7 +303,7 @@ class CrossAttentionInterpolate(nn.Module):
                 "mosaic_b200.CrossAttentionInterpolate serves inference; run it under torch.no_grad() or "
                 "torch.inference_mode()")
         S_from = x_from.shape[0] if self.points_from is None else self.points_from
-        eps = self.kv_norm.eps if self.kv_norm.eps is not None else torch.finfo(x_from.dtype).eps
+        eps = norm_eps(self.kv_norm)
         w_kv = self.to_kv.weight
         if self.kv_norm.weight is not None:  # affine RMSNorm: fold the weight into to_kv's input columns
             w_kv = w_kv * self.kv_norm.weight.unsqueeze(0)

@@ -20,7 +20,7 @@ import torch.nn as nn
 
 from . import _lib
 from .healpix import get_healpix_grid
-from .interp import rad_to_xyz
+from .interp import norm_eps, rad_to_xyz
 from .ops import _ptr, _require_cuda, _stream_ptr
 
 __all__ = ["HEALPixDownsample", "HEALPixUpsample", "healpix_downsample", "healpix_upsample", "updown_rel_pos"]
@@ -88,7 +88,7 @@ class _UpDown(nn.Module):
         return self._pos_cache
 
     def _norm_args(self, x):
-        eps = self.norm.eps if self.norm.eps is not None else torch.finfo(x.dtype).eps
+        eps = norm_eps(self.norm)
         return eps, self.norm.weight
 
     def _check_inference(self, *xs):

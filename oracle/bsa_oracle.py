@@ -346,6 +346,22 @@ def cross_attention_interpolate(x_from, neighbors, rel_pos, w_q, w_kv, w_o, num_
     return out @ w_o.float().t()
 
 
+def swiglu_ffn(x, w13, w2, noise_w=None, z=None):
+    """cSwiGLU.forward (primitives.py:102-106), fp32: x [S, B, dim], z [B, noise_dim];
+    x1, x3 = (x w13^T).chunk(2); w2(silu(x1 + noise_bias(z)) * x3)."""
+    xf = x.float()
+    x1, x3 = (xf @ w13.float().t()).chunk(2, dim=-1)
+    noise = (z.float() @ noise_w.float().t()).unsqueeze(0) if z is not None else 0.0
+    return (torch.nn.functional.silu(x1 + noise) * x3) @ w2.float().t()
+
+
+def mosaic_block_ffn(x, z, w13, w2, noise_w, eps, norm_weight=None):
+    """The FFN half of MosaicBlock.forward (primitives.py:229), fp32:
+    x + ffn(norm2(x), z) with norm2 = torch.nn.RMSNorm (times norm_weight when affine)."""
+    xf = x.float()
+    return xf + swiglu_ffn(rms_norm(xf, eps, norm_weight), w13, w2, noise_w, z)
+
+
 def rad_to_xyz(lonlat):
     """utils.rad_to_xyz (utils.py:7-16): (lon, lat) radians -> unit xyz."""
     lon, lat = lonlat[..., 0], lonlat[..., 1]

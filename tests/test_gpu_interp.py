@@ -117,7 +117,7 @@ def test_module_above_32_neighbours_takes_untiled_kernel():
     assert m._tiles() is None
     with torch.no_grad():
         out = m(x.to(DEV))
-    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 4, torch.finfo(torch.bfloat16).eps)
+    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 4, torch.finfo(torch.float32).eps)
     close_rel(out, ref)
 
 
@@ -137,7 +137,7 @@ def test_module_after_state_dict_load_rebuilds_tiles():
         lin.to(torch.bfloat16)
     with torch.no_grad():
         out = m2(x.to(DEV))
-    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 4, torch.finfo(torch.bfloat16).eps)
+    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 4, torch.finfo(torch.float32).eps)
     close_rel(out, ref)
 
 
@@ -191,7 +191,7 @@ def test_module_matches_oracle(cfg):
     with torch.no_grad():
         out = m(x.to(DEV))
     assert out.shape == (pt.shape[0], B, dim) and out.dtype == torch.bfloat16
-    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, H, torch.finfo(torch.bfloat16).eps)
+    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, H, torch.finfo(torch.float32).eps)
     close_rel(out, ref)
 
 
@@ -218,7 +218,7 @@ def test_full_size_ll_to_healpix():
     m, x, (w_q, w_kv, w_o) = module(768, 12, 24, pf, pt, nb, seed=7, B=1)
     with torch.no_grad():
         out = m(x.to(DEV))
-    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 12, torch.finfo(torch.bfloat16).eps)
+    ref = O.cross_attention_interpolate(x, nb, rel, w_q, w_kv, w_o, 12, torch.finfo(torch.float32).eps)
     close_rel(out, ref)
 
 
