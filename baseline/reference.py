@@ -211,3 +211,31 @@ def build_model(ref, device, ours=True, dtype=None, seed=0):
     if dtype is not None:
         model = model.to(dtype)
     return model.eval()
+
+
+def profile_step(members=2, ours=True):
+    """One forward step of the era5 U-Net (bf16, `members` ensemble members) on cuda:0
+    after three warm-up steps, inside the NVTX range "unet_step", so that a profiler
+    can take exactly that step's launches (ncu --nvtx --nvtx-include "unet_step/")."""
+    import torch
+
+    dev = torch.device("cuda:0")
+    ref = load(dev)
+    model = build_model(ref, dev, ours=ours, dtype=torch.bfloat16, seed=0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(1, 1, 2, GRID_LON, GRID_LAT, 82, generator=g, device=dev).bfloat16()
+    dyt = torch.rand(1, 1, 2, generator=g, device=dev).bfloat16()
+    with torch.no_grad():
+        for _ in range(3):
+            model(x, dyt, members)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("unet_step")
+        out = model(x, dyt, members)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    return out
+
+
+if __name__ == "__main__":
+    # python -m baseline.reference [members] [ref]: one profiled U-Net step (see profile_step)
+    profile_step(int(sys.argv[1]) if len(sys.argv) > 1 else 2, ours=not (len(sys.argv) > 2 and sys.argv[2] == "ref"))
