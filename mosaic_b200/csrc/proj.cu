@@ -184,8 +184,11 @@ __device__ __forceinline__ void load_words16(uint32_t (&w)[16], const __nv_bfloa
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// torch's SiLU in fp32 (x / (1 + exp(-x)), the op math of a bf16 tensor), rounded.
-__device__ __forceinline__ float silu_bf16(float t) { return bf16_round(t / (1.0f + expf(-t))); }
+// torch's SiLU in fp32 (x / (1 + exp(-x)), the op math of a bf16 tensor), rounded to
+// bf16. The exponential and the division are the MUFU forms (a few fp32 ulps, far below
+// the 2^-9 of the rounding that follows); with the accurate library forms the
+// epilogue took as long as the tile's MMAs (U-Net step 409 ms against 388 ms).
+__device__ __forceinline__ float silu_bf16(float t) { return bf16_round(__fdividef(t, 1.0f + __expf(-t))); }
 
 // 32 hidden units of one row for kSwiGLU from the x1 and x3 accumulators:
 // bf16(bf16(silu(bf16(bf16(rs a1) + noise))) * bf16(rs a3)).
