@@ -109,13 +109,21 @@ __device__ __forceinline__ bool wait_noabort_p(uint64_t* bar, uint32_t parity, i
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Both values rounded to bf16 (nearest even) by one packed conversion: the scalar
+// conversion of bf16_round runs on the MUFU / XU pipe, which the SwiGLU epilogue's
+// exponentials and reciprocals need; the packed one does not compete for it.
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t u = pack_bf16x2(a, b);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xffff0000u);
+}
+
 // 32 consecutive output columns of one row (fp32 accumulators) -> packed bf16 words,
 // each scaled by `rs` first (kLinear's row factor; 1 otherwise).
 __device__ __forceinline__ void pack_chunk(uint32_t (&packed)[16], const uint32_t (&acc)[32], float rs = 1.0f) {
 #pragma unroll
   for (int i = 0; i < 16; ++i)
-    packed[i] = pack_bf16x2(bf16_round(__uint_as_float(acc[2 * i]) * rs),
-                            bf16_round(__uint_as_float(acc[2 * i + 1]) * rs));
+    packed[i] = pack_bf16x2(__uint_as_float(acc[2 * i]) * rs, __uint_as_float(acc[2 * i + 1]) * rs);
 }
 
 // Stores a warp's 32 rows x 32 bf16 columns (row = lane, `packed` its 16 words, `dst`
@@ -160,12 +168,14 @@ __device__ __forceinline__ void pack_chunk_res(uint32_t (&packed)[16], const uin
   const bool sc = has_sc;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
-    x0 = bf16_round(x0 + __uint_as_float(pw[i] << 16));
-    x1 = bf16_round(x1 + __uint_as_float(pw[i] & 0xffff0000u));
+    float x0 = __uint_as_float(acc[2 * i]), x1 = __uint_as_float(acc[2 * i + 1]);
+    bf16_round2(x0, x1);
+    x0 += __uint_as_float(pw[i] << 16);
+    x1 += __uint_as_float(pw[i] & 0xffff0000u);
     if (sc) {
-      x0 = bf16_round(x0 + __uint_as_float(sw[i] << 16));
-      x1 = bf16_round(x1 + __uint_as_float(sw[i] & 0xffff0000u));
+      bf16_round2(x0, x1);
+      x0 += __uint_as_float(sw[i] << 16);
+      x1 += __uint_as_float(sw[i] & 0xffff0000u);
     }
     packed[i] = pack_bf16x2(x0, x1);
   }
@@ -184,11 +194,11 @@ __device__ __forceinline__ void load_words16(uint32_t (&w)[16], const __nv_bfloa
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// torch's SiLU in fp32 (x / (1 + exp(-x)), the op math of a bf16 tensor), rounded to
-// bf16. The exponential and the division are the MUFU forms (a few fp32 ulps, far below
-// the 2^-9 of the rounding that follows); with the accurate library forms the
-// epilogue took as long as the tile's MMAs (U-Net step 409 ms against 388 ms).
-__device__ __forceinline__ float silu_bf16(float t) { return bf16_round(__fdividef(t, 1.0f + __expf(-t))); }
+// torch's SiLU in fp32 (x / (1 + exp(-x)), the op math of a bf16 tensor), before its
+// rounding to bf16. The exponential and the division are the MUFU forms (a few fp32
+// ulps, far below the 2^-9 of the rounding that follows); with the accurate library
+// forms the epilogue took as long as the tile's MMAs (U-Net step 409 ms against 388 ms).
+__device__ __forceinline__ float silu_f32(float t) { return __fdividef(t, 1.0f + __expf(-t)); }
 
 // 32 hidden units of one row for kSwiGLU from the x1 and x3 accumulators:
 // bf16(bf16(silu(bf16(bf16(rs a1) + noise))) * bf16(rs a3)).
@@ -196,10 +206,15 @@ __device__ __forceinline__ void pack_chunk_swiglu(uint32_t (&packed)[16], const 
                                                   const uint32_t (&a3)[32], const uint32_t (&nw)[16], float rs) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const float x1a = bf16_round(__uint_as_float(a1[2 * i]) * rs), x1b = bf16_round(__uint_as_float(a1[2 * i + 1]) * rs);
-    const float x3a = bf16_round(__uint_as_float(a3[2 * i]) * rs), x3b = bf16_round(__uint_as_float(a3[2 * i + 1]) * rs);
-    const float ta = bf16_round(x1a + bf16_lo(nw[i])), tb = bf16_round(x1b + bf16_hi(nw[i]));
-    packed[i] = pack_bf16x2(silu_bf16(ta) * x3a, silu_bf16(tb) * x3b);
+    float x1a = __uint_as_float(a1[2 * i]) * rs, x1b = __uint_as_float(a1[2 * i + 1]) * rs;
+    float x3a = __uint_as_float(a3[2 * i]) * rs, x3b = __uint_as_float(a3[2 * i + 1]) * rs;
+    bf16_round2(x1a, x1b);
+    bf16_round2(x3a, x3b);
+    float ta = x1a + bf16_lo(nw[i]), tb = x1b + bf16_hi(nw[i]);
+    bf16_round2(ta, tb);
+    float sa = silu_f32(ta), sb = silu_f32(tb);
+    bf16_round2(sa, sb);
+    packed[i] = pack_bf16x2(sa * x3a, sb * x3b);
   }
 }
 
@@ -207,9 +222,11 @@ __device__ __forceinline__ void pack_chunk_swiglu(uint32_t (&packed)[16], const 
 __device__ __forceinline__ void pack_chunk_residual(uint32_t (&packed)[16], const uint32_t (&acc)[32],
                                                     const uint32_t (&rw)[16], float rs) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    packed[i] = pack_bf16x2(bf16_round(__uint_as_float(acc[2 * i]) * rs) + bf16_lo(rw[i]),
-                            bf16_round(__uint_as_float(acc[2 * i + 1]) * rs) + bf16_hi(rw[i]));
+  for (int i = 0; i < 16; ++i) {
+    float a = __uint_as_float(acc[2 * i]) * rs, b = __uint_as_float(acc[2 * i + 1]) * rs;
+    bf16_round2(a, b);
+    packed[i] = pack_bf16x2(a + bf16_lo(rw[i]), b + bf16_hi(rw[i]));
+  }
 }
 
 // RMSNorm of bf16 rows: y = bf16(x * rsqrt(mean(x^2) + eps) (* w)), one warp per row,
@@ -278,7 +295,8 @@ __device__ __forceinline__ void pack_chunk_tab(uint32_t (&packed)[16], const uin
                                                const float (&cs)[16], const float (&sn)[16], bool rot) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float x0 = bf16_round(__uint_as_float(acc[2 * i])), x1 = bf16_round(__uint_as_float(acc[2 * i + 1]));
+    float x0 = __uint_as_float(acc[2 * i]), x1 = __uint_as_float(acc[2 * i + 1]);
+    bf16_round2(x0, x1);
     if (rot) {
       const float o0 = __fadd_rn(__fmul_rn(x0, cs[i]), __fmul_rn(-x1, sn[i]));
       const float o1 = __fadd_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x0, sn[i]));
