@@ -181,7 +181,7 @@ def build_model(ref, device, ours=True, dtype=None, seed=0):
     (`_MosaicBlock`, whose attention is mosaic_b200.MosaicAttention and whose FFN is the
     fused mosaic_b200.MosaicSwiGLU), primitives.MosaicAttention,
     mosaic.CrossAttentionInterpolate, mosaic.HEALPixDownsample and
-    mosaic.HEALPixUpsample (as INTEGRATION.md describes); ours=False restores the
+    mosaic.HEALPixUpsample (the names those classes are looked up by); ours=False restores the
     reference's own classes. Either way the HEALPix pixel centres come from
     mosaic_b200.healpix (the reference's utils.get_healpix_grid needs healpy, which is
     not installed here)."""

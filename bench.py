@@ -856,8 +856,8 @@ UNET_TFLOP_PER_MEMBER = 11.45  # FlopCounterMode on the reference model at the e
 def model_leg(dev, rank, world, dist, stream, steps, warmup):
     """One 24-member forward step of the whole Mosaic U-Net: the reference's own
     Transformer (mosaic.py, era5 preset, random weights, from baseline/_ref) with
-    mosaic_b200's attention block, interpolation and resampling modules rebound into it
-    (INTEGRATION.md), bf16. Members are sharded over the ranks (num_noise_samples =
+    mosaic_b200's transformer block (attention block + fused FFN), interpolation and
+    resampling modules rebound into it (baseline.reference.build_model), bf16. Members are sharded over the ranks (num_noise_samples =
     24 / N each, the model's own member batching, mosaic.py:300-308) and the output
     fields [1, members, 240, 121, 82] are all-gathered over NCCL inside the timed step.
     Also: the same step captured in one CUDA graph (forward only; replayed, then the
