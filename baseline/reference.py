@@ -213,19 +213,27 @@ def build_model(ref, device, ours=True, dtype=None, seed=0):
     return model.eval()
 
 
-def profile_step(members=2, ours=True):
-    """One forward step of the era5 U-Net (bf16, `members` ensemble members) on cuda:0
-    after three warm-up steps, inside the NVTX range "unet_step", so that a profiler
-    can take exactly that step's launches (ncu --nvtx --nvtx-include "unet_step/")."""
+def profile_step(members=2, ours=True, autocast=False):
+    """One forward step of the era5 U-Net (`members` ensemble members) on cuda:0 after
+    three warm-up steps, inside the NVTX range "unet_step", so that a profiler can take
+    exactly that step's launches (ncu --nvtx --nvtx-include "unet_step/"). bf16 weights
+    and inputs, or with `autocast` fp32 weights and inputs under fp16 autocast (the
+    reference rollout's setting, inference.py:59,379)."""
+    import contextlib
+
     import torch
 
     dev = torch.device("cuda:0")
     ref = load(dev)
-    model = build_model(ref, dev, ours=ours, dtype=torch.bfloat16, seed=0)
+    dt = None if autocast else torch.bfloat16
+    model = build_model(ref, dev, ours=ours, dtype=dt, seed=0)
     g = torch.Generator(device=dev).manual_seed(5)
-    x = torch.randn(1, 1, 2, GRID_LON, GRID_LAT, 82, generator=g, device=dev).bfloat16()
-    dyt = torch.rand(1, 1, 2, generator=g, device=dev).bfloat16()
-    with torch.no_grad():
+    x = torch.randn(1, 1, 2, GRID_LON, GRID_LAT, 82, generator=g, device=dev)
+    dyt = torch.rand(1, 1, 2, generator=g, device=dev)
+    if not autocast:
+        x, dyt = x.bfloat16(), dyt.bfloat16()
+    ctx = torch.autocast("cuda", dtype=torch.float16) if autocast else contextlib.nullcontext()
+    with torch.no_grad(), ctx:
         for _ in range(3):
             model(x, dyt, members)
         torch.cuda.synchronize()
@@ -237,5 +245,6 @@ def profile_step(members=2, ours=True):
 
 
 if __name__ == "__main__":
-    # python -m baseline.reference [members] [ref]: one profiled U-Net step (see profile_step)
-    profile_step(int(sys.argv[1]) if len(sys.argv) > 1 else 2, ours=not (len(sys.argv) > 2 and sys.argv[2] == "ref"))
+    # python -m baseline.reference [members] [ref] [autocast]: one profiled U-Net step (see profile_step)
+    profile_step(int(sys.argv[1]) if len(sys.argv) > 1 else 2, ours="ref" not in sys.argv[2:],
+                 autocast="autocast" in sys.argv[2:])

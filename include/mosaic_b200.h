@@ -219,18 +219,20 @@ MOSAIC_API int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out
                                     int batch, int dim, int num_q_heads, int head_dim, void* stream);
 
 /* mosaic_attn_out_proj followed by the residual add of MosaicBlock.forward
- * (primitives.py:228, `x = x + self.attention(...)`): out [S, B, dim] = bf16(residual +
- * bf16(to_o(attn))), residual [S, B, dim] bf16; out may be residual (in place). dim a
- * multiple of 32. */
+ * (primitives.py:228, `x = x + self.attention(...)`): out [S, B, dim] = T(residual +
+ * T(to_o(attn))) with T = dtype, the type of residual and out (bf16, or fp16: the
+ * block's residual stream under fp16 autocast, whose Linear outputs are fp16); attn and
+ * w_o bf16; out may be residual (in place). dim a multiple of 32. */
 MOSAIC_API int mosaic_attn_out_proj_residual(const void* attn, const void* w_o, const void* residual, void* out,
                                              int* status, int seq_len, int batch, int dim, int num_q_heads,
-                                             int head_dim, void* stream);
+                                             int head_dim, int dtype, void* stream);
 
-/* torch.nn.RMSNorm of bf16 rows (the norm1 / norm2 of MosaicBlock, primitives.py:225-226,
+/* torch.nn.RMSNorm of 16-bit rows (the norm1 / norm2 of MosaicBlock, primitives.py:225-226,
  * with elementwise_affine weight or NULL): y = bf16(x * rsqrt(mean(x^2) + eps) * weight),
- * fp32 arithmetic, the sum of squares in a fixed order. x, y [rows, dim] bf16 (y may be
- * x), weight [dim] fp32 or NULL. dim a multiple of 8. */
-MOSAIC_API int mosaic_rms_norm(const void* x, const float* weight, void* y, int rows, int dim, float eps,
+ * fp32 arithmetic, the sum of squares in a fixed order. x [rows, dim] of type dtype (bf16,
+ * or fp16 for a residual stream under fp16 autocast), y [rows, dim] bf16 (y may be x when
+ * x is bf16), weight [dim] fp32 or NULL. dim a multiple of 8. */
+MOSAIC_API int mosaic_rms_norm(const void* x, const float* weight, void* y, int rows, int dim, float eps, int dtype,
                                void* stream);
 
 /* out [rows, out_features] = row_scale[r] * (a [rows, in_features] w^T) in bf16 (fp32
@@ -241,13 +243,14 @@ MOSAIC_API int mosaic_rms_norm(const void* x, const float* weight, void* y, int 
 MOSAIC_API int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
                              int in_features, int out_features, void* stream);
 
-/* out = residual + bf16(row_scale[r] * (a w^T)), rounded to bf16 once more: a Linear
- * layer followed by a residual add, as `x = x + self.ffn(...)` in MosaicBlock.forward
- * (primitives.py:229) with cSwiGLU's w2 (primitives.py:106) as the Linear. out may be
- * residual itself (in place). Shapes and limits as mosaic_linear. */
+/* out = T(residual + T(row_scale[r] * (a w^T))) with T = dtype, the type of residual and
+ * out (bf16, or fp16 for a residual stream under fp16 autocast): a Linear layer followed
+ * by a residual add, as `x = x + self.ffn(...)` in MosaicBlock.forward (primitives.py:229)
+ * with cSwiGLU's w2 (primitives.py:106) as the Linear. a and w bf16. out may be residual
+ * itself (in place). Shapes and limits as mosaic_linear. */
 MOSAIC_API int mosaic_linear_residual(const void* a, const void* w, const void* residual, void* out,
                                       const float* row_scale, int* status, int rows, int in_features,
-                                      int out_features, void* stream);
+                                      int out_features, int dtype, void* stream);
 
 /* First half of the conditional SwiGLU FFN of a Mosaic block (cSwiGLU.forward,
  * primitives.py:102-106, with MosaicBlock's norm2, primitives.py:227, as row_scale):

@@ -59,9 +59,9 @@ SIGNATURES = {
     "mosaic_attn_qkv_proj": ([_vp] * 9 + [_i] * 6 + [_vp], _i),
     "mosaic_attn_out_proj": ([_vp] * 4 + [_i] * 5 + [_vp], _i),
     "mosaic_linear": ([_vp] * 5 + [_i] * 3 + [_vp], _i),
-    "mosaic_linear_residual": ([_vp] * 6 + [_i] * 3 + [_vp], _i),
-    "mosaic_attn_out_proj_residual": ([_vp] * 5 + [_i] * 5 + [_vp], _i),
-    "mosaic_rms_norm": ([_vp, _vp, _vp, _i, _i, _f, _vp], _i),
+    "mosaic_linear_residual": ([_vp] * 6 + [_i] * 4 + [_vp], _i),
+    "mosaic_attn_out_proj_residual": ([_vp] * 5 + [_i] * 6 + [_vp], _i),
+    "mosaic_rms_norm": ([_vp, _vp, _vp, _i, _i, _f, _i, _vp], _i),
     "mosaic_ffn_swiglu": ([_vp] * 6 + [_i] * 4 + [_vp], _i),
     "mosaic_row_rms": ([_vp, _vp, _i, _i, _f, _vp], _i),
     "mosaic_interp_attend": ([_vp] * 6 + [_i] * 6 + [_f, _vp], _i),

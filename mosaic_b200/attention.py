@@ -90,8 +90,8 @@ def qkv_projection(x, w_qkvg, num_q_heads, num_kv_heads, rope_cos=None, rope_sin
 
 def out_projection(attn, w_o, status=None, residual=None):
     """rearrange(attn, 'b s h d -> s b (h d)') @ w_o^T through mosaic_attn_out_proj:
-    attn [B, S, Hq, 64] -> [S, B, dim] bf16; with `residual` [S, B, dim] bf16 the result
-    is residual + that, rounded again (mosaic_attn_out_proj_residual)."""
+    attn [B, S, Hq, 64] -> [S, B, dim] bf16; with `residual` [S, B, dim] (bf16 or fp16)
+    the result is residual + that in the residual's dtype (mosaic_attn_out_proj_residual)."""
     _require_cuda(attn, w_o)
     B, S, Hq, D = attn.shape
     dim = w_o.shape[0]
@@ -105,11 +105,15 @@ def out_projection(attn, w_o, status=None, residual=None):
             rc = lib.mosaic_attn_out_proj(_ptr(ab), _ptr(wb), _ptr(out), _ptr(status), S, B, dim, Hq, D,
                                           _stream_ptr(attn.device))
         else:
-            rb = _bf16c(residual)
+            if residual.dtype not in (torch.bfloat16, torch.float16):
+                raise TypeError(f"residual must be bf16 or fp16, got {residual.dtype}")
+            rb = residual.contiguous()
             if tuple(rb.shape) != (S, B, dim):
                 raise ValueError(f"residual must be [{S}, {B}, {dim}], got {tuple(rb.shape)}")
+            out = torch.empty_like(rb)
+            dt = _lib.MOSAIC_DTYPE_F16 if rb.dtype == torch.float16 else _lib.MOSAIC_DTYPE_BF16
             rc = lib.mosaic_attn_out_proj_residual(_ptr(ab), _ptr(wb), _ptr(rb), _ptr(out), _ptr(status), S, B, dim,
-                                                   Hq, D, _stream_ptr(attn.device))
+                                                   Hq, D, dt, _stream_ptr(attn.device))
     _lib.check("mosaic_attn_out_proj" if residual is None else "mosaic_attn_out_proj_residual", rc)
     return out
 
@@ -163,9 +167,10 @@ class MosaicAttention(nn.Module):
             self._rope_key = key
 
     def forward(self, x, residual=None):
-        """The block's attention on x [S, B, dim]; with `residual` (a bf16 [S, B, dim]
+        """The block's attention on x [S, B, dim]; with `residual` (a bf16 or fp16 [S, B, dim]
         tensor, mosaic_b200.MosaicBlock passes the stream before norm1) it returns
-        residual + attention(x), the add done in the output projection's epilogue."""
+        residual + attention(x) in the residual's dtype, the add done in the output
+        projection's epilogue."""
         if torch.is_grad_enabled() and (x.requires_grad or any(p_.requires_grad for p_ in self.parameters())):
             raise NotImplementedError(
                 "mosaic_b200.MosaicAttention serves inference (the fused projections have no backward); "

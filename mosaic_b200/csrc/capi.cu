@@ -498,8 +498,10 @@ int mosaic_attn_out_proj(const void* attn, const void* w_o, void* out, int* stat
 }
 
 int mosaic_attn_out_proj_residual(const void* attn, const void* w_o, const void* residual, void* out, int* status,
-                                  int seq_len, int batch, int dim, int num_q_heads, int head_dim, void* stream) {
+                                  int seq_len, int batch, int dim, int num_q_heads, int head_dim, int dtype,
+                                  void* stream) {
   if (seq_len < 0 || batch < 0 || dim <= 0 || num_q_heads <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (head_dim != kHeadDim) return MOSAIC_ERR_UNSUPPORTED;
   if (dim % 32 != 0) return MOSAIC_ERR_UNSUPPORTED;  // whole 32-column chunks of residual and output rows
   if (seq_len == 0 || batch == 0) return MOSAIC_OK;
@@ -508,17 +510,20 @@ int mosaic_attn_out_proj_residual(const void* attn, const void* w_o, const void*
     return MOSAIC_ERR_INVALID_ARGUMENT;
   OutProjLaunch a;
   std::memset(&a, 0, sizeof(a));
-  a.attn = attn; a.w = w_o; a.out = out; a.residual = residual; a.status = status;
+  a.attn = attn; a.w = w_o; a.out = out; a.residual = residual; a.out_f16 = dtype == MOSAIC_DTYPE_F16;
+  a.status = status;
   a.S = seq_len; a.B = batch; a.dim = dim; a.Hq = num_q_heads;
   return launch_out_proj(a, static_cast<cudaStream_t>(stream));
 }
 
-int mosaic_rms_norm(const void* x, const float* weight, void* y, int rows, int dim, float eps, void* stream) {
-  if (rows < 0 || dim <= 0 || !(eps >= 0.f)) return MOSAIC_ERR_INVALID_ARGUMENT;
+int mosaic_rms_norm(const void* x, const float* weight, void* y, int rows, int dim, float eps, int dtype,
+                    void* stream) {
+  if (rows < 0 || dim <= 0 || !(eps >= 0.f) || !valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
+  if (dtype == MOSAIC_DTYPE_F16 && x == y) return MOSAIC_ERR_INVALID_ARGUMENT;  // y is bf16: no in-place
   if (dim % 8 != 0) return MOSAIC_ERR_UNSUPPORTED;
   if (rows == 0) return MOSAIC_OK;
   if (!x || !y || !aligned16(x) || !aligned16(y) || (weight && !aligned16(weight))) return MOSAIC_ERR_INVALID_ARGUMENT;
-  return launch_rms_norm(x, y, weight, rows, dim, eps, static_cast<cudaStream_t>(stream));
+  return launch_rms_norm(x, y, weight, rows, dim, eps, dtype == MOSAIC_DTYPE_F16, static_cast<cudaStream_t>(stream));
 }
 
 int mosaic_linear(const void* a, const void* w, void* out, const float* row_scale, int* status, int rows,
@@ -537,15 +542,16 @@ int mosaic_linear(const void* a, const void* w, void* out, const float* row_scal
 }
 
 int mosaic_linear_residual(const void* a, const void* w, const void* residual, void* out, const float* row_scale,
-                           int* status, int rows, int in_features, int out_features, void* stream) {
-  if (rows < 0 || in_features <= 0 || out_features <= 0) return MOSAIC_ERR_INVALID_ARGUMENT;
+                           int* status, int rows, int in_features, int out_features, int dtype, void* stream) {
+  if (rows < 0 || in_features <= 0 || out_features <= 0 || !valid_dtype(dtype)) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (in_features % 64 != 0 || out_features % 32 != 0) return MOSAIC_ERR_UNSUPPORTED;
   if (rows == 0) return MOSAIC_OK;
   if (!a || !w || !residual || !out) return MOSAIC_ERR_INVALID_ARGUMENT;
   if (!aligned16(a) || !aligned16(w) || !aligned16(residual) || !aligned16(out)) return MOSAIC_ERR_INVALID_ARGUMENT;
   LinearLaunch l;
   std::memset(&l, 0, sizeof(l));
-  l.a = a; l.w = w; l.out = out; l.rscale = row_scale; l.residual = residual; l.status = status;
+  l.a = a; l.w = w; l.out = out; l.rscale = row_scale; l.residual = residual; l.out_f16 = dtype == MOSAIC_DTYPE_F16;
+  l.status = status;
   l.M = rows; l.K = in_features; l.N = out_features;
   return launch_linear(l, static_cast<cudaStream_t>(stream));
 }

@@ -118,7 +118,8 @@ struct OutProjLaunch {
   const void* attn;      // [B, S, Hq*64] bf16
   const void* w;         // [dim, Hq*64] bf16 (to_o.weight)
   void* out;             // [S, B, dim] bf16
-  const void* residual;  // [S, B, dim] bf16 added to the rounded output (may alias out) or null
+  const void* residual;  // [S, B, dim] added to the rounded output (may alias out) or null
+  int out_f16;           // with a residual: residual and output fp16 (else bf16)
   int* status;
   int S, B, dim, Hq;
 };
@@ -127,7 +128,8 @@ struct LinearLaunch {
   const void* w;         // [N, K] bf16
   void* out;             // [M, N] bf16
   const float* rscale;   // [M] fp32 row factors or null
-  const void* residual;  // [M, N] bf16 added to the rounded output (may alias out) or null
+  const void* residual;  // [M, N] added to the rounded output (may alias out) or null
+  int out_f16;           // with a residual: residual and output fp16 (else bf16)
   int* status;
   int M, K, N;
 };
@@ -193,8 +195,10 @@ int launch_swiglu(const SwigluLaunch& a, cudaStream_t stream);
 int launch_interp_attend(const InterpLaunch& a, cudaStream_t stream);
 int launch_row_rms(const void* x, float* rinv, long long rows, int dim, float eps, cudaStream_t stream);
 int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream);
-// y = bf16(x * rsqrt(mean(x^2) + eps) (* w)) per row of x [rows, D] bf16 (y may be x).
-int launch_rms_norm(const void* x, void* y, const float* w, long long rows, int D, float eps, cudaStream_t stream);
+// y = bf16(x * rsqrt(mean(x^2) + eps) (* w)) per row of x [rows, D], x bf16 (y may be x)
+// or fp16 (x_f16).
+int launch_rms_norm(const void* x, void* y, const float* w, long long rows, int D, float eps, bool x_f16,
+                    cudaStream_t stream);
 
 int launch_engine(const EngineLaunch& a, cudaStream_t stream);
 int launch_pool(const PoolLaunch& a, cudaStream_t stream);

@@ -78,6 +78,7 @@ struct ProjParams {
   const __nv_bfloat16* shortcut;  // kUp: [(n f), B, out_dim]; kLinear: residual [M, N]; or null
   const __nv_bfloat16* noise;     // kSwiGLU: [B, hidden] or null
   int hidden;                     // kSwiGLU: output columns (N / 2)
+  int out_f16;                    // kPlain / kLinear with a residual: residual and output are fp16
   int F, out_dim, member, c_blocks;
   int a3d;                        // A is the 3D map (c, f, n) of kDown
   int* status;
@@ -218,28 +219,35 @@ __device__ __forceinline__ void pack_chunk_swiglu(uint32_t (&packed)[16], const 
   }
 }
 
-// 32 output columns of one row for kLinear with a residual: bf16(bf16(rs acc) + res).
+// 32 output columns of one row for kLinear / kPlain with a residual, in the residual's
+// 16-bit type T (bf16, or fp16 for a residual stream under fp16 autocast, where the
+// Linear's output is fp16): T(T(rs acc) + res).
+template <bool kF16>
 __device__ __forceinline__ void pack_chunk_residual(uint32_t (&packed)[16], const uint32_t (&acc)[32],
                                                     const uint32_t (&rw)[16], float rs) {
+  using T = Act<kF16>;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float a = __uint_as_float(acc[2 * i]) * rs, b = __uint_as_float(acc[2 * i + 1]) * rs;
-    bf16_round2(a, b);
-    packed[i] = pack_bf16x2(a + bf16_lo(rw[i]), b + bf16_hi(rw[i]));
+    const float2 y = T::unpack(T::pack(__uint_as_float(acc[2 * i]) * rs, __uint_as_float(acc[2 * i + 1]) * rs));
+    const float2 r = T::unpack(rw[i]);
+    packed[i] = T::pack(y.x + r.x, y.y + r.y);
   }
 }
 
-// RMSNorm of bf16 rows: y = bf16(x * rsqrt(mean(x^2) + eps) (* w)), one warp per row,
-// in place when y == x (the resampling layers) or into another tensor (the norms of a
-// Mosaic block, torch.nn.RMSNorm with the same fp32 arithmetic). The sum of squares is
-// taken over the bf16 values, each lane over its 16-byte chunks in order and the lanes
-// by a fixed butterfly, so it is deterministic.
-__global__ void __launch_bounds__(256) rms_apply_kernel(const __nv_bfloat16* x, __nv_bfloat16* y,
+// RMSNorm of 16-bit rows into bf16 rows: y = bf16(x * rsqrt(mean(x^2) + eps) (* w)), one
+// warp per row, x bf16 (kF16In false; in place when y == x, the resampling layers) or
+// fp16 (a Mosaic block under fp16 autocast, whose residual stream is fp16), the same fp32
+// arithmetic as torch.nn.RMSNorm. The sum of squares is taken over the input values,
+// each lane over its 16-byte chunks in order and the lanes by a fixed butterfly, so it is
+// deterministic.
+template <bool kF16In>
+__global__ void __launch_bounds__(256) rms_apply_kernel(const uint16_t* x, __nv_bfloat16* y,
                                                         const float* __restrict__ w, long long rows, int D, float eps) {
+  using In = Act<kF16In>;
   const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const __nv_bfloat16* xr = x + row * D;
+  const uint16_t* xr = x + row * D;
   __nv_bfloat16* yr = y + row * D;
   float ss = 0.f;
   for (int c = lane * 8; c < D; c += 256) {
@@ -247,8 +255,8 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(const __nv_bfloat16* x, 
     const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float a = __uint_as_float(wd[i] << 16), b = __uint_as_float(wd[i] & 0xffff0000u);
-      ss = fmaf(a, a, fmaf(b, b, ss));
+      const float2 f = In::unpack(wd[i]);
+      ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
     }
   }
 #pragma unroll
@@ -267,9 +275,8 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(const __nv_bfloat16* x, 
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float a = __uint_as_float(wd[i] << 16) * r * wt[2 * i];
-      const float b = __uint_as_float(wd[i] & 0xffff0000u) * r * wt[2 * i + 1];
-      wd[i] = pack_bf16x2(a, b);
+      const float2 f = In::unpack(wd[i]);
+      wd[i] = pack_bf16x2(f.x * r * wt[2 * i], f.y * r * wt[2 * i + 1]);
     }
     *reinterpret_cast<uint4*>(yr + c) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
@@ -521,8 +528,10 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           tmem_ld_wait();
           reg_fence<32>(acc);
           uint32_t packed[16];
-          if (p.shortcut != nullptr)
-            pack_chunk_residual(packed, acc, rw, 1.0f);
+          if (p.shortcut != nullptr && p.out_f16)
+            pack_chunk_residual<true>(packed, acc, rw, 1.0f);
+          else if (p.shortcut != nullptr)
+            pack_chunk_residual<false>(packed, acc, rw, 1.0f);
           else
             pack_chunk(packed, acc);
           warp_store_rows(stage, packed, live ? p.out + o : nullptr, lane);
@@ -536,8 +545,10 @@ __global__ void __launch_bounds__(kPThreads, 1) proj_kernel(const __grid_constan
           tmem_ld_wait();
           reg_fence<32>(acc);
           uint32_t packed[16];
-          if (p.shortcut != nullptr)
-            pack_chunk_residual(packed, acc, rw, rs);
+          if (p.shortcut != nullptr && p.out_f16)
+            pack_chunk_residual<true>(packed, acc, rw, rs);
+          else if (p.shortcut != nullptr)
+            pack_chunk_residual<false>(packed, acc, rw, rs);
           else
             pack_chunk(packed, acc, rs);
           // with a residual the output may alias it: every lane of the warp has read its
@@ -713,6 +724,7 @@ int launch_linear(const LinearLaunch& a, cudaStream_t stream) {
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.rscale = a.rscale;
   p.shortcut = static_cast<const __nv_bfloat16*>(a.residual);
+  p.out_f16 = a.out_f16;
   p.status = a.status;
   p.mode = kLinear;
   p.M = a.M;
@@ -741,13 +753,19 @@ int launch_swiglu(const SwigluLaunch& a, cudaStream_t stream) {
 }
 
 int launch_rms_apply(void* y, const float* w, long long rows, int D, float eps, cudaStream_t stream) {
-  return launch_rms_norm(y, y, w, rows, D, eps, stream);
+  return launch_rms_norm(y, y, w, rows, D, eps, false, stream);
 }
 
-int launch_rms_norm(const void* x, void* y, const float* w, long long rows, int D, float eps, cudaStream_t stream) {
+int launch_rms_norm(const void* x, void* y, const float* w, long long rows, int D, float eps, bool x_f16,
+                    cudaStream_t stream) {
   if (rows == 0) return MOSAIC_OK;
-  rms_apply_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), w, rows, D, eps);
+  const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
+  if (x_f16)
+    rms_apply_kernel<true><<<grid, 256, 0, stream>>>(static_cast<const uint16_t*>(x), static_cast<__nv_bfloat16*>(y),
+                                                     w, rows, D, eps);
+  else
+    rms_apply_kernel<false><<<grid, 256, 0, stream>>>(static_cast<const uint16_t*>(x), static_cast<__nv_bfloat16*>(y),
+                                                      w, rows, D, eps);
   return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
@@ -815,6 +833,7 @@ int launch_out_proj(const OutProjLaunch& a, cudaStream_t stream) {
     return MOSAIC_ERR_CUDA;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.shortcut = static_cast<const __nv_bfloat16*>(a.residual);
+  p.out_f16 = a.out_f16;
   p.status = a.status;
   p.mode = kPlain;
   p.M = a.S * a.B;

@@ -2,7 +2,7 @@
 (primitives.py:92-106) and primitives.MosaicBlock (primitives.py:212-229), on
 libmosaic_b200.so.
 
-    MosaicBlock.forward(x [S, B, dim], z [B, noise_dim]), bf16 stream:
+    MosaicBlock.forward(x [S, B, dim], z [B, noise_dim]), bf16 or fp16 stream:
         y = norm1(x)                        --mosaic_rms_norm-->
         x = x + attention(y)                --mosaic_b200.MosaicAttention, the residual add
                                               in its output projection's epilogue
@@ -21,10 +21,11 @@ Both modules keep the reference's constructor and submodule names (`w13`, `w2`,
 `act_fn`, `noise_bias`; `attention`, `norm1`, `norm2`, `ffn`), so reference state
 dicts load, and rebinding the block class mosaic.py imports (`_MosaicBlock`, or
 primitives.MosaicBlock before mosaic.py is imported) swaps them in. They serve
-inference (no backward). A block whose residual stream is not bf16 (the reference's
-fp32 model under fp16 autocast) keeps that stream: its norms are the module's own
-torch.nn.RMSNorm, the attention and FFN run in bf16 and their outputs are added to x
-in x's dtype.
+inference (no backward). The GEMMs run in bf16. A residual stream in fp16 (the
+reference's model under fp16 autocast, where every Linear outputs fp16) stays fp16:
+the norms read it, and the residual epilogues round the Linear's output to fp16 and add
+in fp16, as autocast does. Any other stream dtype keeps its dtype, with the module's
+own torch.nn.RMSNorm and the adds done by torch.
 """
 import torch
 import torch.nn as nn
@@ -72,32 +73,44 @@ def ffn_swiglu(x, w13_interleaved, batch, row_scale=None, noise=None, status=Non
     return h.reshape(*x.shape[:-1], hidden)
 
 
+def _stream_dtype(t):
+    """A 16-bit residual stream's dtype code (bf16, or fp16 under fp16 autocast)."""
+    if t.dtype == torch.float16:
+        return _lib.MOSAIC_DTYPE_F16
+    if t.dtype == torch.bfloat16:
+        return _lib.MOSAIC_DTYPE_BF16
+    raise TypeError(f"expected a bf16 or fp16 tensor, got {t.dtype}")
+
+
 def linear_residual(a, w, residual, out=None, row_scale=None, status=None):
-    """out = bf16(residual + bf16(row_scale * a w^T)) (out may be residual: in place)."""
+    """out = T(residual + T(row_scale * a w^T)) with T the residual's dtype (bf16 or fp16;
+    out may be residual: in place). a and w run in bf16."""
     _require_cuda(a, w, residual)
     k_in, n_out = a.shape[-1], w.shape[0]
-    ab, wb, rb = _bf16c(a).reshape(-1, k_in), _bf16c(w), _bf16c(residual).reshape(-1, n_out)
+    ab, wb = _bf16c(a).reshape(-1, k_in), _bf16c(w)
+    rb = residual.contiguous().reshape(-1, n_out)
     o = torch.empty_like(rb) if out is None else out.reshape(-1, n_out)
     rs = None if row_scale is None else row_scale.float().contiguous()
     with torch.cuda.device(a.device):
         rc = _lib.load().mosaic_linear_residual(_ptr(ab), _ptr(wb), _ptr(rb), _ptr(o), _ptr(rs), _ptr(status),
-                                                ab.shape[0], k_in, n_out, _stream_ptr(a.device))
+                                                ab.shape[0], k_in, n_out, _stream_dtype(rb), _stream_ptr(a.device))
     _lib.check("mosaic_linear_residual", rc)
     return o.reshape(residual.shape)
 
 
 def rms_norm(x, eps, weight=None):
-    """torch.nn.RMSNorm of a bf16 x [..., dim] through mosaic_rms_norm: bf16(x *
+    """torch.nn.RMSNorm of a bf16 or fp16 x [..., dim] through mosaic_rms_norm: bf16(x *
     rsqrt(mean(x^2) + eps) * weight) in fp32 arithmetic, the norm a Mosaic block feeds
-    its attention and its FFN (primitives.py:228-229)."""
+    its attention and its FFN (primitives.py:228-229); the result is bf16 either way
+    (the GEMMs behind it take bf16)."""
     _require_cuda(x)
     dim = x.shape[-1]
-    xb = _bf16c(x).reshape(-1, dim)
-    y = torch.empty_like(xb)
+    xb = (x if x.dtype in (torch.bfloat16, torch.float16) else x.to(torch.bfloat16)).contiguous().reshape(-1, dim)
+    y = torch.empty(xb.shape, dtype=torch.bfloat16, device=x.device)
     w = None if weight is None else weight.detach().float().contiguous()
     with torch.cuda.device(x.device):
         rc = _lib.load().mosaic_rms_norm(_ptr(xb), _ptr(w), _ptr(y), xb.shape[0], dim, float(eps),
-                                         _stream_ptr(x.device))
+                                         _stream_dtype(xb), _stream_ptr(x.device))
     _lib.check("mosaic_rms_norm", rc)
     return y.reshape(x.shape)
 
@@ -145,7 +158,7 @@ class MosaicSwiGLU(nn.Module):
     def residual_forward(self, x, z, norm):
         """x + self(norm(x), z) for the block's torch.nn.RMSNorm `norm`."""
         _no_grad_check(self, x)
-        if x.dtype == torch.bfloat16:
+        if x.dtype in (torch.bfloat16, torch.float16):
             y = rms_norm(x, norm_eps(norm), norm.weight)
             h = ffn_swiglu(y, self._w13_interleaved(), x.shape[1], noise=self._noise(z))
             return linear_residual(h, self.w2.weight, x)
@@ -169,7 +182,7 @@ class MosaicBlock(nn.Module):
         self.ffn = MosaicSwiGLU(dim, int(dim * config.mlp_ratio), config.noise_dim)
 
     def forward(self, x, z=None):
-        if x.dtype == torch.bfloat16:
+        if x.dtype in (torch.bfloat16, torch.float16):
             x = self.attention(rms_norm(x, norm_eps(self.norm1), self.norm1.weight), residual=x)
         else:
             x = x + self.attention(self.norm1(x))

@@ -73,12 +73,19 @@ def test_capi_rejects_bad_arguments():
     assert sw(x=None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
     assert sw(noise=ctypes.c_void_p(0x10008)) == _lib.MOSAIC_ERR_INVALID_ARGUMENT  # misaligned
     assert sw(rows=0) == _lib.MOSAIC_OK
-    lr = lambda rows=64, k=256, n=256, res=FAKE: lib.mosaic_linear_residual(FAKE, FAKE, res, FAKE, None, None, rows, k,
-                                                                           n, None)
+    lr = lambda rows=64, k=256, n=256, res=FAKE, dt=0: lib.mosaic_linear_residual(FAKE, FAKE, res, FAKE, None, None,
+                                                                                 rows, k, n, dt, None)
     assert lr(k=100) == _lib.MOSAIC_ERR_UNSUPPORTED
     assert lr(n=40) == _lib.MOSAIC_ERR_UNSUPPORTED
     assert lr(res=None) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+    assert lr(dt=5) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
     assert lr(rows=0) == _lib.MOSAIC_OK
+    rn = lambda x=FAKE, y=ctypes.c_void_p(0x20000), dt=0: lib.mosaic_rms_norm(x, None, y, 64, 256, ctypes.c_float(1e-6),
+                                                                              dt, None)
+    assert rn(dt=7) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
+    assert rn(y=FAKE, dt=_lib.MOSAIC_DTYPE_F16) == _lib.MOSAIC_ERR_INVALID_ARGUMENT  # fp16 in, bf16 out: not in place
+    op = lambda dt=0: lib.mosaic_attn_out_proj_residual(FAKE, FAKE, FAKE, FAKE, None, 64, 1, 256, 4, 64, dt, None)
+    assert op(dt=3) == _lib.MOSAIC_ERR_INVALID_ARGUMENT
 
 
 @pytest.mark.skipif(not R.available(), reason="baseline/_ref holds no reference copy")

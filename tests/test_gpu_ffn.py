@@ -172,3 +172,55 @@ def test_attention_residual_in_the_output_projection():
         b = m(x, residual=r)
     torch.cuda.synchronize()
     assert torch.equal(b, r + a)
+
+
+def test_block_ffn_fp16_stream():
+    """A residual stream in fp16 (the model under fp16 autocast) runs fused as well: the
+    norm reads fp16, the w2 epilogue rounds the Linear's output to fp16 and adds in fp16."""
+    S, B, dim = 2048, 2, 768
+    m = weights(dim, 4 * dim, 32, seed=11)
+    norm = torch.nn.RMSNorm(dim, elementwise_affine=False)
+    g = torch.Generator().manual_seed(11)
+    x = (3 * torch.randn(S, B, dim, generator=g)).half()
+    z = torch.randn(B, 32, generator=g)  # fp32 weights: the noise projection runs in fp32 here
+    ref = O.mosaic_block_ffn(x, z, m.w13.weight, m.w2.weight, m.noise_bias.weight, torch.finfo(torch.float32).eps)
+    md = m.to(DEV)
+    with torch.no_grad():
+        out = md.residual_forward(x.to(DEV), z.to(DEV), norm.to(DEV))
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16
+    ffn_scale = (ref - x.float()).abs().max().item()
+    d = (out.float().cpu() - ref).abs()
+    # the FFN runs in bf16 (2e-2 of its scale), then the fp16 add rounds (half an fp16 ulp)
+    assert (d <= 2e-2 * ffn_scale + 2 ** -11 * ref.abs()).all(), d.max().item()
+    assert d.mean().item() <= 2e-3 * ffn_scale + (2 ** -12 * ref.abs()).mean().item()
+
+
+def test_rms_norm_reads_fp16():
+    g = torch.Generator(device=DEV).manual_seed(12)
+    x = (2 * torch.randn(4096, 1024, generator=g, device=DEV)).half()
+    eps = torch.finfo(torch.float32).eps
+    got = F.rms_norm(x, eps)
+    assert got.dtype == torch.bfloat16
+    xf = x.float()
+    want = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).bfloat16()
+    d = (got.float() - want.float()).abs()
+    assert (d <= 2 ** -7 * want.float().abs()).all() and (d > 0).float().mean() < 0.01
+
+
+def test_linear_residual_fp16_residual():
+    M_, K, N = 1024, 3072, 768
+    g = torch.Generator(device=DEV).manual_seed(13)
+    a = torch.randn(M_, K, generator=g, device=DEV).bfloat16()
+    w = (torch.randn(N, K, generator=g, device=DEV) * K ** -0.5).bfloat16()
+    r = torch.randn(M_, N, generator=g, device=DEV).half()
+    out = F.linear_residual(a, w, r)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16
+    # the Linear's output rounded to fp16, then the fp16 add (autocast's rounding points)
+    y = (a.float() @ w.float().t()).half()
+    ref = (r.float() + y.float()).half()
+    d = (out.float() - ref.float()).abs()
+    # y may differ by one fp16 ulp (accumulation order), the sum by one more: both scale
+    # with |y| as well as |out| (the residual can cancel y)
+    assert (d <= 2 ** -9 * (y.float().abs() + ref.float().abs()) + 1e-3).all(), d.max().item()
