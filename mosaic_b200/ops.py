@@ -172,11 +172,33 @@ class MosaicAttnFunction(torch.autograd.Function):
         return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None
 
 
+HEAD_DIM = 64  # the kernels' head dimension
+
+
+def pad_head_dim(*ts):
+    """Zero-pads the last (head) dimension of [B, N, H, d] tensors up to 64 for d < 64:
+    zero columns add nothing to q.k, to the pooled means or to the top-k scores, and the
+    output's padded columns are zero, so a head_dim below 64 (the reference's kernel takes
+    any feature_dim, ops.py:25-60) runs on the 64-wide kernels with the softmax scale of
+    the original d. Raises for d > 64."""
+    d = ts[0].shape[-1]
+    if d > HEAD_DIM:
+        raise ValueError(f"head_dim {d} is not supported (at most {HEAD_DIM})")
+    if d == HEAD_DIM:
+        return ts
+    return tuple(torch.nn.functional.pad(t, (0, HEAD_DIM - d)) for t in ts)
+
+
 def mosaic_sparse_attn(q, k, v, block_indices, block_size, softmax_scale=None):
     """Selected-block attention (ops.py:557-566), differentiable in q, k, v. Under
     torch.compile the call becomes the opaque custom op torch.ops.mosaic_b200.sparse_attn
-    (or sparse_attn_fwd, which has an autograd formula, when an input needs a gradient)."""
+    (or sparse_attn_fwd, which has an autograd formula, when an input needs a gradient).
+    head_dim 64, or less (zero-padded to 64, see pad_head_dim)."""
     softmax_scale = q.shape[-1] ** -0.5 if softmax_scale is None else softmax_scale
+    d = q.shape[-1]
+    if d != HEAD_DIM:
+        q, k, v = pad_head_dim(q, k, v)
+        return mosaic_sparse_attn(q, k, v, block_indices, block_size, softmax_scale)[..., :d].contiguous()
     if torch.compiler.is_compiling():
         from . import torch_ops  # noqa: F401  (registers the op)
 
@@ -191,5 +213,7 @@ def mosaic_sparse_attn_with_lse(q, k, v, block_indices, block_size, softmax_scal
     """Like mosaic_sparse_attn, also returning the log-sum-exp in log2 units
     (fp32 [B, N, Hq]), the second output of ops.mosaic_attn_fwd (ops.py:176)."""
     softmax_scale = q.shape[-1] ** -0.5 if softmax_scale is None else softmax_scale
-    out, lse = _sparse_fwd(q, k, v, block_indices, block_size, softmax_scale, want_lse=True, status=status)
-    return out.to(q.dtype), lse
+    d = q.shape[-1]
+    qp, kp, vp = pad_head_dim(q, k, v)
+    out, lse = _sparse_fwd(qp, kp, vp, block_indices, block_size, softmax_scale, want_lse=True, status=status)
+    return out[..., :d].contiguous().to(q.dtype), lse

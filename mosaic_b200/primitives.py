@@ -21,7 +21,8 @@ import ctypes
 import torch
 
 from . import _lib
-from .ops import _act, _check_qkv, _ptr, _require_cuda, _stream_ptr, act_dtype, dtype_code, mosaic_sparse_attn
+from .ops import (HEAD_DIM, _act, _check_qkv, _ptr, _require_cuda, _stream_ptr, act_dtype, dtype_code,
+                  mosaic_sparse_attn, pad_head_dim)
 
 __all__ = ["mosaic_attn_func", "attn_topk", "block_attention", "block_pool", "cmp_attention", "bsa_attend",
            "mosaic_sparse_attn"]
@@ -73,6 +74,11 @@ def _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_
                             status=None):
     _require_cuda(q, k, v)
     _check_qkv(q, k, v)
+    D0 = q.shape[-1]  # head_dim below 64: zero-padded to 64 (pad_head_dim), scale of D0
+    if D0 != HEAD_DIM:
+        if rope_tables is not None:
+            raise ValueError("rope_tables needs head_dim 64; rotate q and k before the call for other head dims")
+        q, k, v = pad_head_dim(q, k, v)
     B, N, Hq, D = q.shape
     Hk = k.shape[2]
     out_dtype = q.dtype
@@ -118,11 +124,13 @@ def _mosaic_attn_func_eager(q, k, v, weight_ba_cmp_slc, block_attn_size, sparse_
     args.sparse_block_count = K
     args.block_attn_only = int(bool(block_attn_only))
     args.no_compression = int(bool(no_compression))
-    args.softmax_scale = float(D ** -0.5)
+    args.softmax_scale = float(D0 ** -0.5)
     args.dtype = dtype_code(dt)
     with torch.cuda.device(q.device):
         rc = lib.mosaic_bsa_fwd(ctypes.byref(args), _stream_ptr(q.device))
     _lib.check("mosaic_bsa_fwd", rc)
+    if D0 != HEAD_DIM:
+        out = out[..., :D0].contiguous()
     out = out.to(out_dtype)
     return (out, idx) if return_block_indices else out
 
@@ -153,6 +161,11 @@ def block_attention(q, k, v, block_size, status=None):
     """Full attention inside each window of block_size tokens (primitives.py:28-32)."""
     _require_cuda(q, k, v)
     _check_qkv(q, k, v)
+    D0 = q.shape[-1]  # head_dim below 64: zero-padded to 64 (pad_head_dim), scale of D0
+    if D0 != HEAD_DIM:
+        if rope_tables is not None:
+            raise ValueError("rope_tables needs head_dim 64; rotate q and k before the call for other head dims")
+        q, k, v = pad_head_dim(q, k, v)
     B, N, Hq, D = q.shape
     Hk = k.shape[2]
     if N % block_size != 0:
@@ -174,6 +187,11 @@ def block_pool(q, k, v, block_size, rope_tables=None):
     Returns (q_cmp, k_cmp, v_cmp) or, with rope_tables, (q_cmp, k_cmp, v_cmp, q_rot, k_rot)."""
     _require_cuda(q, k, v)
     _check_qkv(q, k, v)
+    D0 = q.shape[-1]  # head_dim below 64: zero-padded to 64 (pad_head_dim), scale of D0
+    if D0 != HEAD_DIM:
+        if rope_tables is not None:
+            raise ValueError("rope_tables needs head_dim 64; rotate q and k before the call for other head dims")
+        q, k, v = pad_head_dim(q, k, v)
     B, N, Hq, D = q.shape
     Hk = k.shape[2]
     if N % block_size != 0:
@@ -225,6 +243,11 @@ def bsa_attend(q, k, v, block_indices, weight_ba_cmp_slc, o_cmp, block_attn_size
     attention `o_cmp` [B, N // sparse_block_size, Hq, D]."""
     _require_cuda(q, k, v)
     _check_qkv(q, k, v)
+    D0 = q.shape[-1]  # head_dim below 64: zero-padded to 64 (pad_head_dim), scale of D0
+    if D0 != HEAD_DIM:
+        if rope_tables is not None:
+            raise ValueError("rope_tables needs head_dim 64; rotate q and k before the call for other head dims")
+        q, k, v = pad_head_dim(q, k, v)
     B, N, Hq, D = q.shape
     Hk = k.shape[2]
     lib = _lib.load()

@@ -107,3 +107,13 @@ def test_oracle_matches_reference_cswiglu(affine):
         got_block = O.mosaic_block_ffn(x, z, m.w13.weight, m.w2.weight, m.noise_bias.weight,
                                        torch.finfo(torch.float32).eps, norm.weight if affine else None)
         torch.testing.assert_close(got_block, want_block, rtol=1e-5, atol=1e-5)
+
+
+def test_pad_head_dim():
+    from mosaic_b200 import ops as mops
+    q = torch.randn(1, 8, 2, 32)
+    (p,) = mops.pad_head_dim(q)
+    assert p.shape == (1, 8, 2, 64) and torch.equal(p[..., :32], q) and not p[..., 32:].any()
+    assert mops.pad_head_dim(torch.randn(1, 8, 2, 64))[0].shape[-1] == 64
+    with pytest.raises(ValueError):
+        mops.pad_head_dim(torch.randn(1, 8, 2, 96))

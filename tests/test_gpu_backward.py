@@ -187,3 +187,21 @@ def test_sparse_bwd_full_size_linearity():
         m = expect.abs().max().item()
         d = (c.float() - expect).abs()
         assert d.max().item() <= 3e-2 * m and d.mean().item() <= 3e-3 * m, (d.max().item(), d.mean().item(), m)
+
+
+def test_backward_head_dim_32():
+    """The gradient through the zero-padding of a head_dim below 64 (pad_head_dim)."""
+    B, N, Hq, Hk, D, bs = 1, 1024, 4, 1, 32, 64
+    g = torch.Generator().manual_seed(32)
+    q, k, v, go = (torch.randn(B, N, h, D, generator=g).bfloat16() for h in (Hq, Hk, Hk, Hq))
+    sel = torch.stack([torch.randperm(N // bs, generator=g)[:4] for _ in range(N // bs)]).reshape(B, N // bs, Hk, 4)
+    qa, ka, va = (t.cuda().requires_grad_() for t in (q, k, v))
+    out = M.mosaic_sparse_attn(qa, ka, va, sel.cuda(), bs)
+    assert out.shape == (B, N, Hq, D)
+    out.backward(go.cuda())
+    torch.cuda.synchronize()
+    for got, ref in zip((qa.grad, ka.grad, va.grad), O.sparse_attention_bwd(q, k, v, sel, bs, go)):
+        assert got.shape == ref.shape
+        m = max(1.0, ref.abs().max().item())
+        e = (got.float().cpu() - ref).abs()
+        assert e.max() <= 2e-2 * m and e.mean() <= 2e-3 * m, (e.max().item(), e.mean().item())

@@ -392,3 +392,23 @@ def test_score_far_above_running_max_in_every_lane(column):
     torch.cuda.synchronize()
     assert mops.check_status(status) == 0
     close(out, O.block_attention(q, k, x["v"], 1024))
+
+
+@pytest.mark.parametrize("D", [32, 48])
+def test_head_dim_below_64(D):
+    """head_dim below 64 (the reference's kernel takes any feature_dim): zero-padded to
+    the kernels' 64 columns with the softmax scale of D, against the oracle at D."""
+    B, N, Hq, Hk = 1, 2048, 8, 2
+    g = torch.Generator().manual_seed(D)
+    q, k, v = (torch.randn(B, N, h, D, generator=g).bfloat16() for h in (Hq, Hk, Hk))
+    w = torch.sigmoid(torch.randn(3, B, N, Hq, 1, generator=g)).bfloat16()
+    out, idx = M.mosaic_attn_func(*cuda(q, k, v, w), 1024, 64, 8, False, return_block_indices=True)
+    torch.cuda.synchronize()
+    assert out.shape == (B, N, Hq, D)
+    qc, kc = O.pool_mean(q, 64), O.pool_mean(k, 64)
+    ok, _ = O.topk_matches(idx.cpu(), O.attn_topk(qc, kc, 8), O.topk_scores(qc, kc))
+    assert ok
+    close(out, O.mosaic_attn_func(q, k, v, w, 1024, 64, 8, False, block_indices=idx.cpu()))
+    sel = random_indices(B, N // 64, Hk, 4, seed=D)
+    o2 = M.mosaic_sparse_attn(*cuda(q, k, v, sel), 64)
+    close(o2, O.sparse_attention(q, k, v, sel, 64))
