@@ -32,6 +32,13 @@
 // exp2 on the FMA pipe, because at head_dim 64 the MUFU rate, not the tensor
 // core, is the first limit.
 //
+// In the full forward this kernel is launched with programmatic stream
+// serialization after the top-k kernel (EngineParams::pdl): its CTAs start while
+// top-k and the coarse attention finish, run the local tiles of their first unit,
+// and wait (griddepcontrol.wait) only before reading block indices (TMA warp) and
+// coarse-attention rows (softmax warps). The top-k kernel completes only after the
+// coarse attention, so one wait covers both.
+//
 // TMEM (512 columns, fp32): S/P buffer b of M-tile m at 64*(2m+b) (P overwrites
 // the first 32 columns of its S buffer as packed 16-bit pairs and feeds P*V from
 // TMEM), O_local of M-tile m at 256+128m, O_selected at 320+128m.
@@ -99,6 +106,8 @@ struct EngineParams {
   int ngroups;  // groups of four query heads per kv head: ceil(G / 4)
   int qtiles;   // 64-query tiles per (batch, kv head)
   int units;    // B * Hk * ngroups * qtiles work units
+  int pdl;      // launched with programmatic serialization: wait for the previous grids before reading
+                // block_idx and o_cmp
 };
 
 // One work unit: (batch b, kv head h, head group grp, 64-query tile starting at n0)
@@ -372,26 +381,31 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
       prefetch_tmap(&p.tm_v);
     }
     int g = 0, it = 0;
-    bool ok = true;
+    bool ok = true, dep_done = !p.pdl;
+    // This query block's selected kv blocks; out-of-range entries are reported and
+    // clamped so that no load leaves the batch. Only this warp reads sel[].
+    auto load_sel = [&](const Unit& w) {
+      const int qb = w.n0 / p.bs;
+      const int64_t* src = p.block_idx + ((static_cast<int64_t>(w.b) * p.nqb + qb) * p.Hk + w.h) * p.K;
+      __syncwarp();
+      for (int s = lane; s < p.K; s += 32) {
+        int64_t v = src[s];
+        if (v < 0 || v >= p.nkb) {
+          if (p.status) atomicOr(p.status, MOSAIC_STATUS_BAD_INDEX);
+          v = 0;
+        }
+        sm.sel[s] = static_cast<int>(v);
+      }
+      __syncwarp();
+    };
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++it) {
       const Unit w = decode_unit(p, u);
-      if (p.K > 0) {
-        // This query block's selected kv blocks; out-of-range entries are
-        // reported and clamped so that no load leaves the batch. Only this warp
-        // reads sel[], so it is rewritten per unit.
-        const int qb = w.n0 / p.bs;
-        const int64_t* src = p.block_idx + ((static_cast<int64_t>(w.b) * p.nqb + qb) * p.Hk + w.h) * p.K;
-        __syncwarp();
-        for (int s = lane; s < p.K; s += 32) {
-          int64_t v = src[s];
-          if (v < 0 || v >= p.nkb) {
-            if (p.status) atomicOr(p.status, MOSAIC_STATUS_BAD_INDEX);
-            v = 0;
-          }
-          sm.sel[s] = static_cast<int>(v);
-        }
-        __syncwarp();
-      }
+      // Once the grids before this one are complete, the indices are read up front;
+      // until then (the first unit of a kernel launched with programmatic
+      // serialization after the top-k kernel) only after the local tiles are
+      // queued, so that the local branch overlaps the end of top-k.
+      const bool sel_now = p.K > 0 && dep_done;
+      if (sel_now) load_sel(w);
       const int qbuf = it & 1;
       if (it >= 2 && !warp_wait(&sm.q_empty[qbuf], ((it - 2) >> 1) & 1, abort_flag, p.status)) {
         ok = false;
@@ -403,6 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
           tma_load_2d_elect(sQ + (2 * qbuf + m) * kQTileBytes + v * kBoxBytes, &p.tm_q, &sm.q_full[qbuf],
                             q_column(w, 2 * m + v, G, p.Hq), w.b * p.Nq + w.n0);
       for (int t = 0; t < w.T; ++t, ++g) {
+        if (t == w.T_loc && p.K > 0 && !sel_now) {
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          dep_done = true;
+          load_sel(w);
+        }
         const int st = g % kStages, r = g / kStages;
         if (r > 0 && !warp_wait(&sm.kv_empty[st], (r - 1) & 1, abort_flag, p.status)) {
           ok = false;
@@ -581,14 +600,23 @@ __global__ void __launch_bounds__(kThreads, 1) bsa_engine_kernel(const __grid_co
         l_loc = l_run;
       }
 
-      // Start the coarse-attention row loads before waiting for the last P*V.
+      // The coarse-attention rows come from a kernel that may still run when this
+      // one starts (programmatic serialization): wait for it before the first read.
+      // The wait returns at once after its first completion, and in a kernel launched
+      // without programmatic serialization; it carries the row pointer, so the loads
+      // below cannot move above it.
+      const uint16_t* o_cmp = p.o_cmp;
+      asm volatile("griddepcontrol.wait;" : "+l"(o_cmp));
+      // Start the coarse-attention row loads before waiting for the last P*V (plain
+      // loads: with programmatic serialization the rows are written while this
+      // kernel runs, so they are not read-only for its lifetime).
       const uint4* cmp_row =
           (live && c1 != 0.f)
-              ? reinterpret_cast<const uint4*>(p.o_cmp + ((static_cast<size_t>(w.b) * p.nqb + n / p.bs) * p.Hq + head) * 64)
+              ? reinterpret_cast<const uint4*>(o_cmp + ((static_cast<size_t>(w.b) * p.nqb + n / p.bs) * p.Hq + head) * 64)
               : nullptr;
       uint4 cmpv[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) cmpv[i] = cmp_row != nullptr ? __ldg(cmp_row + i) : make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < 8; ++i) cmpv[i] = cmp_row != nullptr ? cmp_row[i] : make_uint4(0, 0, 0, 0);
 
       MOSAIC_TRACE_AT(traced_cta && it == MOSAIC_TRACE_IT && row == 0, 2002 + wg);
       if (!bounded_wait(&sm.o_final[wg], it & 1, abort_flag, p.status)) {
@@ -696,6 +724,7 @@ int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
   p.ngroups = (p.G + 3) / 4;
   p.qtiles = (a.Nq + kQTile - 1) / kQTile;
   p.units = a.B * a.Hk * p.ngroups * p.qtiles;
+  p.pdl = a.after_topk ? 1 : 0;
 
   // The shared-memory opt-in is a per-device function attribute: set it once per
   // device and instantiation.
@@ -715,11 +744,19 @@ int launch_engine(const EngineLaunch& a, cudaStream_t stream) {
       cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return MOSAIC_ERR_CUDA;
   const int grid = p.units < sm_count[dev] ? p.units : sm_count[dev];
-  if (a.f16)
-    bsa_engine_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(p);
-  else
-    bsa_engine_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.after_topk ? 1 : 0;
+  const cudaError_t e = a.f16 ? cudaLaunchKernelEx(&cfg, bsa_engine_kernel<true>, p)
+                              : cudaLaunchKernelEx(&cfg, bsa_engine_kernel<false>, p);
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
 size_t engine_max_selected() { return kMaxSel; }

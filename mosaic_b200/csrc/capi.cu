@@ -416,6 +416,7 @@ int mosaic_bsa_fwd(const MosaicBsaArgs* args, void* stream) {
   e.combine = local_only ? kCombineLocal : (no_cmp ? kCombineNoCmp : (want_slc ? kCombineGated : kCombineNoSlc));
   e.softmax_scale = scale;
   e.f16 = f16;
+  e.after_topk = want_slc;
   return launch_engine(e, st);
 }
 

@@ -42,6 +42,7 @@ struct EngineLaunch {
   int combine;
   float softmax_scale;
   bool f16;  // activations are fp16 (else bf16)
+  bool after_topk;  // launched with programmatic serialization after the top-k kernel
 };
 
 // Mean-pool (optionally after 2D RoPE) of q, k, v over contiguous blocks of `bs` rows.

@@ -237,6 +237,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   TopkSmem& sm = *reinterpret_cast<TopkSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i0 = blockIdx.x * kRows, h = blockIdx.y, b = blockIdx.z;
+  // The attention kernel after this one may start its local branch now; it waits
+  // (griddepcontrol.wait) for this grid's completion before it reads the indices.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // q_cmp rows of the strided group {h, h+Hk, ...}, stored with the head dimension
   // permuted by perm_d() so that every thread's B-fragment values of a key row are
@@ -307,6 +310,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
       p.idx[((static_cast<size_t>(b) * p.nb + i) * p.Hk + h) * p.K + s] =
           static_cast<int64_t>(0xFFFFu - (sm.top[r][s] & 0xFFFFu));
   }
+  // Complete only after the coarse attention launched before this kernel, so that
+  // a kernel waiting on this grid also sees the coarse-attention output.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 template <int G, bool kF16>

@@ -320,6 +320,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) topk_tc_kernel(const __grid_con
       }
     }
   }
+  // Complete only after the coarse attention launched before this kernel, so that
+  // a kernel waiting on this grid also sees the coarse-attention output.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 template <int KP, int G, bool kF16>
